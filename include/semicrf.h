@@ -1,0 +1,137 @@
+/*
+ * semicrf.h -- C ABI of the B200 (sm_100a) streaming semi-CRF scan.
+ *
+ * This is the drop-in boundary for the hot path of torch-semimarkov 0.2.0
+ * (src/torch_semimarkov/streaming/).  The reference binds that path from
+ * Python through Triton launchers; each entry point below replaces one of
+ * them (file:line in the reference project):
+ *
+ *   semicrf_forward            launch_streaming_triton_kernel
+ *                              (streaming/triton_forward.py:554-714) and the
+ *                              forward of SemiCRFStreamingTriton
+ *                              (streaming/autograd.py:187-226)
+ *   semicrf_backward           launch_streaming_triton_backward
+ *                              (streaming/triton_backward.py:556-790) and the
+ *                              backward of SemiCRFStreamingTriton
+ *                              (streaming/autograd.py:228-267)
+ *   semicrf_viterbi            SemiMarkovCRFHead.decode_with_traceback /
+ *                              _traceback_single (nn.py:360-531)
+ *   semicrf_score_gold         score_gold_vectorized (helpers.py:365-544)
+ *   semicrf_score_gold_backward  autograd of score_gold_vectorized
+ *   semicrf_checkpoint_interval  _compute_checkpoint_interval
+ *                              (streaming/pytorch_reference.py:25-45)
+ *
+ * Conventions
+ *  - All tensors are device pointers to contiguous row-major float32 (int64
+ *    for lengths/labels) on the current CUDA device.
+ *  - The caller owns every buffer.  The library never allocates or frees
+ *    device memory: scratch space is passed in, sized by the matching
+ *    *_workspace_size query.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls only
+ *    enqueue work; they do not synchronise.
+ *  - Return value: SEMICRF_OK or an error code; semicrf_strerror() names it.
+ */
+#ifndef SEMICRF_H_
+#define SEMICRF_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SEMICRF_ABI_VERSION 1
+
+enum semicrf_status {
+    SEMICRF_OK = 0,
+    SEMICRF_ERR_INVALID_ARGUMENT = 1, /* bad sizes / null pointers / K < 1 */
+    SEMICRF_ERR_UNSUPPORTED = 2,      /* shape outside the supported range */
+    SEMICRF_ERR_WORKSPACE = 3,        /* workspace smaller than queried */
+    SEMICRF_ERR_CUDA = 4,             /* a CUDA launch failed */
+    SEMICRF_ERR_SEMIRING = 5          /* semiring is neither log nor max */
+};
+
+enum semicrf_semiring { SEMICRF_LOG = 0, SEMICRF_MAX = 1 };
+
+/* One streaming problem: the arguments of semi_crf_streaming_forward
+ * (streaming/autograd.py:270-281). */
+typedef struct semicrf_problem {
+    int64_t batch;                /* B */
+    int64_t T;                    /* cum_scores has T+1 rows */
+    int64_t K;                    /* max duration; durations 1..max(1,K-1) */
+    int64_t C;                    /* number of labels */
+    const float* cum_scores;      /* (B, T+1, C) */
+    const float* transition;      /* (C, C) [src, dst] or (K, C, C) */
+    int32_t transition_ndim;      /* 2 or 3 */
+    int32_t semiring;             /* enum semicrf_semiring */
+    const float* duration_bias;   /* (K, C) */
+    const int64_t* lengths;       /* (B,), each in [0, T] */
+    const float* proj_start;      /* (B, T, C) or NULL */
+    const float* proj_end;        /* (B, T, C) or NULL */
+    int64_t checkpoint_interval;  /* S >= K (see semicrf_checkpoint_interval) */
+} semicrf_problem;
+
+/* _compute_checkpoint_interval: max(K, floor(sqrt(T*K))). */
+int64_t semicrf_checkpoint_interval(int64_t T, int64_t K);
+
+/* Bytes of state semicrf_forward keeps for semicrf_backward (float64 log-Z
+ * and the normalised ring checkpoints). */
+size_t semicrf_saved_size(const semicrf_problem* p);
+size_t semicrf_forward_workspace_size(const semicrf_problem* p);
+
+/* Forward scan.  Writes partition (B,) and, when ring_checkpoints is not
+ * NULL, the ring buffer of alpha at every multiple of S in the reference
+ * layout (B, num_ring_checkpoints, K, C) (NEG_INF = -1e9 where unset;
+ * checkpoint 0 holds alpha[0] = 0 in slot 0).  When saved is not NULL the
+ * state needed by semicrf_backward is written there. */
+int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_checkpoints,
+                    int64_t num_ring_checkpoints, void* saved, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+size_t semicrf_backward_workspace_size(const semicrf_problem* p);
+
+/* Backward: gradients of sum_b grad_output[b] * partition[b].
+ * grad_cum (B,T+1,C), grad_transition (C,C) or (K,C,C), grad_duration_bias
+ * (K,C) are always written; grad_proj_start / grad_proj_end (B,T,C) when the
+ * corresponding projection is present.  `saved` is the buffer filled by
+ * semicrf_forward for the same problem. */
+int semicrf_backward(const semicrf_problem* p, const void* saved, const float* grad_output,
+                     float* grad_cum, float* grad_transition, float* grad_duration_bias,
+                     float* grad_proj_start, float* grad_proj_end, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+size_t semicrf_viterbi_workspace_size(const semicrf_problem* p);
+
+/* Max-semiring scan with compact (k, c_src) backpointers and a GPU
+ * backtrace.  scores (B,); segments of sequence b are written at offset b*T
+ * of seg_start/seg_end/seg_label/seg_score, in order, nseg[b] of them.
+ * Sequences with length 0 or longer than max_traceback_length get nseg = 0
+ * (their score is still written).  seg_score follows nn.py:533-555. */
+int semicrf_viterbi(const semicrf_problem* p, int64_t max_traceback_length, float* scores,
+                    int32_t* seg_start, int32_t* seg_end, int32_t* seg_label,
+                    double* seg_score, int32_t* nseg, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Gold-segmentation score (helpers.py:365-544): out (B,). transition (C,C). */
+int semicrf_score_gold(int64_t B, int64_t T, int64_t K, int64_t C, const float* cum_scores,
+                       const int64_t* labels, const int64_t* lengths, const float* transition,
+                       const float* duration_bias, float* out, void* stream);
+
+/* Its gradient: grad_cum (B,T+1,C) is overwritten; grad_transition (C,C)
+ * and grad_duration_bias (K,C) are overwritten with sum_b grad_out[b]*d/d. */
+int semicrf_score_gold_backward(int64_t B, int64_t T, int64_t K, int64_t C,
+                                const int64_t* labels, const int64_t* lengths,
+                                const float* grad_out, float* grad_cum, float* grad_transition,
+                                float* grad_duration_bias, void* workspace,
+                                size_t workspace_bytes, void* stream);
+size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_t C);
+
+const char* semicrf_strerror(int status);
+int semicrf_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SEMICRF_H_ */

@@ -1,0 +1,300 @@
+"""CUDA path vs the reference (golden fixtures) and the CPU oracle.
+
+Tolerances (north star: 1e-5 relative against a float64 reference run):
+  * partition / Viterbi score: |d| <= 1e-5 * |ref| + 1e-5
+  * gradients: norm-wise, ||d||_inf <= 1e-5 * ||ref||_inf + 1e-6 (per-element
+    relative error is ill-posed for near-zero marginals)
+  * segmentations: identical, or -- at rounding-level near-ties -- a path whose
+    float64 score equals the float64 optimum to 1e-6 relative.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_names, load_golden, streaming_inputs_from_golden
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+
+def _dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+def assert_close_rel(got, ref, rtol=RTOL, atol=1e-5, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(got - ref)
+    bound = rtol * np.abs(ref) + atol
+    bad = err > bound
+    assert not bad.any(), f"{what}: max err {err.max():.3e} at {np.argwhere(bad)[:3].tolist()}"
+
+
+def assert_grad_close(got, ref, rtol=RTOL, floor=1e-6, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = max(np.abs(ref).max(), 0.0)
+    err = np.abs(got - ref).max() if got.size else 0.0
+    assert err <= rtol * scale + floor, f"{what}: ||d||inf={err:.3e} ||ref||inf={scale:.3e}"
+
+
+STREAM = [n for n in golden_names("stream_") + golden_names("cfg") if "kcc" not in n]
+
+
+@pytest.mark.parametrize("name", STREAM)
+def test_streaming_forward_backward_vs_reference(name):
+    from torch_semimarkov_b200 import semi_crf_streaming_forward
+
+    dev = _dev()
+    g = load_golden(name)
+    inp = streaming_inputs_from_golden(g)
+    K = int(g["K"])
+    semiring = str(g["semiring"])
+    leaves = {k: (None if v is None else v.to(dev).requires_grad_(True)) for k, v in inp.items()}
+    lengths = torch.as_tensor(g["lengths"]).to(dev)
+    part = semi_crf_streaming_forward(leaves["cum_scores"], leaves["transition"],
+                                      leaves["duration_bias"], lengths, K, semiring=semiring,
+                                      proj_start=leaves["proj_start"],
+                                      proj_end=leaves["proj_end"])
+    part.backward(torch.as_tensor(g["grad_output"], dtype=torch.float32, device=dev))
+    torch.cuda.synchronize()
+    assert_close_rel(part.detach().cpu().numpy(), g["partition"], what="partition")
+    gc = leaves["cum_scores"].grad.cpu().numpy()
+    if "grad_cum_scores" in g:
+        assert_grad_close(gc, g["grad_cum_scores"], what="grad_cum")
+    else:
+        assert_grad_close(gc[:, :64], g["grad_cum_head"], what="grad_cum head")
+        np.testing.assert_allclose([gc.sum(), np.abs(gc).sum()], g["grad_cum_checksum"],
+                                   rtol=1e-4, atol=1e-3)
+    assert_grad_close(leaves["transition"].grad.cpu().numpy(), g["grad_transition"],
+                      what="grad_transition")
+    assert_grad_close(leaves["duration_bias"].grad.cpu().numpy(), g["grad_duration_bias"],
+                      what="grad_duration_bias")
+    for key in ("proj_start", "proj_end"):
+        if "grad_" + key in g:
+            assert_grad_close(leaves[key].grad.cpu().numpy(), g["grad_" + key], what=key)
+
+
+@pytest.mark.parametrize("name", ["stream_basic", "stream_ckpt_div", "stream_zero_len",
+                                  "stream_k1", "stream_c24", "stream_basic_max"])
+def test_ring_checkpoints_layout_and_values(name):
+    from torch_semimarkov_b200 import launch_streaming_triton_kernel
+
+    dev = _dev()
+    g = load_golden(name)
+    inp = streaming_inputs_from_golden(g)
+    K, T = int(g["K"]), int(g["T"])
+    part, ck, S = launch_streaming_triton_kernel(
+        inp["cum_scores"].to(dev), inp["transition"].to(dev), inp["duration_bias"].to(dev),
+        torch.as_tensor(g["lengths"]).to(dev), K, semiring=str(g["semiring"]))
+    assert S == int(g["checkpoint_interval"])
+    assert ck.shape == ((g["B"]), (T + S - 1) // S + 1, K, int(g["C"]))
+    ref = g["ring_checkpoints"]  # reference PyTorch layout: ceil(T/S) checkpoints
+    got = ck[:, : ref.shape[1]].cpu().numpy()
+    unset = ref <= -1e8
+    np.testing.assert_array_equal(got[unset], np.float32(-1e9))
+    assert_close_rel(got[~unset], ref[~unset], what="checkpoints")
+    assert torch.all(ck[:, 0, 0] == 0)
+
+
+HEAD = golden_names("head_")
+
+
+@pytest.mark.parametrize("name", HEAD)
+def test_head_decode_and_loss_vs_reference(name, oracle):
+    from inputs import make_hidden
+
+    from torch_semimarkov_b200 import SemiMarkovCRFHead
+
+    dev = _dev()
+    g = load_golden(name)
+    B, T, K, C = int(g["B"]), int(g["T"]), int(g["K"]), int(g["C"])
+    hd = int(g["hidden_dim"])
+    p = make_hidden(B, T, C, K, int(g["seed"]), str(g["gen"]), None if hd < 0 else hd)
+    crf = SemiMarkovCRFHead(num_classes=C, max_duration=K, hidden_dim=None if hd < 0 else hd)
+    with torch.no_grad():
+        crf.transition.copy_(p["transition"])
+        crf.duration_dist.duration_bias.copy_(p["duration_bias"])
+        if hd > 0:
+            crf.projection.weight.copy_(p["proj_weight"])
+            crf.projection.bias.copy_(p["proj_bias"])
+    crf = crf.to(dev)
+    hidden = p["hidden"].to(dev)
+    lengths = torch.as_tensor(g["lengths"]).to(dev)
+    labels = p["labels"].to(dev)
+
+    res = crf(hidden, lengths)
+    assert_close_rel(res["partition"].detach().cpu().numpy(), g["partition"], rtol=2e-5,
+                     what="partition")
+    loss = crf.compute_loss(hidden, lengths, labels, reduction="sum")
+    loss.backward()
+    assert abs(float(loss) - float(g["loss_sum"])) <= 2e-5 * abs(float(g["loss_sum"])) + 1e-3
+    assert_grad_close(crf.transition.grad.cpu().numpy(), g["grad_transition"], rtol=2e-5,
+                      floor=1e-4, what="grad_transition")
+    assert_grad_close(crf.duration_dist.duration_bias.grad.cpu().numpy(),
+                      g["grad_duration_bias"], rtol=2e-5, floor=1e-4, what="grad_db")
+    if hd > 0:
+        assert_grad_close(crf.projection.weight.grad.cpu().numpy(), g["grad_proj_weight"],
+                          rtol=1e-4, floor=1e-3, what="grad_proj_weight")
+
+    with torch.no_grad():
+        sc = crf.decode(hidden, lengths)
+        vr = crf.decode_with_traceback(hidden, lengths,
+                                       max_traceback_length=int(g["max_traceback_length"]))
+    L = g["lengths"]
+    assert_close_rel(sc.cpu().numpy()[L > 0], g["decode_scores"][L > 0], what="decode")
+    assert_close_rel(vr.scores.cpu().numpy()[L > 0], g["viterbi_scores"][L > 0], what="viterbi")
+    # float64 optimum of the same float32 cum_scores for near-tie arbitration
+    cum = crf._cum_scores(hidden).detach().cpu().numpy()
+    sc64, _ = oracle.viterbi(cum, g["transition"], g["duration_bias"], L, K, 0)
+    cum64 = cum.astype(np.float64)
+    tr64 = g["transition"].astype(np.float64)
+    db64 = g["duration_bias"].astype(np.float64)
+    for b in range(B):
+        n = int(g["nseg"][b])
+        got = [(s.start, s.end, s.label) for s in vr.segments[b]]
+        ref = [tuple(int(v) for v in x) for x in g["segments"][b, :n]]
+        if got == ref:
+            np.testing.assert_allclose([s.score for s in vr.segments[b]],
+                                       g["segment_scores"][b, :n], rtol=1e-6, atol=1e-5)
+            continue
+        assert len(got) > 0 and got[0][0] == 0 and got[-1][1] == L[b] - 1
+        tot, prev = 0.0, None
+        for (st, en, c) in got:
+            assert en >= st
+            d = min(en - st + 1, K - 1)
+            tot += cum64[b, en + 1, c] - cum64[b, st, c] + db64[d, c]
+            tot += tr64[prev, c] if prev is not None else tr64[:, c].max()
+            prev = c
+        assert abs(tot - sc64[b]) <= 1e-6 * abs(sc64[b]) + 1e-5, (name, b, tot, sc64[b])
+
+
+@pytest.mark.parametrize("name", golden_names("gold_"))
+def test_gold_score_vs_reference(name):
+    from torch_semimarkov_b200 import score_gold_vectorized
+
+    dev = _dev()
+    g = load_golden(name)
+    cum = torch.as_tensor(g["cum_scores"]).float().to(dev).requires_grad_(True)
+    tr = torch.as_tensor(g["transition"]).float().to(dev).requires_grad_(True)
+    db = torch.as_tensor(g["duration_bias"]).float().to(dev).requires_grad_(True)
+    labels = torch.as_tensor(g["labels"]).to(dev)
+    lengths = torch.as_tensor(g["lengths"]).to(dev)
+    K = int(g["K"])
+    out = score_gold_vectorized(cum, labels, lengths, tr, db, K)
+    assert_close_rel(out.detach().cpu().numpy(), g["gold_score"], rtol=1e-5, atol=1e-4,
+                     what="gold")
+    w = torch.linspace(0.5, 1.5, out.shape[0], device=dev)
+    (out * w).sum().backward()
+    # expected gradients: +-w at segment boundaries, transition / duration counts
+    lab, L, T = g["labels"], g["lengths"], int(g["T"])
+    C = int(g["C"])
+    gc = np.zeros((len(L), T + 1, C))
+    gt = np.zeros((C, C))
+    gd = np.zeros((K, C))
+    for b in range(len(L)):
+        wb = float(w[b])
+        if T == 1:
+            if L[b] > 0:
+                gc[b, 1, lab[b, 0]] += wb
+                gc[b, 0, lab[b, 0]] -= wb
+                gd[1, lab[b, 0]] += wb
+            continue
+        st, prev = 0, None
+        for p in range(L[b]):
+            if p == L[b] - 1 or lab[b, p] != lab[b, p + 1]:
+                c = lab[b, st]
+                gc[b, p + 1, c] += wb
+                gc[b, st, c] -= wb
+                gd[min(max(p - st + 1, 1), K - 1), c] += wb
+                if prev is not None:
+                    gt[prev, c] += wb
+                prev, st = c, p + 1
+    np.testing.assert_allclose(cum.grad.cpu().numpy(), gc, atol=1e-6)
+    np.testing.assert_allclose(tr.grad.cpu().numpy(), gt, atol=1e-5)
+    np.testing.assert_allclose(db.grad.cpu().numpy(), gd, atol=1e-5)
+
+
+# ---------------------------------------------------------------------------
+# seeded random cases against the float64 oracle (sizes it finishes in seconds)
+# ---------------------------------------------------------------------------
+
+ORACLE_CASES = [
+    # B, T, K, C, gen, proj, semiring
+    (4, 257, 17, 5, "default", None, "log"),
+    (3, 300, 40, 24, "cfg2", None, "log"),
+    (2, 400, 64, 8, "cfg3", "both", "log"),
+    (2, 97, 13, 33, "default", "start", "log"),
+    (2, 150, 10, 64, "default", None, "log"),
+    (2, 60, 9, 130, "default", "end", "log"),
+    (3, 180, 25, 16, "cfg5", None, "max"),
+    (2, 120, 1, 6, "default", None, "log"),
+    (2, 90, 2, 7, "default", None, "max"),
+]
+
+
+@pytest.mark.parametrize("case", ORACLE_CASES)
+def test_random_vs_oracle(case, oracle):
+    from inputs import make_streaming_inputs
+
+    from torch_semimarkov_b200 import semi_crf_streaming_forward
+
+    B, T, K, C, gen, proj, semiring = case
+    dev = _dev()
+    inp = make_streaming_inputs(B, T, K, C, seed=100 + T + K + C, gen=gen, proj=proj)
+    rng = np.random.default_rng(T)
+    lengths = np.concatenate([[T], rng.integers(max(1, T // 3), T + 1, size=B - 1)])
+    gout = rng.uniform(0.5, 1.5, size=B)
+    np_in = {k: (None if v is None else v.numpy()) for k, v in inp.items()}
+    part_ref, grads_ref = oracle.forward_backward(
+        np_in["cum_scores"], np_in["transition"], np_in["duration_bias"], lengths, K, gout,
+        semiring, np_in["proj_start"], np_in["proj_end"], threads=8)
+    leaves = {k: (None if v is None else v.to(dev).requires_grad_(True)) for k, v in inp.items()}
+    part = semi_crf_streaming_forward(leaves["cum_scores"], leaves["transition"],
+                                      leaves["duration_bias"], torch.as_tensor(lengths).to(dev),
+                                      K, semiring=semiring, proj_start=leaves["proj_start"],
+                                      proj_end=leaves["proj_end"])
+    part.backward(torch.as_tensor(gout, dtype=torch.float32, device=dev))
+    assert_close_rel(part.detach().cpu().numpy(), part_ref, what="partition")
+    assert_grad_close(leaves["cum_scores"].grad.cpu().numpy(), grads_ref["cum_scores"],
+                      what="grad_cum")
+    assert_grad_close(leaves["transition"].grad.cpu().numpy(), grads_ref["transition"],
+                      what="grad_tr")
+    assert_grad_close(leaves["duration_bias"].grad.cpu().numpy(), grads_ref["duration_bias"],
+                      what="grad_db")
+    for key in ("proj_start", "proj_end"):
+        if leaves[key] is not None:
+            assert_grad_close(leaves[key].grad.cpu().numpy(), grads_ref[key], what=key)
+
+
+def test_decode_batch_vs_oracle(oracle):
+    """Config-5-shaped Viterbi batch (ragged lengths) against the float64 oracle."""
+    from inputs import make_streaming_inputs
+
+    from torch_semimarkov_b200 import _lib
+
+    dev = _dev()
+    B, T, K, C = 16, 512, 32, 16
+    inp = make_streaming_inputs(B, T, K, C, seed=55, gen="cfg5")
+    lengths = np.random.default_rng(5).integers(T // 2, T + 1, size=B)
+    prob = _lib.Problem(inp["cum_scores"].to(dev), inp["transition"].to(dev),
+                        inp["duration_bias"].to(dev), torch.as_tensor(lengths).to(dev), K, "max")
+    scores, ss, se, sl, sv, ns = _lib.viterbi(prob, 10000)
+    sc64, segs64 = oracle.viterbi(inp["cum_scores"].numpy(), inp["transition"].numpy(),
+                                  inp["duration_bias"].numpy(), lengths, K, 10000, threads=8)
+    assert_close_rel(scores.cpu().numpy(), sc64, what="viterbi score")
+    ns = ns.cpu().numpy()
+    same = 0
+    for b in range(B):
+        got = list(zip(ss[b, : ns[b]].tolist(), se[b, : ns[b]].tolist(), sl[b, : ns[b]].tolist()))
+        ref = [s[:3] for s in segs64[b]]
+        same += got == ref
+        # coverage and score of the decoded path
+        assert got[0][0] == 0 and got[-1][1] == lengths[b] - 1
+        assert all(got[i][0] == got[i - 1][1] + 1 for i in range(1, len(got)))
+        seg_sum = float(sv[b, : ns[b]].sum())
+        assert abs(seg_sum - sc64[b]) <= 1e-5 * abs(sc64[b]) + 1e-3
+    assert same >= B - 1, f"only {same}/{B} segmentations identical"

@@ -1,0 +1,405 @@
+// api.cu -- the extern "C" entry points declared in include/semicrf.h.
+//
+// Every entry point validates its arguments, carves the caller-provided
+// workspace, and enqueues kernels on the given stream.  No device memory is
+// allocated here and nothing synchronises.
+
+#include <cmath>
+#include <cstring>
+
+#include "semicrf_internal.cuh"
+
+using namespace semicrf;
+
+namespace {
+
+constexpr int kP = 8;  // chain block size (chain_block_size)
+
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) & ~size_t(255);
+    T* r = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return r;
+  }
+  size_t bytes() const { return (off + 255) & ~size_t(255); }
+};
+
+int kcap_of(int64_t K) { return K > 1 ? (int)(K - 1) : 1; }
+int sint_of(const semicrf_problem* p) {
+  const int64_t S = p->checkpoint_interval;
+  return (int)(((S + kP - 1) / kP) * kP);
+}
+int nint_of(const semicrf_problem* p) { return (int)(p->T / sint_of(p) + 1); }
+
+// shape-level checks (used by the size queries, which take no pointers)
+int validate_shape(const semicrf_problem* p) {
+  if (!p) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (p->batch < 0 || p->T < 0 || p->K < 1 || p->C < 1) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (p->semiring != SEMICRF_LOG && p->semiring != SEMICRF_MAX) return SEMICRF_ERR_SEMIRING;
+  if (p->transition_ndim != 2 && p->transition_ndim != 3) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (p->checkpoint_interval < p->K) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (p->C > 256 || p->T > (int64_t)1 << 30 || p->K > 32767) return SEMICRF_ERR_UNSUPPORTED;
+  if (p->transition_ndim == 3) return SEMICRF_ERR_UNSUPPORTED;
+  if (!chain_supported((int)p->C, (int)p->K, p->semiring, p->semiring == SEMICRF_MAX))
+    return SEMICRF_ERR_UNSUPPORTED;
+  return SEMICRF_OK;
+}
+
+int validate(const semicrf_problem* p) {
+  const int st = validate_shape(p);
+  if (st != SEMICRF_OK) return st;
+  if (p->batch > 0 && (!p->cum_scores || !p->transition || !p->duration_bias || !p->lengths))
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  return SEMICRF_OK;
+}
+
+Prepared carve_prep(Carver& cv, int C, int K) {
+  Prepared pr{};
+  const int kx = kcap_of(K) + kP + 1;
+  pr.mx_f = cv.take<float>((size_t)C * C);
+  pr.mx_b = cv.take<float>((size_t)C * C);
+  pr.colmax_f = cv.take<float>(C);
+  pr.colmax_b = cv.take<float>(C);
+  pr.dbl = cv.take<float>((size_t)kx * C);
+  pr.dbe = cv.take<float>((size_t)kx * C);
+  pr.dbmax = cv.take<float>(C);
+  pr.kx = kx;
+  return pr;
+}
+
+struct SavedLayout {
+  double* logz;
+  float* sv_f;
+  double* sv_d;
+};
+
+SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
+  SavedLayout s{};
+  const size_t B = p->batch, C = p->C;
+  const size_t kc = kcap_of(p->K), nint = nint_of(p);
+  s.logz = cv.take<double>(B);
+  s.sv_f = cv.take<float>(B * nint * (kc * C + 2 * C));
+  s.sv_d = cv.take<double>(B * nint * kc);
+  return s;
+}
+
+ChainArgs base_args(const semicrf_problem* p) {
+  ChainArgs a{};
+  a.cum = p->cum_scores;
+  a.ps = p->proj_start;
+  a.pe = p->proj_end;
+  a.lengths = p->lengths;
+  return a;
+}
+
+ChainLaunch base_launch(const semicrf_problem* p, const Prepared& pr) {
+  ChainLaunch L{};
+  L.B = (int)p->batch;
+  L.T = (int)p->T;
+  L.K = (int)p->K;
+  L.C = (int)p->C;
+  L.kcap = kcap_of(p->K);
+  L.prep = pr;
+  return L;
+}
+
+struct BwdLayout {
+  Prepared pr;
+  float *xa, *ma, *xb, *mb, *pstart, *alse, *part_tr, *part_db;
+  double *na, *nb;
+};
+
+BwdLayout carve_bwd(Carver& cv, const semicrf_problem* p) {
+  BwdLayout w{};
+  w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
+  const size_t nt = (size_t)p->batch * (p->T + 1);
+  w.xa = cv.take<float>(n);
+  w.ma = cv.take<float>(n);
+  w.xb = cv.take<float>(n);
+  w.mb = cv.take<float>(n);
+  w.pstart = cv.take<float>(n);
+  w.alse = p->semiring == SEMICRF_MAX ? cv.take<float>(n) : nullptr;
+  w.na = cv.take<double>(nt);
+  w.nb = cv.take<double>(nt);
+  w.part_tr = cv.take<float>((size_t)p->batch * p->C * p->C);
+  w.part_db = cv.take<float>((size_t)p->batch * p->K * p->C);
+  return w;
+}
+
+struct VitLayout {
+  Prepared pr;
+  int16_t* bp_k;
+  uint8_t* bp_c;
+  int* final_c;
+};
+
+VitLayout carve_vit(Carver& cv, const semicrf_problem* p) {
+  VitLayout w{};
+  w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
+  w.bp_k = cv.take<int16_t>(n);
+  w.bp_c = cv.take<uint8_t>(n);
+  w.final_c = cv.take<int>(p->batch);
+  return w;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? SEMICRF_OK : SEMICRF_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+int semicrf_abi_version(void) { return SEMICRF_ABI_VERSION; }
+
+const char* semicrf_strerror(int status) {
+  switch (status) {
+    case SEMICRF_OK: return "ok";
+    case SEMICRF_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SEMICRF_ERR_UNSUPPORTED: return "unsupported problem shape";
+    case SEMICRF_ERR_WORKSPACE: return "workspace too small";
+    case SEMICRF_ERR_CUDA: return "CUDA launch failed";
+    case SEMICRF_ERR_SEMIRING: return "semiring must be 'log' or 'max'";
+    default: return "unknown error";
+  }
+}
+
+int64_t semicrf_checkpoint_interval(int64_t T, int64_t K) {
+  const int64_t opt = (int64_t)std::sqrt((double)(T * K));
+  return opt > K ? opt : K;
+}
+
+size_t semicrf_saved_size(const semicrf_problem* p) {
+  if (validate_shape(p) != SEMICRF_OK) return 0;
+  Carver cv(nullptr);
+  carve_saved(cv, p);
+  return cv.bytes();
+}
+
+size_t semicrf_forward_workspace_size(const semicrf_problem* p) {
+  if (validate_shape(p) != SEMICRF_OK) return 0;
+  Carver cv(nullptr);
+  carve_prep(cv, (int)p->C, (int)p->K);
+  return cv.bytes();
+}
+
+int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_checkpoints,
+                    int64_t num_ring_checkpoints, void* saved, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  int st = validate(p);
+  if (st != SEMICRF_OK) return st;
+  if (p->batch == 0) return SEMICRF_OK;
+  if (!partition) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (ring_checkpoints && num_ring_checkpoints < 1) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < semicrf_forward_workspace_size(p) || !workspace)
+    return SEMICRF_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carver cv(workspace);
+  Prepared pr = carve_prep(cv, (int)p->C, (int)p->K);
+  cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
+                              kcap_of(p->K), kP, p->semiring, pr, s);
+  if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+  ChainLaunch L = base_launch(p, pr);
+  ChainArgs a = base_args(p);
+  a.mode = 0;
+  a.dir = 0;
+  a.mx = pr.mx_f;
+  a.colmax = pr.colmax_f;
+  a.partition = partition;
+  a.ref_ckpt = ring_checkpoints;
+  a.nref = (int)num_ring_checkpoints;
+  a.sref = (int)p->checkpoint_interval;
+  a.sint = sint_of(p);
+  a.nint = nint_of(p);
+  if (saved) {
+    Carver sc(saved);
+    SavedLayout sl = carve_saved(sc, p);
+    a.logz = sl.logz;
+    a.sv_f = sl.sv_f;
+    a.sv_d = sl.sv_d;
+    a.write_saved = 1;
+  }
+  L.a0 = a;
+  L.a1 = a;
+  L.n1 = (int)p->batch;
+  return cuda_status(launch_chain(L, (int)p->batch, p->semiring, false, s));
+}
+
+size_t semicrf_backward_workspace_size(const semicrf_problem* p) {
+  if (validate_shape(p) != SEMICRF_OK) return 0;
+  Carver cv(nullptr);
+  carve_bwd(cv, p);
+  return cv.bytes();
+}
+
+int semicrf_backward(const semicrf_problem* p, const void* saved, const float* grad_output,
+                     float* grad_cum, float* grad_transition, float* grad_duration_bias,
+                     float* grad_proj_start, float* grad_proj_end, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  int st = validate(p);
+  if (st != SEMICRF_OK) return st;
+  if (p->batch == 0) return SEMICRF_OK;
+  if (!saved || !grad_output || !grad_cum || !grad_transition || !grad_duration_bias)
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  if ((p->proj_start && !grad_proj_start) || (p->proj_end && !grad_proj_end))
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < semicrf_backward_workspace_size(p) || !workspace)
+    return SEMICRF_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carver cv(workspace);
+  BwdLayout w = carve_bwd(cv, p);
+  Carver sc(const_cast<void*>(saved));
+  SavedLayout sl = carve_saved(sc, p);
+  cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
+                              kcap_of(p->K), kP, p->semiring, w.pr, s);
+  if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+
+  // beta chains (one per sequence) and alpha checkpoint segments, one launch
+  ChainLaunch L = base_launch(p, w.pr);
+  ChainArgs ab = base_args(p);
+  ab.mode = 0;
+  ab.dir = 1;
+  ab.mx = w.pr.mx_b;
+  ab.colmax = w.pr.colmax_b;
+  ab.tab_x = w.xb;
+  ab.tab_m = w.mb;
+  ab.tab_n = w.nb;
+  ChainArgs aa = base_args(p);
+  aa.mode = 1;
+  aa.dir = 0;
+  aa.mx = w.pr.mx_f;
+  aa.colmax = w.pr.colmax_f;
+  aa.sv_f = sl.sv_f;
+  aa.sv_d = sl.sv_d;
+  aa.sint = sint_of(p);
+  aa.nint = nint_of(p);
+  aa.tab_x = w.xa;
+  aa.tab_m = w.ma;
+  aa.tab_n = w.na;
+  L.a0 = ab;
+  L.a1 = aa;
+  L.n1 = (int)p->batch;
+  const int grid = (int)p->batch + (int)p->batch * aa.nint;
+  e = launch_chain(L, grid, p->semiring, false, s);
+  if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+
+  MargArgs m{};
+  m.B = (int)p->batch;
+  m.T = (int)p->T;
+  m.K = (int)p->K;
+  m.C = (int)p->C;
+  m.kcap = kcap_of(p->K);
+  m.cum = p->cum_scores;
+  m.ps = p->proj_start;
+  m.pe = p->proj_end;
+  m.tr = p->transition;
+  m.dbl = w.pr.dbl;
+  m.lengths = p->lengths;
+  m.logz = sl.logz;
+  m.grad_output = grad_output;
+  m.xa = w.xa;
+  m.ma = w.ma;
+  m.na = w.na;
+  m.xb = w.xb;
+  m.mb = w.mb;
+  m.nb = w.nb;
+  m.grad_cum = grad_cum;
+  m.grad_ps = p->proj_start ? grad_proj_start : nullptr;
+  m.grad_pe = p->proj_end ? grad_proj_end : nullptr;
+  m.part_tr = w.part_tr;
+  m.part_db = w.part_db;
+  e = launch_marginals_impl(m, p->semiring, w.alse, w.pstart, s);
+  if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+  return cuda_status(launch_reduce_shared(m, grad_transition, grad_duration_bias, s));
+}
+
+size_t semicrf_viterbi_workspace_size(const semicrf_problem* p) {
+  if (validate_shape(p) != SEMICRF_OK) return 0;
+  Carver cv(nullptr);
+  carve_vit(cv, p);
+  return cv.bytes();
+}
+
+int semicrf_viterbi(const semicrf_problem* p, int64_t max_traceback_length, float* scores,
+                    int32_t* seg_start, int32_t* seg_end, int32_t* seg_label, double* seg_score,
+                    int32_t* nseg, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate(p);
+  if (st != SEMICRF_OK) return st;
+  if (p->batch == 0) return SEMICRF_OK;
+  if (p->semiring != SEMICRF_MAX) return SEMICRF_ERR_SEMIRING;
+  if (p->proj_start || p->proj_end) return SEMICRF_ERR_UNSUPPORTED;  // nn.py:479 has none
+  if (!scores || !seg_start || !seg_end || !seg_label || !seg_score || !nseg)
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < semicrf_viterbi_workspace_size(p) || !workspace)
+    return SEMICRF_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carver cv(workspace);
+  VitLayout w = carve_vit(cv, p);
+  cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
+                              kcap_of(p->K), kP, SEMICRF_MAX, w.pr, s);
+  if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+  ChainLaunch L = base_launch(p, w.pr);
+  ChainArgs a = base_args(p);
+  a.mode = 0;
+  a.dir = 0;
+  a.mx = w.pr.mx_f;
+  a.colmax = w.pr.colmax_f;
+  a.score = scores;
+  a.bp_k = w.bp_k;
+  a.bp_c = w.bp_c;
+  a.final_c = w.final_c;
+  L.a0 = a;
+  L.a1 = a;
+  L.n1 = (int)p->batch;
+  e = launch_chain(L, (int)p->batch, SEMICRF_MAX, true, s);
+  if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+  return cuda_status(launch_backtrace((int)p->batch, (int)p->T, (int)p->K, (int)p->C,
+                                      p->cum_scores, p->transition, p->duration_bias,
+                                      p->lengths, max_traceback_length, w.bp_k, w.bp_c,
+                                      w.final_c, seg_start, seg_end, seg_label, seg_score,
+                                      nseg, s));
+}
+
+int semicrf_score_gold(int64_t B, int64_t T, int64_t K, int64_t C, const float* cum_scores,
+                       const int64_t* labels, const int64_t* lengths, const float* transition,
+                       const float* duration_bias, float* out, void* stream) {
+  if (B < 0 || T < 0 || K < 1 || C < 1) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (B == 0) return SEMICRF_OK;
+  if (T == 1 && K < 2) return SEMICRF_ERR_INVALID_ARGUMENT;  // helpers.py:412 indexes db[1]
+  if (!cum_scores || !labels || !lengths || !transition || !duration_bias || !out)
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  return cuda_status(launch_gold((int)B, (int)T, (int)K, (int)C, cum_scores, labels, lengths,
+                                 transition, duration_bias, out,
+                                 static_cast<cudaStream_t>(stream)));
+}
+
+size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_t C) {
+  (void)T;
+  if (B < 0 || K < 1 || C < 1) return 0;
+  return (size_t)B * (C * C + K * C) * sizeof(float) + 256;
+}
+
+int semicrf_score_gold_backward(int64_t B, int64_t T, int64_t K, int64_t C,
+                                const int64_t* labels, const int64_t* lengths,
+                                const float* grad_out, float* grad_cum, float* grad_transition,
+                                float* grad_duration_bias, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (B < 0 || T < 0 || K < 1 || C < 1) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (T == 1 && K < 2) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (B == 0) return SEMICRF_OK;
+  if (!labels || !lengths || !grad_out || !grad_cum || !grad_transition || !grad_duration_bias)
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (!workspace || workspace_bytes < semicrf_score_gold_workspace_size(B, T, K, C))
+    return SEMICRF_ERR_WORKSPACE;
+  return cuda_status(launch_gold_backward((int)B, (int)T, (int)K, (int)C, labels, lengths,
+                                          grad_out, grad_cum, grad_transition,
+                                          grad_duration_bias, static_cast<float*>(workspace),
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

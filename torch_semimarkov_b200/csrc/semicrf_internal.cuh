@@ -1,0 +1,157 @@
+// Internal declarations shared by the CUDA translation units of libsemicrf.
+//
+// Numerical conventions (all kernels):
+//  * Scores are natural-log float32.  Every chain keeps its values relative
+//    to an integer-valued per-block normaliser N (float64), so stored
+//    quantities stay O(10) and differences N(s) - N(u) are exact in float32.
+//  * Prefix-sum differences cum[u] - cum[s] are always formed first (they
+//    are exact or nearly so) before small terms are added.
+//  * "-inf" is a real IEEE -inf internally; the reference's NEG_INF (-1e9)
+//    only appears at the API boundary (checkpoints of unreached positions,
+//    the partition of an empty sequence).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/semicrf.h"
+
+namespace semicrf {
+
+constexpr float kNegInf = -__builtin_huge_valf();
+constexpr float kRefNegInf = -1e9f;  // streaming/constants.py:10
+
+// ---------------------------------------------------------------------------
+// small device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float ex(float x) {  // e^x, x <= 0 in all uses that matter
+  return __expf(x);
+}
+__device__ __forceinline__ float lg(float x) { return __logf(x); }
+
+__device__ __forceinline__ float warp_max(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// per-launch constants prepared by prep_kernel (chain.cu)
+// ---------------------------------------------------------------------------
+struct Prepared {
+  // mat-vec operand for the forward chain (M = transition) and the backward
+  // chain (M = transition^T).  Log semiring: exp(M - colmax); max: M.
+  float* mx_f;
+  float* mx_b;
+  float* colmax_f;  // (C)
+  float* colmax_b;
+  float* dbl;       // (KX, C): log duration bias by duration k, -inf outside 1..kcap
+  float* dbe;       // (KX, C): exp(dbl - dbmax)
+  float* dbmax;     // (C)
+  int kx;           // rows of dbl / dbe = kcap + P + 1
+};
+
+// One chain role (see chain.cu for the algorithm).
+struct ChainArgs {
+  int mode;   // 0 = whole sequence, 1 = one checkpoint segment (restart)
+  int dir;    // 0 = forward (alpha), 1 = backward (beta)
+  // inputs
+  const float* cum;
+  const float* ps;
+  const float* pe;
+  const int64_t* lengths;
+  // prepared constants
+  const float* mx;
+  const float* colmax;
+  // forward outputs
+  float* partition;      // (B)
+  double* logz;          // (B)
+  float* ref_ckpt;       // (B, nref, K, C) reference layout, or null
+  int nref;
+  int sref;
+  // restart state
+  float* sv_f;           // (B, nint, kcap*C + 2*C)
+  double* sv_d;          // (B, nint, kcap)
+  int nint;
+  int sint;              // multiple of P
+  int write_saved;
+  // tables indexed by cum position t, or null
+  float* tab_x;          // (B, T+1, C)
+  float* tab_m;          // (B, T+1, C)
+  double* tab_n;         // (B, T+1)
+  // Viterbi
+  int16_t* bp_k;         // (B, T+1, C)
+  uint8_t* bp_c;         // (B, T+1, C)
+  int* final_c;          // (B)
+  float* score;          // (B) max-semiring score
+};
+
+struct ChainLaunch {
+  int B, T, K, C, kcap;
+  Prepared prep;
+  int n1;          // CTAs [0, n1) run role a0, [n1, grid) run role a1
+  ChainArgs a0;
+  ChainArgs a1;
+};
+
+// launchers (chain.cu)
+cudaError_t launch_prep(const float* tr, const float* db, int K, int C, int kcap, int P,
+                        int semiring, const Prepared& prep, cudaStream_t s);
+cudaError_t launch_chain(const ChainLaunch& L, int grid, int semiring, bool backpointers,
+                         cudaStream_t s);
+int chain_block_size(int C);  // P used by launch_chain for this C
+size_t chain_smem_bytes(int C, int K, int semiring, bool backpointers);
+bool chain_supported(int C, int K, int semiring, bool backpointers);
+
+// marginals.cu
+struct MargArgs {
+  int B, T, K, C, kcap;
+  const float* cum;
+  const float* ps;
+  const float* pe;
+  const float* tr;
+  const float* dbl;
+  const int64_t* lengths;
+  const double* logz;
+  const float* grad_output;
+  const float* xa; const float* ma; const double* na;
+  const float* xb; const float* mb; const double* nb;
+  float* grad_cum;
+  float* grad_ps;
+  float* grad_pe;
+  float* part_tr;  // (B, C*C) per-sequence transition gradients
+  float* part_db;  // (B, K*C) per-sequence duration-bias gradients
+};
+// semiring 0 = log, 1 = max; alse / pstart are (B, T+1, C) scratch tables
+cudaError_t launch_marginals_impl(const MargArgs& a, int semiring, float* alse, float* pstart,
+                                  cudaStream_t s);
+cudaError_t launch_reduce_shared(const MargArgs& a, float* grad_tr, float* grad_db,
+                                 cudaStream_t s);
+
+// viterbi.cu
+cudaError_t launch_backtrace(int B, int T, int K, int C, const float* cum, const float* tr,
+                             const float* db, const int64_t* lengths, int64_t max_len,
+                             const int16_t* bp_k, const uint8_t* bp_c, const int* final_c,
+                             int32_t* seg_start, int32_t* seg_end, int32_t* seg_label,
+                             double* seg_score, int32_t* nseg, cudaStream_t s);
+
+// gold.cu
+cudaError_t launch_gold(int B, int T, int K, int C, const float* cum, const int64_t* labels,
+                        const int64_t* lengths, const float* tr, const float* db, float* out,
+                        cudaStream_t s);
+cudaError_t launch_gold_backward(int B, int T, int K, int C, const int64_t* labels,
+                                 const int64_t* lengths, const float* grad_out,
+                                 float* grad_cum, float* grad_tr, float* grad_db,
+                                 float* part, cudaStream_t s);
+
+}  // namespace semicrf

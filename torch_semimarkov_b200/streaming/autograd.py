@@ -1,0 +1,139 @@
+"""Autograd functions and the public entry point of the streaming semi-CRF.
+
+Mirrors streaming/autograd.py of torch-semimarkov 0.2.0 (the drop-in
+boundary): ``semi_crf_streaming_forward`` keeps its signature and semantics
+(:270-431); ``use_triton`` / ``use_compile`` are accepted and ignored because
+there is exactly one backend -- the sm_100a kernels of libsemicrf.so.
+``SemiCRFStreaming`` and ``SemiCRFStreamingTriton`` are the same
+autograd.Function (the reference has a PyTorch one and a Triton one,
+:33-267).  The launcher names of the reference's Triton path
+(``launch_streaming_triton_kernel`` / ``launch_streaming_triton_backward``,
+triton_forward.py:554 / triton_backward.py:556) are kept with their return
+conventions so callers and tests written against them run unchanged.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import _lib
+
+HAS_TRITON = True  # kept for API compatibility: the launcher names below exist
+
+
+class SemiCRFStreaming(torch.autograd.Function):
+    """Streaming semi-CRF log-partition (or max score) with a checkpointed backward.
+
+    Forward: one CUDA chain per sequence keeps the O(K*C) ring on chip and
+    saves normalised ring checkpoints every S' (a multiple of the block size
+    >= S = max(K, sqrt(T*K))).  Backward: beta chains and alpha recomputes
+    between checkpoints run in one launch, then per-position marginals give
+    the gradients.  Shared-parameter gradients are sum_b grad_output[b] *
+    marginals_b (reference autograd.py:134-145).
+    """
+
+    @staticmethod
+    def forward(ctx, cum_scores, transition, duration_bias, lengths, K, semiring="log",
+                proj_start=None, proj_end=None):
+        prob = _lib.Problem(cum_scores, transition, duration_bias, lengths, K, semiring,
+                            proj_start, proj_end)
+        partition, _, saved = _lib.forward(prob, want_saved=True)
+        ctx.prob = prob
+        ctx.saved_state = saved
+        ctx.in_dtypes = (cum_scores.dtype, transition.dtype, duration_bias.dtype,
+                         None if proj_start is None else proj_start.dtype,
+                         None if proj_end is None else proj_end.dtype)
+        return partition.to(cum_scores.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        prob = ctx.prob
+        gc, gt, gd, gps, gpe = _lib.backward(prob, ctx.saved_state, grad_output)
+        dts = ctx.in_dtypes
+        gc = gc.to(dts[0])
+        gt = gt.to(dts[1])
+        gd = gd.to(dts[2])
+        if gps is not None:
+            gps = gps.to(dts[3])
+        if gpe is not None:
+            gpe = gpe.to(dts[4])
+        ctx.prob = None
+        ctx.saved_state = None
+        return gc, gt, gd, None, None, None, gps, gpe
+
+
+SemiCRFStreamingTriton = SemiCRFStreaming
+
+
+def semi_crf_streaming_forward(
+    cum_scores: torch.Tensor,
+    transition: torch.Tensor,
+    duration_bias: torch.Tensor,
+    lengths: torch.Tensor,
+    K: int,
+    semiring: str = "log",
+    proj_start: Optional[torch.Tensor] = None,
+    proj_end: Optional[torch.Tensor] = None,
+    use_triton: bool = True,
+    use_compile: bool = False,
+) -> torch.Tensor:
+    """Semi-CRF partition function (log) or best score (max) with streaming
+    edges, shape (batch,).  Same arguments as the reference
+    (streaming/autograd.py:270-431):
+
+    cum_scores (batch, T+1, C) float32 prefix sums of the projected scores;
+    transition (C, C) [src, dst] or (K, C, C); duration_bias (K, C);
+    lengths (batch,); K max duration (durations 1..max(1, K-1));
+    semiring "log" | "max"; proj_start / proj_end (batch, T, C) optional.
+    ``use_triton`` and ``use_compile`` are ignored (one backend).
+    """
+    if semiring not in ("log", "max"):
+        raise ValueError(f"semiring must be 'log' or 'max', got {semiring!r}")
+    needs_grad = (
+        cum_scores.requires_grad
+        or transition.requires_grad
+        or duration_bias.requires_grad
+        or (proj_start is not None and proj_start.requires_grad)
+        or (proj_end is not None and proj_end.requires_grad)
+    )
+    if needs_grad and torch.is_grad_enabled():
+        return SemiCRFStreaming.apply(cum_scores, transition, duration_bias, lengths, K,
+                                      semiring, proj_start, proj_end)
+    prob = _lib.Problem(cum_scores, transition, duration_bias, lengths, K, semiring,
+                        proj_start, proj_end)
+    partition, _, _ = _lib.forward(prob, want_saved=False)
+    return partition.to(cum_scores.dtype)
+
+
+def launch_streaming_triton_kernel(cum_scores, transition, duration_bias, lengths, K,
+                                   semiring="log", checkpoint_interval=None, proj_start=None,
+                                   proj_end=None):
+    """Forward launcher with the reference Triton launcher's contract
+    (triton_forward.py:554-714): returns (partition (B,), ring_checkpoints
+    (B, ceil(T/S)+1, K, C), S).  Checkpoint i holds the ring of alpha after
+    position i*S (slot p % K holds alpha[p]); unset entries are NEG_INF."""
+    prob = _lib.Problem(cum_scores, transition, duration_bias, lengths, K, semiring,
+                        proj_start, proj_end, checkpoint_interval)
+    n = (prob.T + prob.S - 1) // prob.S + 1
+    partition, ck, _ = _lib.forward(prob, want_saved=False, num_ring_checkpoints=n)
+    return partition, ck, prob.S
+
+
+def launch_streaming_triton_backward(cum_scores, transition, duration_bias, lengths, log_Z,
+                                     ring_checkpoints, checkpoint_interval, grad_output,
+                                     proj_start=None, proj_end=None):
+    """Backward launcher with the reference contract (triton_backward.py:556-790):
+    returns (grad_cum, grad_transition, grad_duration_bias, grad_proj_start,
+    grad_proj_end), shared-parameter gradients already reduced with
+    grad_output.  The float32 ring checkpoints of the reference format are too
+    coarse (absolute alpha values) for the 1e-5 gradient contract, so the
+    normalised checkpoints are regenerated by a forward pass here; ``log_Z``
+    and ``ring_checkpoints`` are accepted for signature compatibility.  K is
+    taken from duration_bias.shape[0]."""
+    K = duration_bias.shape[0]
+    prob = _lib.Problem(cum_scores, transition, duration_bias, lengths, K, "log",
+                        proj_start, proj_end, checkpoint_interval)
+    _, _, saved = _lib.forward(prob, want_saved=True)
+    return _lib.backward(prob, saved, grad_output)
