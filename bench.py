@@ -331,7 +331,8 @@ def main():
         "compute_roofline": {"terms_per_launch": terms,
                              "achieved_gterms_s": terms / t_fwd / 1e9,
                              "ns_per_position_step": t_fwd / T * 1e9},
-        "gpu_launches": 9 * args.steps,
+        # per step: forward = prep + chain; backward = prep + beta chain + reduce
+        "gpu_launches": 5 * args.steps,
         "clocks": clocks,
     }
     if viterbi:

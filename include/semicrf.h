@@ -70,7 +70,16 @@ typedef struct semicrf_problem {
     const float* proj_start;      /* (B, T, C) or NULL */
     const float* proj_end;        /* (B, T, C) or NULL */
     int64_t checkpoint_interval;  /* S >= K (see semicrf_checkpoint_interval) */
+    int32_t backward_mode;        /* what the forward keeps for the backward:
+                                     SEMICRF_KEEP_ALPHA: float64 alpha tables,
+                                       O(B*T*C) memory, no recompute;
+                                     SEMICRF_RECOMPUTE: ring checkpoints every
+                                       S' >= S, O(B*T/S*K*C) memory, alpha is
+                                       recomputed segment-parallel */
+    int32_t reserved;
 } semicrf_problem;
+
+enum semicrf_backward_mode { SEMICRF_KEEP_ALPHA = 0, SEMICRF_RECOMPUTE = 1 };
 
 /* _compute_checkpoint_interval: max(K, floor(sqrt(T*K))). */
 int64_t semicrf_checkpoint_interval(int64_t T, int64_t K);

@@ -127,18 +127,42 @@ def test_head_decode_and_loss_vs_reference(name, oracle):
     labels = p["labels"].to(dev)
 
     res = crf(hidden, lengths)
-    assert_close_rel(res["partition"].detach().cpu().numpy(), g["partition"], rtol=2e-5,
-                     what="partition")
+    # float64 oracle on the same float32 cum_scores: the tight (1e-5) check
+    cum_np = res["cum_scores"].detach().cpu().numpy()
+    part_ref, gr = oracle.forward_backward(cum_np, g["transition"], g["duration_bias"],
+                                           g["lengths"], K, threads=8)
+    assert_close_rel(res["partition"].detach().cpu().numpy(), part_ref, what="partition")
+    # the fixture was produced by the reference module in float32: compare loosely
+    assert_close_rel(res["partition"].detach().cpu().numpy(), g["partition"], rtol=2e-4,
+                     atol=1e-2, what="partition vs float32 reference")
     loss = crf.compute_loss(hidden, lengths, labels, reduction="sum")
     loss.backward()
-    assert abs(float(loss) - float(g["loss_sum"])) <= 2e-5 * abs(float(g["loss_sum"])) + 1e-3
-    assert_grad_close(crf.transition.grad.cpu().numpy(), g["grad_transition"], rtol=2e-5,
-                      floor=1e-4, what="grad_transition")
+    gold = oracle.score_gold(cum_np, g["labels"], g["lengths"], g["transition"],
+                             g["duration_bias"], K)
+    assert abs(float(loss) - float((part_ref - gold).sum())) <= 1e-5 * abs(float(loss)) + 1e-3
+    assert abs(float(loss) - float(g["loss_sum"])) <= 2e-4 * abs(float(g["loss_sum"])) + 1e-2
+    # d loss / d transition = d partition / d transition - gold transition counts
+    lab, Ls = g["labels"], g["lengths"]
+    gt_gold = np.zeros((C, C))
+    gd_gold = np.zeros((K, C))
+    for b in range(B):
+        st, prev = 0, None
+        for pos in range(Ls[b]):
+            if pos == Ls[b] - 1 or lab[b, pos] != lab[b, pos + 1]:
+                cl = lab[b, st]
+                gd_gold[min(max(pos - st + 1, 1), K - 1), cl] += 1
+                if prev is not None:
+                    gt_gold[prev, cl] += 1
+                prev, st = cl, pos + 1
+    assert_grad_close(crf.transition.grad.cpu().numpy(), gr["transition"] - gt_gold,
+                      what="grad_transition")
     assert_grad_close(crf.duration_dist.duration_bias.grad.cpu().numpy(),
-                      g["grad_duration_bias"], rtol=2e-5, floor=1e-4, what="grad_db")
+                      gr["duration_bias"] - gd_gold, what="grad_duration_bias")
+    assert_grad_close(crf.transition.grad.cpu().numpy(), g["grad_transition"], rtol=2e-3,
+                      floor=1e-3, what="grad_transition vs float32 reference")
     if hd > 0:
         assert_grad_close(crf.projection.weight.grad.cpu().numpy(), g["grad_proj_weight"],
-                          rtol=1e-4, floor=1e-3, what="grad_proj_weight")
+                          rtol=2e-3, floor=1e-3, what="grad_proj_weight vs float32 reference")
 
     with torch.no_grad():
         sc = crf.decode(hidden, lengths)

@@ -45,7 +45,8 @@ def test_abi_helpers():
 def _problem(**kw):
     from torch_semimarkov_b200 import _lib
 
-    base = dict(batch=0, T=10, K=4, C=3, transition_ndim=2, semiring=0, checkpoint_interval=6)
+    base = dict(batch=0, T=10, K=4, C=3, transition_ndim=2, semiring=0, checkpoint_interval=6,
+                backward_mode=0)
     base.update(kw)
     return _lib.SemicrfProblem(**base)
 
@@ -70,18 +71,31 @@ def test_validation_codes_without_gpu():
     assert lib.semicrf_saved_size(ctypes.byref(_problem(K=0))) == 0
     assert lib.semicrf_backward_workspace_size(ctypes.byref(_problem(batch=2))) > 0
     assert lib.semicrf_score_gold(2, 1, 1, 3, None, None, None, None, None, None, None) == 1
+    p = _problem(backward_mode=5)
+    assert lib.semicrf_forward(ctypes.byref(p), None, None, 0, None, None, 0, None) == 1
 
 
 def test_workspace_sizes_scale():
     from torch_semimarkov_b200 import _lib
 
     lib = _lib.load()
-    small = lib.semicrf_backward_workspace_size(ctypes.byref(_problem(batch=2, T=100)))
-    big = lib.semicrf_backward_workspace_size(ctypes.byref(_problem(batch=4, T=1000)))
+    # recompute mode: the backward workspace holds the recomputed alpha tables
+    small = lib.semicrf_backward_workspace_size(ctypes.byref(_problem(batch=2, T=100,
+                                                                      backward_mode=1)))
+    big = lib.semicrf_backward_workspace_size(ctypes.byref(_problem(batch=4, T=1000,
+                                                                    backward_mode=1)))
     assert big > 10 * small
-    s = lib.semicrf_saved_size(ctypes.byref(_problem(batch=3, T=1000, K=30, C=24,
-                                                    checkpoint_interval=173)))
-    assert s >= 3 * 8
+    # max semiring keeps its float32 tables in the workspace
+    mbig = lib.semicrf_backward_workspace_size(ctypes.byref(_problem(batch=4, T=1000, semiring=1)))
+    assert mbig > 4 * 1001 * 3 * 4 * 4
+    keep = lib.semicrf_saved_size(ctypes.byref(_problem(batch=3, T=1000, K=30, C=24,
+                                                       checkpoint_interval=173)))
+    rec = lib.semicrf_saved_size(ctypes.byref(_problem(batch=3, T=1000, K=30, C=24,
+                                                      checkpoint_interval=173, backward_mode=1)))
+    # keep-alpha holds float64 tables (2*C+1 doubles per position); recompute
+    # holds ~T/S' ring checkpoints of K*C doubles
+    assert keep >= 8 * 3 * 1001 * 49
+    assert rec < keep / 3
 
 
 def test_cpu_tensors_raise_no_fallback():

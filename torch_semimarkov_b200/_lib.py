@@ -26,6 +26,23 @@ SEMICRF_ERR_WORKSPACE = 3
 SEMICRF_ERR_CUDA = 4
 SEMICRF_ERR_SEMIRING = 5
 SEMIRINGS = {"log": 0, "max": 1}
+KEEP_ALPHA, RECOMPUTE = 0, 1
+# Keep float64 alpha tables for the backward (no recompute) while they stay
+# under this many bytes; above it the forward keeps sqrt(T)-spaced ring
+# checkpoints and the backward recomputes alpha between them.  The
+# environment variable TORCH_SEMIMARKOV_B200_BACKWARD=keep|recompute forces
+# one or the other.
+KEEP_ALPHA_MAX_BYTES = 8 << 30
+
+
+def backward_mode_for(B: int, T: int, C: int) -> int:
+    env = os.environ.get("TORCH_SEMIMARKOV_B200_BACKWARD", "").lower()
+    if env == "recompute":
+        return RECOMPUTE
+    if env == "keep":
+        return KEEP_ALPHA
+    table_bytes = 8 * B * (T + 1) * (2 * C + 1)
+    return KEEP_ALPHA if table_bytes <= KEEP_ALPHA_MAX_BYTES else RECOMPUTE
 
 # every symbol include/semicrf.h declares
 EXPORTED_SYMBOLS = (
@@ -62,6 +79,8 @@ class SemicrfProblem(ctypes.Structure):
         ("proj_start", ctypes.c_void_p),
         ("proj_end", ctypes.c_void_p),
         ("checkpoint_interval", ctypes.c_int64),
+        ("backward_mode", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -139,7 +158,8 @@ class Problem:
     """Validated, contiguous inputs of one streaming call plus its C struct."""
 
     def __init__(self, cum_scores, transition, duration_bias, lengths, K, semiring="log",
-                 proj_start=None, proj_end=None, checkpoint_interval_: Optional[int] = None):
+                 proj_start=None, proj_end=None, checkpoint_interval_: Optional[int] = None,
+                 backward_mode: Optional[int] = None):
         if semiring not in SEMIRINGS:
             raise ValueError(f"semiring must be 'log' or 'max', got {semiring!r}")
         if not isinstance(cum_scores, torch.Tensor) or cum_scores.dim() != 3:
@@ -194,6 +214,8 @@ class Problem:
             S = max(int(checkpoint_interval_), K)
         self.S = S
         self.device = dev
+        self.backward_mode = (backward_mode_for(B, T, C) if backward_mode is None
+                              else int(backward_mode))
         self.c = SemicrfProblem(
             batch=B, T=T, K=K, C=C, cum_scores=self.cum.data_ptr(),
             transition=self.tr.data_ptr(), transition_ndim=self.tr.dim(),
@@ -201,7 +223,7 @@ class Problem:
             lengths=self.lengths.data_ptr(),
             proj_start=None if self.ps is None else self.ps.data_ptr(),
             proj_end=None if self.pe is None else self.pe.data_ptr(),
-            checkpoint_interval=S)
+            checkpoint_interval=S, backward_mode=self.backward_mode, reserved=0)
 
     @property
     def cref(self):

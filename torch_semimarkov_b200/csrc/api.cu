@@ -45,8 +45,11 @@ int validate_shape(const semicrf_problem* p) {
   if (p->checkpoint_interval < p->K) return SEMICRF_ERR_INVALID_ARGUMENT;
   if (p->C > 256 || p->T > (int64_t)1 << 30 || p->K > 32767) return SEMICRF_ERR_UNSUPPORTED;
   if (p->transition_ndim == 3) return SEMICRF_ERR_UNSUPPORTED;
-  if (!chain_supported((int)p->C, (int)p->K, p->semiring, p->semiring == SEMICRF_MAX))
+  if (p->backward_mode != SEMICRF_KEEP_ALPHA && p->backward_mode != SEMICRF_RECOMPUTE)
+    return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (p->semiring == SEMICRF_LOG && !lchain_supported((int)p->C, (int)p->K))
     return SEMICRF_ERR_UNSUPPORTED;
+  if (!chain_supported((int)p->C, (int)p->K, SEMICRF_MAX, true)) return SEMICRF_ERR_UNSUPPORTED;
   return SEMICRF_OK;
 }
 
@@ -60,7 +63,7 @@ int validate(const semicrf_problem* p) {
 
 Prepared carve_prep(Carver& cv, int C, int K) {
   Prepared pr{};
-  const int kx = kcap_of(K) + kP + 1;
+  const int kx = kcap_of(K) + kPrepRowsExtra;
   pr.mx_f = cv.take<float>((size_t)C * C);
   pr.mx_b = cv.take<float>((size_t)C * C);
   pr.colmax_f = cv.take<float>(C);
@@ -74,8 +77,12 @@ Prepared carve_prep(Carver& cv, int C, int K) {
 
 struct SavedLayout {
   double* logz;
-  float* sv_f;
+  float* sv_f;     // max semiring: float32 restart records
   double* sv_d;
+  double* sv;      // log semiring, SEMICRF_RECOMPUTE: float64 restart records
+  double* a_tab;   // log semiring, SEMICRF_KEEP_ALPHA: alpha tables
+  double* A_tab;
+  double* n_tab;
 };
 
 SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
@@ -83,8 +90,17 @@ SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
   const size_t B = p->batch, C = p->C;
   const size_t kc = kcap_of(p->K), nint = nint_of(p);
   s.logz = cv.take<double>(B);
-  s.sv_f = cv.take<float>(B * nint * (kc * C + 2 * C));
-  s.sv_d = cv.take<double>(B * nint * kc);
+  if (p->semiring == SEMICRF_MAX) {
+    s.sv_f = cv.take<float>(B * nint * (kc * C + 2 * C));
+    s.sv_d = cv.take<double>(B * nint * kc);
+  } else if (p->backward_mode == SEMICRF_RECOMPUTE) {
+    s.sv = cv.take<double>(B * nint * lchain_saved_doubles((int)p->C, (int)p->K));
+  } else {
+    const size_t n = B * (p->T + 1) * C;
+    s.a_tab = cv.take<double>(n);
+    s.A_tab = cv.take<double>(n);
+    s.n_tab = cv.take<double>(B * (p->T + 1));
+  }
   return s;
 }
 
@@ -113,6 +129,29 @@ struct BwdLayout {
   float *xa, *ma, *xb, *mb, *pstart, *alse, *part_tr, *part_db;
   double *na, *nb;
 };
+
+struct LBwdLayout {
+  Prepared pr;
+  double *a_tab, *A_tab, *n_tab, *part_tr, *part_db, *gws;
+};
+
+LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
+  LBwdLayout w{};
+  w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  if (p->backward_mode == SEMICRF_RECOMPUTE) {
+    const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
+    w.a_tab = cv.take<double>(n);
+    w.A_tab = cv.take<double>(n);
+    w.n_tab = cv.take<double>((size_t)p->batch * (p->T + 1));
+  }
+  w.part_tr = cv.take<double>((size_t)p->batch * p->C * p->C);
+  w.part_db = cv.take<double>((size_t)p->batch * p->K * p->C);
+  size_t g1 = lchain_gws_doubles_per_cta((int)p->C, (int)p->K);
+  const size_t g2 = lchain_ws_gws_doubles_per_cta((int)p->C, (int)p->K);
+  if (g2 > g1) g1 = g2;
+  w.gws = cv.take<double>((size_t)p->batch * g1);
+  return w;
+}
 
 BwdLayout carve_bwd(Carver& cv, const semicrf_problem* p) {
   BwdLayout w{};
@@ -204,6 +243,49 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
   cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
                               kcap_of(p->K), kP, p->semiring, pr, s);
   if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+  if (p->semiring == SEMICRF_LOG) {
+    LChainLaunch L{};
+    L.B = (int)p->batch;
+    L.T = (int)p->T;
+    L.K = (int)p->K;
+    L.C = (int)p->C;
+    L.dbe = pr.dbe;
+    L.dbmax = pr.dbmax;
+    LChainArgs a{};
+    a.mode = 0;
+    a.dir = 0;
+    a.cum = p->cum_scores;
+    a.ps = p->proj_start;
+    a.pe = p->proj_end;
+    a.lengths = p->lengths;
+    a.mx = pr.mx_f;
+    a.colmax = pr.colmax_f;
+    a.partition = partition;
+    a.ref_ckpt = ring_checkpoints;
+    a.nref = (int)num_ring_checkpoints;
+    a.sref = (int)p->checkpoint_interval;
+    a.sint = sint_of(p);
+    a.nint = nint_of(p);
+    if (saved) {
+      Carver sc(saved);
+      SavedLayout sl = carve_saved(sc, p);
+      a.logz = sl.logz;
+      if (p->backward_mode == SEMICRF_RECOMPUTE) {
+        a.sv = sl.sv;
+        a.write_saved = 1;
+      } else {
+        a.a_tab = sl.a_tab;
+        a.A_tab = sl.A_tab;
+        a.n_tab = sl.n_tab;
+      }
+    }
+    L.a0 = a;
+    L.a1 = a;
+    L.n1 = (int)p->batch;
+    if (!a.ref_ckpt && !a.write_saved && lchain_ws_supported((int)p->C, (int)p->K))
+      return cuda_status(launch_lchain_ws(L, s));
+    return cuda_status(launch_lchain(L, (int)p->batch, s));
+  }
   ChainLaunch L = base_launch(p, pr);
   ChainArgs a = base_args(p);
   a.mode = 0;
@@ -233,7 +315,10 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
 size_t semicrf_backward_workspace_size(const semicrf_problem* p) {
   if (validate_shape(p) != SEMICRF_OK) return 0;
   Carver cv(nullptr);
-  carve_bwd(cv, p);
+  if (p->semiring == SEMICRF_LOG)
+    carve_lbwd(cv, p);
+  else
+    carve_bwd(cv, p);
   return cv.bytes();
 }
 
@@ -251,6 +336,82 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
   if (workspace_bytes < semicrf_backward_workspace_size(p) || !workspace)
     return SEMICRF_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->semiring == SEMICRF_LOG) {
+    Carver cv(workspace);
+    LBwdLayout w = carve_lbwd(cv, p);
+    Carver sc(const_cast<void*>(saved));
+    SavedLayout sl = carve_saved(sc, p);
+    cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
+                                kcap_of(p->K), kP, SEMICRF_LOG, w.pr, s);
+    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+    LChainLaunch L{};
+    L.B = (int)p->batch;
+    L.T = (int)p->T;
+    L.K = (int)p->K;
+    L.C = (int)p->C;
+    L.dbe = w.pr.dbe;
+    L.dbmax = w.pr.dbmax;
+    const double* ta = sl.a_tab;
+    const double* tA = sl.A_tab;
+    const double* tn = sl.n_tab;
+    if (p->backward_mode == SEMICRF_RECOMPUTE) {
+      // alpha between checkpoints, all segments of all sequences in parallel
+      LChainArgs r{};
+      r.mode = 1;
+      r.dir = 0;
+      r.cum = p->cum_scores;
+      r.ps = p->proj_start;
+      r.pe = p->proj_end;
+      r.lengths = p->lengths;
+      r.mx = w.pr.mx_f;
+      r.colmax = w.pr.colmax_f;
+      r.sv = sl.sv;
+      r.sint = sint_of(p);
+      r.nint = nint_of(p);
+      r.a_tab = w.a_tab;
+      r.A_tab = w.A_tab;
+      r.n_tab = w.n_tab;
+      L.a0 = r;
+      L.a1 = r;
+      L.n1 = (int)p->batch * r.nint;
+      e = launch_lchain(L, L.n1, s);
+      if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+      ta = w.a_tab;
+      tA = w.A_tab;
+      tn = w.n_tab;
+    }
+    LChainArgs bb{};
+    bb.mode = 0;
+    bb.dir = 1;
+    bb.cum = p->cum_scores;
+    bb.ps = p->proj_start;
+    bb.pe = p->proj_end;
+    bb.lengths = p->lengths;
+    bb.mx = w.pr.mx_b;
+    bb.colmax = w.pr.colmax_b;
+    bb.in_a = ta;
+    bb.in_A = tA;
+    bb.in_n = tn;
+    bb.logz_in = sl.logz;
+    bb.grad_output = grad_output;
+    bb.grad_cum = grad_cum;
+    bb.grad_ps = p->proj_start ? grad_proj_start : nullptr;
+    bb.grad_pe = p->proj_end ? grad_proj_end : nullptr;
+    bb.part_tr = w.part_tr;
+    bb.part_db = w.part_db;
+    bb.gws = w.gws;
+    L.a0 = bb;
+    L.a1 = bb;
+    L.n1 = (int)p->batch;
+    if (lchain_ws_supported((int)p->C, (int)p->K))
+      e = launch_lchain_ws(L, s);
+    else
+      e = launch_lchain(L, (int)p->batch, s);
+    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+    return cuda_status(launch_lreduce((int)p->batch, (int)p->K, (int)p->C, w.part_tr,
+                                      w.part_db, grad_output, p->transition, grad_transition,
+                                      grad_duration_bias, s));
+  }
   Carver cv(workspace);
   BwdLayout w = carve_bwd(cv, p);
   Carver sc(const_cast<void*>(saved));

@@ -65,7 +65,7 @@ __host__ __device__ inline void make_plan(Plan& p, int C, int K, int P, int semi
   p.P = P;
   p.CP = round_cp(C);
   p.R = p.kcap + P;
-  p.kx = p.kcap + P + 1;
+  p.kx = p.kcap + P + 1;  // rows used here; the prepared arrays have kcap + 17
   p.nsplit = kThreads / C > 0 ? kThreads / C : 1;
   p.mx_smem = mx_smem;
   p.db_smem = db_smem;
@@ -172,7 +172,8 @@ __global__ void prep_kernel(const float* __restrict__ tr, const float* __restric
 
 cudaError_t launch_prep(const float* tr, const float* db, int K, int C, int kcap, int P,
                         int semiring, const Prepared& prep, cudaStream_t s) {
-  const int kx = kcap + P + 1;
+  const int kx = kcap + kPrepRowsExtra;
+  (void)P;
   int work = C * C > kx * C ? C * C : kx * C;
   int grid = (work + 255) / 256;
   if (grid > 1024) grid = 1024;

@@ -1,0 +1,728 @@
+// lchain_ws.cu -- warp-specialised float64 log-semiring chain (C <= 64).
+//
+// Same recurrence and linear-domain float64 formulation as lchain.cu (see
+// there for the derivation and the reference citations), reorganised so that
+// the per-position critical path never waits for bulk work:
+//
+//   serial warp(s)  (one lane per label): for block tau of LP targets, the
+//       near sources (blocks tau-1 and tau), the state a, the float64 mat-vec
+//       and the new source E.  About a dozen dependent float64 operations
+//       plus one shared-memory broadcast per position.
+//   bulk warps      (the other 6-7 warps): while the serial warp works on
+//       block tau they prepare block tau+1 -- its normaliser, frame factors,
+//       g/h factors and the far part of every target's k-sum (all sources
+//       before block tau) -- and, in the backward, accumulate the gradients of
+//       block tau-1.
+// Hand-off uses named barriers (FULL[b]: bulk -> serial, DONE[b]: serial ->
+// bulk, double-buffered by block parity).
+//
+// Frames.  Each block beta has a normaliser n_beta and a per-label content
+// anchor cA_beta[c] = cum(u0_beta, c).  Sources of block beta are stored as
+//     E[s,c] = exp(m[s,c] + soff(s,c) - n_beta - csign*(cum(s,c) - cA_beta[c]))
+// and enter the k-sum of a target in block tau with the factor
+//     W[beta->tau,c] = prod_{gamma=beta}^{tau-1} w_gamma[c],
+//     w_gamma[c]    = exp(n_gamma - n_{gamma+1} + csign*(cA_{gamma+1}[c] - cA_gamma[c])).
+// Targets use a[u,c] = g[u,c] * sum_s E[s,c] W Db[u-s,c] with
+//     g[u,c] = exp(toff(u,c) + dbmax[c] + csign*(cum(u,c) - cA_tau[c])),
+// and new sources E[u,c] = ym[u,c] * h[u,c],
+//     h[u,c] = exp(colmax[c] + soff(u,c) - csign*(cum(u,c) - cA_tau[c])).
+// Nothing in the ring is ever rewritten, so the bulk warps can read it while
+// the serial warp appends.  n_tau is predicted two blocks ahead from the
+// measured scale of the state (float64 leaves a very wide margin for the
+// prediction error).
+
+#include "semicrf_internal.cuh"
+
+namespace semicrf {
+
+#ifdef SEMICRF_TIMING
+__device__ unsigned long long g_wstim[256][16];
+#define WT_DECL unsigned long long wt_[16] = {}; unsigned long long wck_ = clock64();
+#define WT_ADD(i) (wt_[i] += clock64() - wck_, wck_ = clock64())
+#define WT_FLUSH(lo)                                                              \
+  if ((tid == 0 || tid == CP) && blockIdx.x < 256)                                  \
+    for (int q_ = 0; q_ < 8; ++q_) g_wstim[blockIdx.x][(lo) + q_] = wt_[(lo) + q_];
+#else
+#define WT_DECL
+#define WT_ADD(i)
+#define WT_FLUSH(lo)
+#endif
+
+namespace {
+
+constexpr int kWsThreads = 256;
+constexpr size_t kWsSmemMax = 227 * 1024;
+
+enum : int { kBarFull0 = 1, kBarFull1 = 2, kBarDone0 = 3, kBarDone1 = 4, kBarBulk = 5,
+             kBarSerial = 6 };
+
+__device__ __forceinline__ void bar_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+struct WsPlan {
+  int C, CP, K, kcap, LP, R, kx, nbr, nbulk, nsplit, nw, nwt;
+  bool db_smem, acc_smem;
+  int o_ring, o_dbe, o_mx, o_dbmax, o_colmax, o_wring, o_lend, o_nring, o_ca, o_far, o_g,
+      o_h, o_wprev, o_sa, o_sy, o_ss, o_part, o_accdb, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_xs;
+  int bytes;
+};
+
+__host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP, bool db_smem,
+                                        bool acc_smem) {
+  p.C = C;
+  p.CP = CP;
+  p.K = K;
+  p.kcap = K > 1 ? K - 1 : 1;
+  p.LP = LP;
+  p.R = p.kcap + 2 * LP;
+  p.kx = p.kcap + kPrepRowsExtra;
+  int nbr = (p.R + LP - 1) / LP + 4;  // blocks whose frame factors are kept (power of 2)
+  p.nbr = 1;
+  while (p.nbr < nbr) p.nbr <<= 1;
+  p.nbulk = kWsThreads - 2 * CP;  // warps sharing a sub-partition with a serial warp idle
+  p.nsplit = p.nbulk / C > 0 ? p.nbulk / C : 1;
+  p.nw = (p.kcap + LP - 1) / LP;
+  p.nwt = p.nbr;
+  p.db_smem = db_smem;
+  p.acc_smem = acc_smem;
+  int o = 0;
+  auto take = [&](int n) {
+    const int r = o;
+    o += (n + 15) & ~15;
+    return r;
+  };
+  p.o_ring = take(8 * p.R * C);
+  p.o_dbe = db_smem ? take(4 * p.kx * C) : -1;
+  p.o_mx = take(4 * C * C);
+  p.o_dbmax = take(8 * CP);
+  p.o_colmax = take(8 * CP);
+  p.o_wring = take(8 * p.nbr * CP);
+  p.o_lend = take(8 * (p.nbr + 2));
+  p.o_nring = take(8 * (p.nbr + 2));
+  p.o_ca = take(8 * 2 * CP);
+  p.o_far = take(8 * 2 * LP * CP);
+  p.o_g = take(8 * 2 * LP * CP);
+  p.o_h = take(8 * 2 * LP * CP);
+  p.o_wprev = take(8 * 2 * CP);
+  p.o_sa = take(8 * 2 * LP * CP);
+  p.o_sy = take(8 * 2 * LP * CP);
+  p.o_ss = take(8 * 2 * LP * CP);
+  p.o_part = take(8 * p.nsplit * LP * C);
+  p.o_accdb = acc_smem ? take(8 * p.kcap * C) : -1;
+  p.o_abuf = take(8 * CP);
+  p.o_wt = take(8 * 2 * p.nwt * CP);  // W tables of the last two prepared blocks
+  p.o_misc = take(8 * 16);
+  p.o_edb = take(8 * CP);
+  p.o_ecm = take(8 * CP);
+  p.o_xs = take(8 * 8 * CP);  // alpha rows of a flushed block (grad_tr)
+  p.bytes = o;
+}
+
+__host__ __device__ inline int ws_cp(int C) { return C <= 32 ? 32 : 64; }
+
+__host__ __device__ inline bool ws_choose(WsPlan& p, int C, int K) {
+  if (C > 64) return false;
+  const int CP = ws_cp(C);
+  ws_make(p, C, K, CP, 8, true, true);
+  if ((size_t)p.bytes <= kWsSmemMax) return true;
+  ws_make(p, C, K, CP, 8, false, true);
+  if ((size_t)p.bytes <= kWsSmemMax) return true;
+  ws_make(p, C, K, CP, 8, false, false);
+  return (size_t)p.bytes <= kWsSmemMax;
+}
+
+}  // namespace
+
+bool lchain_ws_supported(int C, int K) {
+  WsPlan p;
+  return ws_choose(p, C, K);
+}
+
+size_t lchain_ws_gws_doubles_per_cta(int C, int K) {
+  WsPlan p;
+  if (!ws_choose(p, C, K)) return 0;
+  return p.acc_smem ? 0 : (size_t)p.kcap * C;
+}
+
+// ---------------------------------------------------------------------------
+template <int CP, int LP>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    lchain_ws_kernel(const __grid_constant__ LChainLaunch L) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  constexpr int SW = CP / 32;
+  constexpr int NT = kWsThreads;
+  // Warps w and w+4 share a sub-partition.  The serial warps are 0..SW-1;
+  // warps 4..4+SW-1 stay idle so that nothing competes with the critical path.
+  constexpr int NBT = NT - 2 * CP;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool serial = tid < CP;
+  const bool idle = warp >= 4 && warp < 4 + SW;
+  const int btid = (warp < 4) ? tid - CP : tid - 2 * CP;  // bulk thread index
+  constexpr int NPART = NT - CP;  // threads taking part in FULL / DONE (serial + bulk)
+  const LChainArgs& A = L.a0;
+  const int b = blockIdx.x;
+  if (b >= L.B) return;
+  const int C = L.C, K = L.K, T = L.T;
+  const int dir = A.dir;
+  const bool bwd = dir == 1;
+  const double csign = dir == 0 ? 1.0 : -1.0;
+  const long long lraw = A.lengths[b];
+  const int Lb = lraw < 0 ? 0 : (lraw > T ? T : (int)lraw);
+  const int u_begin = 0, u_end = Lb;
+  const int NB = (u_end - u_begin + LP - 1) / LP;  // target blocks
+
+  WsPlan pl;
+  ws_choose(pl, C, K);
+  const int kcap = pl.kcap, R = pl.R, NBR = pl.nbr;
+  double* ring = reinterpret_cast<double*>(smraw + pl.o_ring);
+  float* dbe_s = pl.db_smem ? reinterpret_cast<float*>(smraw + pl.o_dbe) : nullptr;
+  const float* dbe = pl.db_smem ? dbe_s : L.dbe;
+  float* mx = reinterpret_cast<float*>(smraw + pl.o_mx);
+  double* dbmax = reinterpret_cast<double*>(smraw + pl.o_dbmax);
+  double* colmax = reinterpret_cast<double*>(smraw + pl.o_colmax);
+  double* wring = reinterpret_cast<double*>(smraw + pl.o_wring);  // w_gamma, index (gamma+1) mod NBR
+  double* lend = reinterpret_cast<double*>(smraw + pl.o_lend);    // log scale at block end
+  double* nring = reinterpret_cast<double*>(smraw + pl.o_nring);  // n_gamma
+  double* cA = reinterpret_cast<double*>(smraw + pl.o_ca);        // [2][CP] anchors (bulk)
+  double* farb = reinterpret_cast<double*>(smraw + pl.o_far);     // [2][LP][CP]
+  double* gb = reinterpret_cast<double*>(smraw + pl.o_g);
+  double* hb = reinterpret_cast<double*>(smraw + pl.o_h);
+  double* wprev = reinterpret_cast<double*>(smraw + pl.o_wprev);  // [2][CP]
+  double* sab = reinterpret_cast<double*>(smraw + pl.o_sa);
+  double* syb = reinterpret_cast<double*>(smraw + pl.o_sy);
+  double* ssb = reinterpret_cast<double*>(smraw + pl.o_ss);
+  double* part = reinterpret_cast<double*>(smraw + pl.o_part);
+  double* abuf = reinterpret_cast<double*>(smraw + pl.o_abuf);
+  // wt[(tau&1)][q][c] = W[(tau-q) -> tau, c]  (q = 0 .. nwt-1, 0 beyond the start)
+  double* wt = reinterpret_cast<double*>(smraw + pl.o_wt);
+  const int NWT = pl.nwt;
+  double* misc = reinterpret_cast<double*>(smraw + pl.o_misc);
+  double* edb = reinterpret_cast<double*>(smraw + pl.o_edb);  // exp(dbmax)
+  double* ecm = reinterpret_cast<double*>(smraw + pl.o_ecm);  // exp(colmax)
+  double* xs = reinterpret_cast<double*>(smraw + pl.o_xs);    // [LP][CP]
+  double* accdb = pl.acc_smem ? reinterpret_cast<double*>(smraw + pl.o_accdb)
+                              : A.gws + (size_t)b * ((size_t)kcap * C);
+  auto lidx = [&](int gamma) { return (gamma + NBR) & (NBR - 1); };  // gamma >= -NBR
+
+  const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
+  const float* ps_b = A.ps ? A.ps + (size_t)b * T * C : nullptr;
+  const float* pe_b = A.pe ? A.pe + (size_t)b * T * C : nullptr;
+  auto cpos = [&](int u) { return dir == 0 ? u : Lb - u; };
+  auto soff_at = [&](int u, int c) -> double {
+    const int t = cpos(u);
+    if (dir == 0) return (ps_b && t < T) ? (double)ps_b[(size_t)t * C + c] : 0.0;
+    return (pe_b && t >= 1) ? (double)pe_b[(size_t)(t - 1) * C + c] : 0.0;
+  };
+  auto toff_at = [&](int u, int c) -> double {
+    const int t = cpos(u);
+    if (dir == 0) return (pe_b && t >= 1) ? (double)pe_b[(size_t)(t - 1) * C + c] : 0.0;
+    return (ps_b && t < T) ? (double)ps_b[(size_t)t * C + c] : 0.0;
+  };
+  auto cumd = [&](int u, int c) -> double { return (double)cum_b[(size_t)cpos(u) * C + c]; };
+
+  // ---- constants ----------------------------------------------------------
+  for (int i = tid; i < CP; i += NT) {
+    dbmax[i] = i < C ? (double)L.dbmax[i] : 0.0;
+    colmax[i] = i < C ? (double)A.colmax[i] : 0.0;
+    edb[i] = i < C ? exp((double)L.dbmax[i]) : 0.0;
+    ecm[i] = i < C ? exp((double)A.colmax[i]) : 0.0;
+  }
+  for (int i = tid; i < C * C; i += NT) mx[i] = A.mx[i];
+  if (dbe_s)
+    for (int i = tid; i < pl.kx * C; i += NT) dbe_s[i] = L.dbe[i];
+  if (bwd)
+    for (int i = tid; i < kcap * C; i += NT) accdb[i] = 0.0;
+  for (int i = tid; i < R * C; i += NT) ring[i] = 0.0;
+  __syncthreads();
+
+  const int c = tid;  // serial lane label
+  const bool cv = serial && c < C;
+  double* atab_b = A.a_tab ? A.a_tab + (size_t)b * (T + 1) * C : nullptr;
+  double* Atab_b = A.A_tab ? A.A_tab + (size_t)b * (T + 1) * C : nullptr;
+  double* ntab_b = A.n_tab ? A.n_tab + (size_t)b * (T + 1) : nullptr;
+  const double* xa_b = bwd ? A.in_a + (size_t)b * (T + 1) * C : nullptr;
+  const double* ya_b = bwd ? A.in_A + (size_t)b * (T + 1) * C : nullptr;
+  const double* na_b = bwd ? A.in_n + (size_t)b * (T + 1) : nullptr;
+  const double logz = bwd ? A.logz_in[b] : 0.0;
+  const double gout = bwd ? (double)A.grad_output[b] : 0.0;
+  float* gcum_b = bwd ? A.grad_cum + (size_t)b * (T + 1) * C : nullptr;
+  float* gps_b = (bwd && A.grad_ps) ? A.grad_ps + (size_t)b * T * C : nullptr;
+  float* gpe_b = (bwd && A.grad_pe) ? A.grad_pe + (size_t)b * T * C : nullptr;
+  double* ptr_b = bwd ? A.part_tr + (size_t)b * C * C : nullptr;
+
+  // ---- initial state (position u_begin = 0, "block -1") -----------------
+  // frame of block -1: n = 0, anchor cA_{-1} = cum(0)
+  double a0 = 0.0;
+  if (serial) {
+    double ym0;
+    if (dir == 0) {
+      a0 = cv ? 1.0 : 0.0;
+      // ym0 = sum_c' Mx[c',c] (alpha[0] = 0 for every label)
+      double y = 0.0;
+      if (cv)
+        for (int q = 0; q < C; ++q) y += (double)mx[q * C + c];
+      ym0 = y;
+    } else {
+      ym0 = cv ? exp(-colmax[c]) : 0.0;  // beta[Lb] = 0
+    }
+    if (cv) {
+      const double e0 = ym0 * exp(colmax[c] + soff_at(0, c));
+      ring[0 * C + c] = e0;  // slot of position 0
+      const int t0 = cpos(0);
+      if (atab_b && dir == 0) atab_b[(size_t)t0 * C + c] = a0;
+      if (Atab_b && dir == 0) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
+      cA[1 * CP + c] = cumd(0, c);  // anchor of block -1 (parity of -1 is 1)
+    }
+    if (tid == 0) {
+      if (ntab_b && dir == 0) ntab_b[cpos(0)] = 0.0;
+      nring[lidx(-1)] = 0.0;
+      lend[lidx(-1)] = 0.0;  // log(max a[0]) = 0 forward; the backward starts from beta
+    }
+  }
+  // backward: position t = Lb (u = 0) and rows beyond Lb
+  if (bwd) {
+    const double f = exp(na_b[Lb] - logz);
+    for (int i = tid; i < (T + 1 - Lb) * C; i += NT) {
+      const int t = Lb + i / C, cc = i % C;
+      float pend = 0.f;
+      if (t == Lb && Lb >= 1) pend = (float)(gout * xa_b[(size_t)Lb * C + cc] * f);
+      gcum_b[(size_t)t * C + cc] = pend;
+      if (gps_b && t < T) gps_b[(size_t)t * C + cc] = 0.f;
+      if (gpe_b && t >= 1) gpe_b[(size_t)(t - 1) * C + cc] = (t == Lb) ? pend : 0.f;
+    }
+    for (int i = tid; i < C * C; i += NT) ptr_b[i] = 0.0;
+  }
+  __syncthreads();
+
+  WT_DECL
+  if (idle) {
+    // co-resident with a serial warp: stay out of its way
+  } else if (!serial) {
+    // =====================================================================
+    // bulk warps
+    // =====================================================================
+    // prepare(tau): frame, factors and far sums of block tau into buffer tau&1
+    auto prepare = [&](int tau) {
+      const int bf = tau & 1;
+      const int u0 = u_begin + 1 + tau * LP;
+      const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
+      // normaliser prediction from the scales measured two blocks back
+      if (btid == 0) {
+        double n;
+        if (tau < 2) {
+          n = lend[lidx(-1)];
+        } else {
+          const double l2 = lend[lidx(tau - 2)];
+          const double l3 = lend[lidx(tau - 3)];
+          double gr = l2 - l3;
+          gr = fmin(fmax(gr, -150.0), 150.0);
+          n = l2 + 2.0 * gr;
+        }
+        nring[lidx(tau)] = n;
+      }
+      // anchors of this block
+      for (int i = btid; i < C; i += NBT) cA[bf * CP + i] = cumd(u0, i);
+      bar_sync(kBarBulk, NBT);
+      const double n_tau = nring[lidx(tau)];
+      const double n_prev = nring[lidx(tau - 1)];
+      // w_{tau-1}: frame tau-1 -> tau, and this block's W table
+      for (int i = btid; i < C; i += NBT) {
+        const double w = exp(fmin(fmax(n_prev - n_tau + csign * (cA[bf * CP + i] - cA[(bf ^ 1) * CP + i]),
+                                       -700.0), 700.0));
+        wring[lidx(tau - 1) * CP + i] = w;
+        wprev[bf * CP + i] = w;
+      }
+      bar_sync(kBarBulk, NBT);
+      {
+        double* wcur = wt + (size_t)bf * NWT * CP;
+        const double* wold = wt + (size_t)(bf ^ 1) * NWT * CP;
+        for (int w = btid; w < NWT * C; w += NBT) {
+          const int q = w / C, cc = w % C;
+          double v;
+          if (q == 0) {
+            v = 1.0;
+          } else if (tau == 0) {
+            v = (q == 1) ? wring[lidx(-1) * CP + cc] : 0.0;  // only block -1 exists
+          } else {
+            v = wold[(q - 1) * CP + cc] * wring[lidx(tau - 1) * CP + cc];
+          }
+          wcur[q * CP + cc] = v;
+        }
+      }
+      // g / h of the targets: g = exp(toff + dbmax + d), h = exp(colmax + soff - d)
+      const bool noproj = ps_b == nullptr && pe_b == nullptr;
+      for (int w = btid; w < nP * C; w += NBT) {
+        const int i = w / C, cc = w % C;
+        const int u = u0 + i;
+        const double d = csign * (cumd(u, cc) - cA[bf * CP + cc]);
+        if (noproj) {
+          const double e = exp(fmin(fmax(d, -650.0), 650.0));
+          gb[(bf * LP + i) * CP + cc] = edb[cc] * e;
+          hb[(bf * LP + i) * CP + cc] = ecm[cc] / e;
+        } else {
+          gb[(bf * LP + i) * CP + cc] = exp(fmin(toff_at(u, cc) + dbmax[cc] + d, 700.0));
+          hb[(bf * LP + i) * CP + cc] = exp(fmin(colmax[cc] + soff_at(u, cc) - d, 700.0));
+        }
+      }
+      bar_sync(kBarBulk, NBT);
+      WT_ADD(2);
+      // far sums over sources s in [s_lo, s_hi], s_hi = u0-LP-1 (end of block tau-2).
+      // Chunks are whole source blocks, so the frame factor is one lookup per block.
+      const int s_hi = u0 - LP - 1;
+      const int s_lo = (u0 - kcap) > 0 ? (u0 - kcap) : 0;
+      const int ns = s_hi - s_lo + 1;
+      const int nsplit = pl.nsplit;
+      const double* wcur = wt + (size_t)bf * NWT * CP;
+      if (ns > 0) {
+        const int nblk_src = (ns + LP - 1) / LP + 1;  // source blocks touched (upper bound)
+        const int bpc = (nblk_src + nsplit - 1) / nsplit;  // source blocks per chunk
+        for (int w = btid; w < C * nsplit; w += NBT) {
+          const int cc = w % C, j = w / C;
+          double acc[LP];
+#pragma unroll
+          for (int i = 0; i < LP; ++i) acc[i] = 0.0;
+          // source blocks q = 2 + j*bpc .. 2 + (j+1)*bpc - 1 back from tau (q=2 ends at s_hi)
+          const int q0 = 2 + j * bpc;
+          int s_top = s_hi - (q0 - 2) * LP;
+          if (s_top >= s_lo) {
+            double win[LP];
+#pragma unroll
+            for (int i = 0; i < LP; ++i) win[i] = (double)dbe[(u0 - s_top + i) * C + cc];
+            int slot = s_top % R;
+            for (int q = q0; q < q0 + bpc && s_top - (q - q0) * LP >= s_lo; ++q) {
+              const double W = (q < NWT) ? wcur[q * CP + cc] : 0.0;
+              const int sb = s_top - (q - q0) * LP;  // newest source of this block
+#pragma unroll
+              for (int r = 0; r < LP; ++r) {
+                const int s = sb - r;
+                const double x = (s >= s_lo) ? ring[slot * C + cc] * W : 0.0;
+#pragma unroll
+                for (int i = 0; i < LP; ++i) acc[i] = fma(x, win[(r + i) % LP], acc[i]);
+                int kn = u0 - s + LP;
+                if (kn > pl.kx - 1) kn = pl.kx - 1;
+                win[r % LP] = (double)dbe[kn * C + cc];
+                slot = (slot == 0) ? R - 1 : slot - 1;
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < LP; ++i) part[(j * LP + i) * C + cc] = acc[i];
+        }
+        bar_sync(kBarBulk, NBT);
+        WT_ADD(3);
+        for (int w = btid; w < LP * C; w += NBT) {
+          const int i = w / C, cc = w % C;
+          double s = 0.0;
+          for (int j = 0; j < nsplit; ++j) s += part[(j * LP + i) * C + cc];
+          farb[(bf * LP + i) * CP + cc] = s;
+        }
+      } else {
+        for (int w = btid; w < LP * C; w += NBT) {
+          const int i = w / C, cc = w % C;
+          farb[(bf * LP + i) * CP + cc] = 0.0;
+        }
+      }
+      __threadfence_block();
+      WT_ADD(4);
+    };
+
+    // gradients of block tau (backward)
+    auto flush = [&](int tau) {
+      const int bf = tau & 1;
+      const int u0 = u_begin + 1 + tau * LP;
+      const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
+      const double n_tau = nring[lidx(tau)];
+      const double* wcur = wt + (size_t)bf * NWT * CP;  // W[(tau-q) -> tau]
+      for (int w = btid; w < nP * C; w += NBT) {
+        const int i = w / C, cc = w % C;
+        const int u = u0 + i, t = Lb - u;
+        const double f = exp(na_b[t] + n_tau - logz);
+        const double sa = sab[(bf * LP + i) * CP + cc];
+        const double pst = ya_b[(size_t)t * C + cc] * sa * f;
+        const double pend = (t >= 1) ? xa_b[(size_t)t * C + cc] * syb[(bf * LP + i) * CP + cc] * f
+                                     : 0.0;
+        gcum_b[(size_t)t * C + cc] = (float)(gout * (pend - pst));
+        if (gps_b) gps_b[(size_t)t * C + cc] = (float)(gout * pst);
+        if (gpe_b && t >= 1) gpe_b[(size_t)(t - 1) * C + cc] = (float)(gout * pend);
+        const double S = ssb[(bf * LP + i) * CP + cc];
+        ssb[(bf * LP + i) * CP + cc] = (S > 0.0) ? pst / S : 0.0;  // omega
+        sab[(bf * LP + i) * CP + cc] = sa * f;
+      }
+      for (int w = btid; w < nP * C; w += NBT) {
+        const int i = w / C, cc = w % C;
+        xs[i * CP + cc] = xa_b[(size_t)(Lb - (u0 + i)) * C + cc];
+      }
+      bar_sync(kBarBulk, NBT);
+      // transition: part_tr[c',c] += sum_i a_alpha[t_i,c'] * (a_beta f)[i,c]
+      for (int p = btid; p < C * C; p += NBT) {
+        const int cs = p / C, cd = p % C;
+        double acc = 0.0;
+        for (int i = 0; i < nP; ++i) acc = fma(xs[i * CP + cs], sab[(bf * LP + i) * CP + cd], acc);
+        ptr_b[p] += acc;
+      }
+      // duration bias: accdb[k,c] += Db[k,c] * sum_i omega[i,c] * E[u_i - k, c] W.
+      // Item = (label, k-range [k_lo, k_lo+LP)); for target i the sources are
+      // u0+i-k_lo-q (q < LP): a window that slides up by one per target.
+      for (int w = btid; w < pl.nw * C; w += NBT) {
+        const int cc = w % C, r = w / C;
+        const int k_lo = 1 + r * LP;
+        double acc[LP], win[LP];
+        const int s0 = u0 - k_lo;  // source of lag 0 for target 0
+        int slot0 = s0 >= 0 ? s0 % R : 0;
+        {
+          int sl = slot0;
+#pragma unroll
+          for (int q = 0; q < LP; ++q) {
+            acc[q] = 0.0;
+            // window for target 0: sources u0 - k_lo - q
+            const int s = s0 - q;
+            double v = 0.0;
+            if (s >= 0 && k_lo + q <= kcap) {
+              const int beta = (s - u_begin - 1) >= 0 ? (s - u_begin - 1) / LP : -1;
+              v = ring[sl * C + cc] * wcur[(tau - beta) * CP + cc];
+            }
+            win[q] = v;
+            sl = (sl == 0) ? R - 1 : sl - 1;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < LP; ++i) {
+          if (i < nP) {
+            const double om = ssb[(bf * LP + i) * CP + cc];
+#pragma unroll
+            for (int q = 0; q < LP; ++q) acc[q] = fma(om, win[(q + LP - i) % LP], acc[q]);
+            // slide: add source u0 + i + 1 - k_lo (lag q = 0 for target i+1)
+            const int s = s0 + i + 1;
+            slot0 = (slot0 + 1 == R) ? 0 : slot0 + 1;
+            double v = 0.0;
+            if (s >= 0 && i + 1 < nP) {
+              const int beta = (s - u_begin - 1) >= 0 ? (s - u_begin - 1) / LP : -1;
+              v = ring[slot0 * C + cc] * wcur[(tau - beta) * CP + cc];
+            }
+            win[(LP - 1 - i) % LP] = v;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < LP; ++q) {
+          const int k = k_lo + q;
+          if (k <= kcap) accdb[(k - 1) * C + cc] += acc[q] * (double)dbe[k * C + cc];
+        }
+      }
+      bar_sync(kBarBulk, NBT);
+    };
+
+    if (NB > 0) {
+      prepare(0);
+      bar_arrive(kBarFull0, NPART);
+    }
+    if (NB > 1) {
+      prepare(1);
+      bar_arrive(kBarFull1, NPART);
+    }
+    for (int tau = 2; tau < NB + 2; ++tau) {
+      WT_ADD(5);
+      bar_sync(((tau - 2) & 1) ? kBarDone1 : kBarDone0, NPART);
+      WT_ADD(0);
+      if (bwd) flush(tau - 2);
+      WT_ADD(1);
+      if (tau < NB) {
+        prepare(tau);
+        bar_arrive((tau & 1) ? kBarFull1 : kBarFull0, NPART);
+      }
+    }
+    WT_FLUSH(0);
+  } else {
+    // =====================================================================
+    // serial warp(s)
+    // =====================================================================
+    double mxr[CP == 32 ? 32 : 1];
+#pragma unroll
+    for (int q = 0; q < (CP == 32 ? 32 : 1); ++q)
+      mxr[q] = (CP == 32 && cv && q < C) ? (double)mx[q * C + c] : 0.0;
+    const double ecol = cv ? exp(colmax[c]) : 0.0;
+    double dbk[2 * LP];  // Db[k] for k = 0 .. 2LP-1 (index 0 unused)
+#pragma unroll
+    for (int k = 0; k < 2 * LP; ++k) dbk[k] = (cv && k >= 1) ? (double)dbe[k * C + c] : 0.0;
+    auto sync_serial = [&]() {
+      if (SW == 1)
+        __syncwarp();
+      else
+        bar_sync(kBarSerial, CP);
+    };
+    auto matvec = [&](double a) -> double {
+      abuf[c] = cv ? a : 0.0;
+      sync_serial();
+      double y[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) y[q] = 0.0;
+      if (CP == 32) {
+        const double2* ab2 = reinterpret_cast<const double2*>(abuf);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const double2 v = ab2[q];
+          y[(2 * q) & 7] = fma(v.x, mxr[2 * q], y[(2 * q) & 7]);
+          y[(2 * q + 1) & 7] = fma(v.y, mxr[2 * q + 1], y[(2 * q + 1) & 7]);
+        }
+      } else if (cv) {
+        const double2* ab2 = reinterpret_cast<const double2*>(abuf);
+#pragma unroll 4
+        for (int q = 0; q < CP / 2; ++q) {
+          const double2 v = ab2[q];
+          const int q0 = 2 * q, q1 = 2 * q + 1;
+          y[q0 & 7] = fma(v.x, q0 < C ? (double)mx[q0 * C + c] : 0.0, y[q0 & 7]);
+          y[q1 & 7] = fma(v.y, q1 < C ? (double)mx[q1 * C + c] : 0.0, y[q1 & 7]);
+        }
+      }
+      sync_serial();
+      return ((y[0] + y[1]) + (y[2] + y[3])) + ((y[4] + y[5]) + (y[6] + y[7]));
+    };
+    auto group_maxd = [&](double v) -> double {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (SW == 1) return v;
+      if (lane == 0) misc[8 + warp] = v;
+      bar_sync(kBarSerial, CP);
+      double r = fmax(misc[8], misc[9]);
+      bar_sync(kBarSerial, CP);
+      return r;
+    };
+    auto group_sumd = [&](double v) -> double {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (SW == 1) return v;
+      if (lane == 0) misc[8 + warp] = v;
+      bar_sync(kBarSerial, CP);
+      double r = misc[8] + misc[9];
+      bar_sync(kBarSerial, CP);
+      return r;
+    };
+
+    // near window: sources of the previous block (index j <-> u0 - LP + j)
+    double ep[LP];
+#pragma unroll
+    for (int j = 0; j < LP; ++j) ep[j] = 0.0;
+    ep[LP - 1] = cv ? ring[0 * C + c] : 0.0;  // position 0
+    double a_last = a0;
+    double n_last = 0.0;
+    for (int tau = 0; tau < NB; ++tau) {
+      const int bf = tau & 1;
+      WT_ADD(12);
+      bar_sync(bf ? kBarFull1 : kBarFull0, NPART);
+      WT_ADD(8);
+      const int u0 = u_begin + 1 + tau * LP;
+      const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
+      const double n_tau = nring[lidx(tau)];
+      const double wp = cv ? wprev[bf * CP + c] : 0.0;
+#pragma unroll
+      for (int j = 0; j < LP; ++j) ep[j] *= wp;
+      double ec[LP];
+#pragma unroll
+      for (int i = 0; i < LP; ++i) ec[i] = 0.0;
+      int slot = u0 % R;
+#pragma unroll
+      for (int i = 0; i < LP; ++i) {
+        if (i < nP) {
+          const int u = u0 + i;
+          double S = 0.0, a = 0.0;
+          if (cv) {
+            double pp[4] = {farb[(bf * LP + i) * CP + c], 0.0, 0.0, 0.0};
+#pragma unroll
+            for (int j = 0; j < LP; ++j) pp[j & 3] = fma(ep[j], dbk[LP + i - j], pp[j & 3]);
+#pragma unroll
+            for (int j = 0; j + 1 < i; ++j) pp[(j + 1) & 3] = fma(ec[j], dbk[i - j], pp[(j + 1) & 3]);
+            const double part0 = (pp[0] + pp[1]) + (pp[2] + pp[3]);
+            S = (i >= 1) ? fma(ec[i - 1], dbk[1], part0) : part0;
+            a = (S > 0.0) ? gb[(bf * LP + i) * CP + c] * S : 0.0;
+          }
+          WT_ADD(9);
+          const double ym = matvec(a);
+          WT_ADD(10);
+          if (cv) {
+            const double e = (ym > 0.0) ? ym * hb[(bf * LP + i) * CP + c] : 0.0;
+            ec[i] = e;
+            ring[slot * C + c] = e;
+            const int t = cpos(u);
+            if (atab_b) atab_b[(size_t)t * C + c] = a;
+            if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
+            if (bwd) {
+              sab[(bf * LP + i) * CP + c] = a;
+              syb[(bf * LP + i) * CP + c] = ym * ecol;
+              ssb[(bf * LP + i) * CP + c] = S;
+            }
+          }
+          if (tid == 0 && ntab_b) ntab_b[cpos(u)] = n_tau;
+          a_last = a;
+          slot = (slot + 1 == R) ? 0 : slot + 1;
+          WT_ADD(11);
+        }
+      }
+      // scale at the end of the block, for the bulk's normaliser prediction
+      const double m = group_maxd(cv ? a_last : 0.0);
+      if (tid == 0) lend[lidx(tau)] = n_tau + (m > 0.0 ? log(m) : 0.0);
+      n_last = n_tau;
+      // the near window of the next block is this block (padded with zeros)
+#pragma unroll
+      for (int j = 0; j < LP; ++j) ep[j] = ec[j];
+      if (nP < LP) {
+        // only the last block can be short; no next block reads ep
+      }
+      __threadfence_block();
+      bar_arrive(bf ? kBarDone1 : kBarDone0, NPART);
+    }
+    WT_FLUSH(8);
+    // forward output: logZ = n(Lb) + log sum_c a[Lb,c]
+    if (dir == 0) {
+      const double s = group_sumd(cv ? a_last : 0.0);
+      if (tid == 0) {
+        const double lz = (Lb == 0 || !(s > 0.0)) ? (double)kRefNegInf : n_last + log(s);
+        if (A.partition) A.partition[b] = (float)lz;
+        if (A.logz) A.logz[b] = lz;
+      }
+    }
+  }
+  __syncthreads();
+  if (bwd) {
+    for (int i = tid; i < K * C; i += NT) {
+      const int k = i / C, cc = i % C;
+      double v = 0.0;
+      if (K == 1) {
+        v = (k == 0) ? accdb[cc] : 0.0;
+      } else if (k >= 1) {
+        v = accdb[(k - 1) * C + cc];
+      }
+      A.part_db[(size_t)b * K * C + i] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int CP>
+static cudaError_t launch_ws_cp(const LChainLaunch& L, size_t smem, cudaStream_t s) {
+  auto kern = lchain_ws_kernel<CP, 8>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kern<<<L.B, kWsThreads, smem, s>>>(L);
+  return cudaGetLastError();
+}
+
+// one CTA per sequence; L.a0 is the (mode 0) role
+#ifdef SEMICRF_TIMING
+extern "C" int semicrf_debug_wstiming(unsigned long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, g_wstim, sizeof(g_wstim));
+}
+#endif
+
+cudaError_t launch_lchain_ws(const LChainLaunch& L, cudaStream_t s) {
+  if (L.B <= 0) return cudaSuccess;
+  WsPlan p;
+  if (!ws_choose(p, L.C, L.K)) return cudaErrorInvalidValue;
+  if (ws_cp(L.C) == 32) return launch_ws_cp<32>(L, (size_t)p.bytes, s);
+  return launch_ws_cp<64>(L, (size_t)p.bytes, s);
+}
+
+}  // namespace semicrf

@@ -104,6 +104,67 @@ struct ChainLaunch {
   ChainArgs a1;
 };
 
+// float64 linear-domain log-semiring chain (lchain.cu)
+struct LChainArgs {
+  int mode;  // 0 = whole sequence, 1 = checkpoint segment (forward only)
+  int dir;   // 0 = forward (alpha), 1 = backward (beta + fused gradients)
+  const float* cum;
+  const float* ps;
+  const float* pe;
+  const int64_t* lengths;
+  const float* mx;       // exp(M - colmax), float32 (C*C)
+  const float* colmax;   // (C)
+  // forward outputs
+  float* partition;
+  double* logz;
+  float* ref_ckpt;
+  int nref;
+  int sref;
+  // restart states (checkpoint mode)
+  double* sv;
+  int nint;
+  int sint;
+  int write_saved;
+  // alpha tables written by the forward / the recompute: a = exp(alpha - n),
+  // A = exp(A - n), n per position, indexed by cum position t
+  double* a_tab;
+  double* A_tab;
+  double* n_tab;
+  // backward inputs
+  const double* in_a;
+  const double* in_A;
+  const double* in_n;
+  const double* logz_in;
+  const float* grad_output;
+  // backward outputs
+  float* grad_cum;
+  float* grad_ps;
+  float* grad_pe;
+  double* part_tr;  // (B, C*C) per-sequence, without exp(tr) and grad_output
+  double* part_db;  // (B, K*C) per-sequence, without grad_output
+  double* gws;      // per-CTA global scratch (lchain_gws_doubles_per_cta each)
+};
+struct LChainLaunch {
+  int B, T, K, C;
+  const float* dbe;    // (kx, C) exp(db - dbmax), zero outside durations 1..kcap
+  const float* dbmax;  // (C)
+  int n1;              // CTAs [0, n1) run a0, the rest a1
+  LChainArgs a0;
+  LChainArgs a1;
+};
+cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s);
+// warp-specialised variant for C <= 64, whole-sequence chains (mode 0) only
+cudaError_t launch_lchain_ws(const LChainLaunch& L, cudaStream_t s);
+bool lchain_ws_supported(int C, int K);
+size_t lchain_ws_gws_doubles_per_cta(int C, int K);
+bool lchain_supported(int C, int K);
+size_t lchain_saved_doubles(int C, int K);       // restart record per checkpoint
+size_t lchain_gws_doubles_per_cta(int C, int K);
+cudaError_t launch_lreduce(int B, int K, int C, const double* part_tr, const double* part_db,
+                           const float* grad_output, const float* tr, float* grad_tr,
+                           float* grad_db, cudaStream_t s);
+constexpr int kPrepRowsExtra = 17;  // dbl/dbe rows = kcap + kPrepRowsExtra
+
 // launchers (chain.cu)
 cudaError_t launch_prep(const float* tr, const float* db, int K, int C, int kcap, int P,
                         int semiring, const Prepared& prep, cudaStream_t s);
