@@ -136,6 +136,25 @@ int semicrf_score_gold_backward(int64_t B, int64_t T, int64_t K, int64_t C,
                                 size_t workspace_bytes, void* stream);
 size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_t C);
 
+/* Partition-only forward scan that allocates nothing and takes no workspace.
+ * It has no counterpart in the reference: it is for hosts that cannot supply
+ * a device buffer (a JNI/cgo/N-API runtime with no device allocator, which
+ * must not call cudaMalloc on its request path).  Results equal
+ * semicrf_forward's partition for the same problem.
+ *  - Scratch: a fixed 1 MiB device array inside the library, one per
+ *    device; every accepted shape fits (the largest, C=256 with K=64,
+ *    needs 675 KiB).  A problem whose semicrf_forward_workspace_size
+ *    exceeds 1 MiB is rejected with SEMICRF_ERR_WORKSPACE (before any CUDA
+ *    call).
+ *  - Nothing in the scratch needs to start at zero (each call writes what it
+ *    reads, in stream order).
+ *  - Calls on one device share that scratch: overlapping calls (different
+ *    streams, unordered) race; the caller must order them.
+ *  - The first call on a device resolves the scratch address
+ *    (cudaGetSymbolAddress) with that device current; make it before
+ *    capturing any stream on that device. */
+int semicrf_forward_noalloc(const semicrf_problem* p, float* partition, void* stream);
+
 const char* semicrf_strerror(int status);
 int semicrf_abi_version(void);
 

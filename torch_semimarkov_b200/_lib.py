@@ -59,6 +59,7 @@ EXPORTED_SYMBOLS = (
     "semicrf_score_gold_workspace_size",
     "semicrf_strerror",
     "semicrf_abi_version",
+    "semicrf_forward_noalloc",
 )
 
 
@@ -122,6 +123,8 @@ def load():
     lib.semicrf_strerror.restype = ctypes.c_char_p
     lib.semicrf_strerror.argtypes = [ci]
     lib.semicrf_abi_version.restype = ci
+    lib.semicrf_forward_noalloc.restype = ci
+    lib.semicrf_forward_noalloc.argtypes = [P, vp, vp]
     _lib = lib
     return lib
 

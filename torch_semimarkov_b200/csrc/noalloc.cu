@@ -1,0 +1,78 @@
+// noalloc.cu -- semicrf_forward_noalloc: the partition-only forward scan with
+// its scratch space in a fixed file-scope device array instead of a
+// caller-supplied workspace.
+//
+// Who needs it: hosts that cannot hand the library a device buffer.  A
+// foreign-language runtime (JNI, cgo, N-API) that binds the C ABI usually has
+// no device allocator of its own, and calling cudaMalloc/cudaFree from its
+// request path would both synchronise the device and compete with whatever
+// caching allocator already owns the GPU's memory.  Such a caller can still
+// run inference (the log-partition or the Viterbi score) with this entry
+// point: it allocates nothing at run time.
+//
+// Limits and rules:
+//  - The scratch holds the forward's prepared constants (the exponentiated
+//    transition and duration tables, about 8*C*C + 8*(K+16)*C bytes).  It is
+//    kNoallocScratchBytes (1 MiB) large.  Every shape the scan accepts fits
+//    (the largest, C=256 with K=64, needs 675 KiB); a problem whose forward
+//    workspace (semicrf_forward_workspace_size) exceeds 1 MiB is rejected with
+//    SEMICRF_ERR_WORKSPACE before any CUDA call.
+//  - Nothing in the scratch has to start at zero: every byte the scan reads
+//    is first written by the preparation kernel of the same call, earlier on
+//    the same stream.
+//  - There is one scratch per device, shared by every call on that device.
+//    Calls that can overlap in time (different streams, or different host
+//    threads without ordering between their streams) race on it; the caller
+//    must order them.
+//  - The first call on a device (with that device current) resolves the
+//    scratch's device address once with cudaGetSymbolAddress, which may load
+//    this library's device code into the context.  Make that first call
+//    before capturing any stream on that device.
+
+#include <mutex>
+
+#include "semicrf_internal.cuh"
+
+namespace {
+
+constexpr size_t kNoallocScratchBytes = size_t(1) << 20;
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of this device's scratch; resolved once per device.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return SEMICRF_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr)
+      return SEMICRF_ERR_CUDA;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SEMICRF_OK;
+}
+
+}  // namespace
+
+extern "C" int semicrf_forward_noalloc(const semicrf_problem* p, float* partition,
+                                       void* stream) {
+  if (!p) return SEMICRF_ERR_INVALID_ARGUMENT;
+  // semicrf_forward checks every argument before it touches the device.  Given
+  // no workspace it returns SEMICRF_OK for an empty batch, its validation
+  // error for a bad problem, and otherwise stops at the workspace check.
+  const int pre = semicrf_forward(p, partition, nullptr, 0, nullptr, nullptr, 0, stream);
+  if (pre != SEMICRF_ERR_WORKSPACE) return pre;
+  if (semicrf_forward_workspace_size(p) > kNoallocScratchBytes) return SEMICRF_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != SEMICRF_OK) return st;
+  return semicrf_forward(p, partition, nullptr, 0, nullptr, scratch, kNoallocScratchBytes,
+                         stream);
+}
