@@ -46,6 +46,10 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-viterbi", action="store_true")
+    # smaller per-rank batches / sequences, e.g. for profiler captures of one
+    # kernel; the benchmark line is only the configuration-2 number at the defaults
+    ap.add_argument("--batch", type=int, default=B)
+    ap.add_argument("--seq-len", type=int, default=T)
     return ap.parse_args()
 
 
@@ -165,6 +169,18 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+def profiled_traffic():
+    """DRAM bytes (read + write) per launch of the dominant kernel from the
+    committed ncu summary (profiles/lchain_ws_kernel_cfg2.txt), or None."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", "lchain_ws_kernel_cfg2.txt")):
+            if line.startswith("traffic_bytes_per_launch_full_size:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
 def make_workload(rank, device):
     import torch
 
@@ -177,7 +193,9 @@ def make_workload(rank, device):
 
 
 def main():
+    global B, T
     args = parse()
+    B, T = args.batch, args.seq_len
     if args.impl == "reference":
         run_reference(args)
         return
@@ -265,19 +283,28 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = world * B * T / float(te)
 
-    # ---- dominant kernel: the forward chain, timed alone ----
+    # ---- the kernels of one step, timed alone: the forward launch (alpha and
+    # beta chains side by side, the dominant kernel) and the backward kernels
     prob = _lib.Problem(cum, tr, db, lengths, K, "log")
+    gout = torch.ones(B, dtype=torch.float32, device=dev)
+    saved = None
     for _ in range(2):
-        _lib.forward(prob, want_saved=True)
-    fe = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(3)]
-    for a, b_ in fe:
+        _, _, saved = _lib.forward(prob, want_saved=True)
+        _lib.backward(prob, saved, gout)
+    fe = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(3)]
+    for e0, e1, e2, e3 in fe:
         flush.zero_()
-        a.record()
-        _lib.forward(prob, want_saved=True)
-        b_.record()
+        e0.record()
+        _, _, saved = _lib.forward(prob, want_saved=True)
+        e1.record()
+        flush.zero_()
+        e2.record()
+        _lib.backward(prob, saved, gout)
+        e3.record()
     torch.cuda.synchronize()
-    t_fwd = statistics.mean(a.elapsed_time(b_) for a, b_ in fe) / 1e3
+    t_fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in fe) / 1e3
+    t_bwd = statistics.mean(e[2].elapsed_time(e[3]) for e in fe) / 1e3
+    del saved
 
     viterbi = None
     if not args.no_viterbi and rank == 0:
@@ -302,37 +329,45 @@ def main():
     except Exception:
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    # algorithmic bytes of one forward-chain launch: cum_scores read once,
-    # partition + float64 log Z written, restart checkpoints written.
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    # algorithmic bytes of one forward launch: cum_scores read by each of the
+    # two chains, their float64 tables written (2C+1 doubles per position and
+    # chain), log Z and the partition written
     lsum = int(lengths_h.sum())
-    S = _lib.checkpoint_interval(T, K)
-    sint = ((S + 7) // 8) * 8
-    nint = T // sint + 1
-    bytes_fwd = 4 * B * (T + 1) * C + B * (4 + 8) + B * nint * ((K - 1) * C * 4 + 2 * C * 4 + (K - 1) * 8)
+    bytes_fwd = 2 * 4 * B * (T + 1) * C + 2 * 8 * B * (T + 1) * (2 * C + 1) + B * (4 + 8)
     achieved = bytes_fwd / t_fwd / 1e9
-    # semiring terms of the factorised recurrence, per forward launch
-    terms = lsum * ((K - 1) * C + C * C)
+    # float64 FMAs of the factorised recurrence per forward launch: per
+    # position and chain, the C x C mat-vec and the (K-1) x C duration sums
+    kcap = max(K - 1, 1)
+    fmas = 2 * lsum * (C * C + kcap * C)
+    traffic = profiled_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 genomic windows: per rank B=64 T=10000 K=300 C=24, "
-                               "lengths U[8000,10000], log fwd+bwd",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"cfg2 genomic windows: per rank B={B} T={T} K={K} C={C}, "
+                               "lengths U[0.8T,T], log fwd+bwd (float32 in/out, float64 "
+                               "arithmetic)",
                    "global_batch": B * world, "seq_len": T, "K": K, "C": C,
                    "parallelism": f"dp{world} (batch-sharded, weak)",
                    "l2": "flushed (256 MiB write) between timed steps"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * (T + 1) * C,
                 "d2h_bytes_per_step": 4 * (C * C + K * C + 1)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": None,
-                     "kernel": "chain_kernel (forward)", "kernel_ms": t_fwd * 1e3,
-                     "note": "HBM is not binding: the scan is bound by its serial per-position "
-                             "latency; see compute_roofline"},
-        "compute_roofline": {"terms_per_launch": terms,
-                             "achieved_gterms_s": terms / t_fwd / 1e9,
-                             "ns_per_position_step": t_fwd / T * 1e9},
-        # per step: forward = prep + chain; backward = prep + beta chain + reduce
-        "gpu_launches": 5 * args.steps,
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "peak_source": peak_src,
+                     "kernel": "lchain_ws_kernel<32,8>: alpha and beta chains, 2B CTAs",
+                     "kernel_ms": t_fwd * 1e3, "backward_kernels_ms": t_bwd * 1e3,
+                     "note": "HBM is not binding: each chain is a serial recurrence over T "
+                             "(one CTA per chain), bound by its per-position latency; see "
+                             "compute_roofline"},
+        "compute_roofline": {"fp64_fma_per_launch": fmas,
+                             "achieved_fp64_tflops": 2 * fmas / t_fwd / 1e12,
+                             "ns_per_position_step": t_fwd / T * 1e9,
+                             "ctas": 2 * B, "sms": torch.cuda.get_device_properties(dev)
+                             .multi_processor_count},
+        # per step: forward = prep (2) + chains (1); backward = pos, tr, db, reduce
+        "gpu_launches": 7 * args.steps,
         "clocks": clocks,
     }
     if viterbi:

@@ -142,8 +142,8 @@ size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_
  * must not call cudaMalloc on its request path).  Results equal
  * semicrf_forward's partition for the same problem.
  *  - Scratch: a fixed 1 MiB device array inside the library, one per
- *    device; every accepted shape fits (the largest, C=256 with K=64,
- *    needs 675 KiB).  A problem whose semicrf_forward_workspace_size
+ *    device; every accepted shape fits (the largest, at C=256, need
+ *    under 700 KiB).  A problem whose semicrf_forward_workspace_size
  *    exceeds 1 MiB is rejected with SEMICRF_ERR_WORKSPACE (before any CUDA
  *    call).
  *  - Nothing in the scratch needs to start at zero (each call writes what it

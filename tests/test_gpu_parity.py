@@ -262,6 +262,18 @@ ORACLE_CASES = [
 
 @pytest.mark.parametrize("case", ORACLE_CASES)
 def test_random_vs_oracle(case, oracle):
+    _random_vs_oracle(case, oracle)
+
+
+@pytest.mark.parametrize("case", [ORACLE_CASES[1], ORACLE_CASES[2], ORACLE_CASES[5],
+                                  ORACLE_CASES[6], ORACLE_CASES[7]])
+def test_random_vs_oracle_recompute(case, oracle, monkeypatch):
+    """The memory-light layout: ring checkpoints saved, alpha recomputed."""
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_BACKWARD", "recompute")
+    _random_vs_oracle(case, oracle)
+
+
+def _random_vs_oracle(case, oracle):
     from inputs import make_streaming_inputs
 
     from torch_semimarkov_b200 import semi_crf_streaming_forward

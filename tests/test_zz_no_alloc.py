@@ -78,16 +78,27 @@ def test_noalloc_size_checks_without_gpu():
     """Needs no GPU: validation and the scratch-size check precede any CUDA call."""
     L = _lib()
     lib = L.load()
-    # every shape the scan accepts fits the 1 MiB scratch; the widest
-    # (C=256 at its largest K) is the biggest
-    for C, K in [(256, 64), (192, 88), (128, 126), (8, 2900), (1, 13000)]:
-        p = _shape(C=C, K=K, checkpoint_interval=max(K, 1000))
+    # every shape the scan accepts fits the 1 MiB scratch: for each C the
+    # largest accepted K (found by bisection) needs the most
+    for C in (1, 8, 24, 64, 128, 256):
+        lo, hi = 1, 32767
+        while lo < hi:
+            mid = (lo + hi + 1) // 2
+            p = _shape(C=C, K=mid, checkpoint_interval=max(mid, 1000))
+            if lib.semicrf_forward_workspace_size(ctypes.byref(p)) > 0:
+                lo = mid
+            else:
+                hi = mid - 1
+        p = _shape(C=C, K=lo, checkpoint_interval=max(lo, 1000))
         need = lib.semicrf_forward_workspace_size(ctypes.byref(p))
-        assert 0 < need <= (1 << 20), (C, K, need)
+        assert 0 < need <= (1 << 20), (C, lo, need)
         assert lib.semicrf_forward_noalloc(ctypes.byref(p), None, None) == L.SEMICRF_OK
+        big = _shape(C=C, K=lo + 1, checkpoint_interval=max(lo + 1, 1000))
+        want = lib.semicrf_forward(ctypes.byref(big), None, None, 0, None, None, 0, None)
+        assert want != L.SEMICRF_OK and lib.semicrf_forward_noalloc(ctypes.byref(big), None,
+                                                                    None) == want
     # shapes the scan rejects get semicrf_forward's code, before any device work
-    for kw in [dict(K=0), dict(semiring=7), dict(C=300), dict(C=256, K=65, checkpoint_interval=65),
-               dict(batch=2)]:
+    for kw in [dict(K=0), dict(semiring=7), dict(C=300), dict(batch=2)]:
         p = _shape(**kw)
         want = lib.semicrf_forward(ctypes.byref(p), None, None, 0, None, None, 0, None)
         assert want != L.SEMICRF_OK, kw

@@ -27,12 +27,13 @@ SEMICRF_ERR_CUDA = 4
 SEMICRF_ERR_SEMIRING = 5
 SEMIRINGS = {"log": 0, "max": 1}
 KEEP_ALPHA, RECOMPUTE = 0, 1
-# Keep float64 alpha tables for the backward (no recompute) while they stay
-# under this many bytes; above it the forward keeps sqrt(T)-spaced ring
-# checkpoints and the backward recomputes alpha between them.  The
+# Keep the float64 tables of both chains (alpha, and beta computed beside it
+# in the forward launch) for the backward while they stay under this many
+# bytes; above it the forward keeps sqrt(T)-spaced ring checkpoints and the
+# backward recomputes alpha between them and runs the beta chain itself.  The
 # environment variable TORCH_SEMIMARKOV_B200_BACKWARD=keep|recompute forces
 # one or the other.
-KEEP_ALPHA_MAX_BYTES = 8 << 30
+KEEP_ALPHA_MAX_BYTES = 16 << 30
 
 
 def backward_mode_for(B: int, T: int, C: int) -> int:
@@ -41,7 +42,7 @@ def backward_mode_for(B: int, T: int, C: int) -> int:
         return RECOMPUTE
     if env == "keep":
         return KEEP_ALPHA
-    table_bytes = 8 * B * (T + 1) * (2 * C + 1)
+    table_bytes = 16 * B * (T + 1) * (2 * C + 1)
     return KEEP_ALPHA if table_bytes <= KEEP_ALPHA_MAX_BYTES else RECOMPUTE
 
 # every symbol include/semicrf.h declares

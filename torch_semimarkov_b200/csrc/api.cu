@@ -49,6 +49,8 @@ int validate_shape(const semicrf_problem* p) {
     return SEMICRF_ERR_INVALID_ARGUMENT;
   if (p->semiring == SEMICRF_LOG && !lchain_supported((int)p->C, (int)p->K))
     return SEMICRF_ERR_UNSUPPORTED;
+  if (p->semiring == SEMICRF_LOG && !lmarg_plan(1, 1, (int)p->K, (int)p->C).ok)
+    return SEMICRF_ERR_UNSUPPORTED;
   if (!chain_supported((int)p->C, (int)p->K, SEMICRF_MAX, true)) return SEMICRF_ERR_UNSUPPORTED;
   return SEMICRF_OK;
 }
@@ -83,6 +85,9 @@ struct SavedLayout {
   double* a_tab;   // log semiring, SEMICRF_KEEP_ALPHA: alpha tables
   double* A_tab;
   double* n_tab;
+  double* b_tab;   // ... and the beta chain's tables
+  double* B_tab;
+  double* m_tab;
 };
 
 SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
@@ -100,6 +105,9 @@ SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
     s.a_tab = cv.take<double>(n);
     s.A_tab = cv.take<double>(n);
     s.n_tab = cv.take<double>(B * (p->T + 1));
+    s.b_tab = cv.take<double>(n);
+    s.B_tab = cv.take<double>(n);
+    s.m_tab = cv.take<double>(B * (p->T + 1));
   }
   return s;
 }
@@ -132,25 +140,49 @@ struct BwdLayout {
 
 struct LBwdLayout {
   Prepared pr;
-  double *a_tab, *A_tab, *n_tab, *part_tr, *part_db, *gws;
+  double *a_tab, *A_tab, *n_tab;  // SEMICRF_RECOMPUTE: alpha tables
+  double *b_tab, *B_tab, *m_tab;  // SEMICRF_RECOMPUTE: beta tables
+  double *la, *lb, *part_tr, *part_db;
+  LMargPlan mp;
 };
 
 LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
   LBwdLayout w{};
   w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
+  const size_t nt = (size_t)p->batch * (p->T + 1);
   if (p->backward_mode == SEMICRF_RECOMPUTE) {
-    const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
     w.a_tab = cv.take<double>(n);
     w.A_tab = cv.take<double>(n);
-    w.n_tab = cv.take<double>((size_t)p->batch * (p->T + 1));
+    w.n_tab = cv.take<double>(nt);
+    w.b_tab = cv.take<double>(n);
+    w.B_tab = cv.take<double>(n);
+    w.m_tab = cv.take<double>(nt);
   }
-  w.part_tr = cv.take<double>((size_t)p->batch * p->C * p->C);
-  w.part_db = cv.take<double>((size_t)p->batch * p->K * p->C);
-  size_t g1 = lchain_gws_doubles_per_cta((int)p->C, (int)p->K);
-  const size_t g2 = lchain_ws_gws_doubles_per_cta((int)p->C, (int)p->K);
-  if (g2 > g1) g1 = g2;
-  w.gws = cv.take<double>((size_t)p->batch * g1);
+  w.mp = lmarg_plan((int)p->batch, (int)p->T, (int)p->K, (int)p->C);
+  w.la = cv.take<double>(n);
+  w.lb = cv.take<double>(n);
+  w.part_tr = cv.take<double>((size_t)p->batch * w.mp.nchunk * p->C * p->C);
+  w.part_db = cv.take<double>((size_t)p->batch * w.mp.nsplit * kcap_of(p->K) * p->C);
   return w;
+}
+
+// the beta chain (dir 1) of a log-semiring problem, writing its tables
+LChainArgs beta_chain_args(const semicrf_problem* p, const Prepared& pr, double* b_tab,
+                           double* B_tab, double* m_tab) {
+  LChainArgs a{};
+  a.mode = 0;
+  a.dir = 1;
+  a.cum = p->cum_scores;
+  a.ps = p->proj_start;
+  a.pe = p->proj_end;
+  a.lengths = p->lengths;
+  a.mx = pr.mx_b;
+  a.colmax = pr.colmax_b;
+  a.a_tab = b_tab;
+  a.A_tab = B_tab;
+  a.n_tab = m_tab;
+  return a;
 }
 
 BwdLayout carve_bwd(Carver& cv, const semicrf_problem* p) {
@@ -266,25 +298,30 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     a.sref = (int)p->checkpoint_interval;
     a.sint = sint_of(p);
     a.nint = nint_of(p);
-    if (saved) {
-      Carver sc(saved);
-      SavedLayout sl = carve_saved(sc, p);
-      a.logz = sl.logz;
-      if (p->backward_mode == SEMICRF_RECOMPUTE) {
-        a.sv = sl.sv;
-        a.write_saved = 1;
-      } else {
-        a.a_tab = sl.a_tab;
-        a.A_tab = sl.A_tab;
-        a.n_tab = sl.n_tab;
-      }
-    }
     L.a0 = a;
     L.a1 = a;
     L.n1 = (int)p->batch;
-    if (!a.ref_ckpt && !a.write_saved && lchain_ws_supported((int)p->C, (int)p->K))
-      return cuda_status(launch_lchain_ws(L, s));
-    return cuda_status(launch_lchain(L, (int)p->batch, s));
+    int grid = (int)p->batch;
+    if (saved) {
+      Carver sc(saved);
+      SavedLayout sl = carve_saved(sc, p);
+      L.a0.logz = sl.logz;
+      if (p->backward_mode == SEMICRF_RECOMPUTE) {
+        L.a0.sv = sl.sv;
+        L.a0.write_saved = 1;
+      } else {
+        // keep both chains' tables: the beta chain does not depend on alpha,
+        // so it runs beside the alpha chain in the same launch
+        L.a0.a_tab = sl.a_tab;
+        L.a0.A_tab = sl.A_tab;
+        L.a0.n_tab = sl.n_tab;
+        L.a1 = beta_chain_args(p, pr, sl.b_tab, sl.B_tab, sl.m_tab);
+        grid = 2 * (int)p->batch;
+      }
+    }
+    if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_ws_supported((int)p->C, (int)p->K))
+      return cuda_status(launch_lchain_ws(L, grid, s));
+    return cuda_status(launch_lchain(L, grid, s));
   }
   ChainLaunch L = base_launch(p, pr);
   ChainArgs a = base_args(p);
@@ -341,9 +378,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     LBwdLayout w = carve_lbwd(cv, p);
     Carver sc(const_cast<void*>(saved));
     SavedLayout sl = carve_saved(sc, p);
-    cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
-                                kcap_of(p->K), kP, SEMICRF_LOG, w.pr, s);
-    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+    cudaError_t e = cudaSuccess;
     LChainLaunch L{};
     L.B = (int)p->batch;
     L.T = (int)p->T;
@@ -351,11 +386,14 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     L.C = (int)p->C;
     L.dbe = w.pr.dbe;
     L.dbmax = w.pr.dbmax;
-    const double* ta = sl.a_tab;
-    const double* tA = sl.A_tab;
-    const double* tn = sl.n_tab;
+    const double *xa = sl.a_tab, *xA = sl.A_tab, *xn = sl.n_tab;
+    const double *ya = sl.b_tab, *yA = sl.B_tab, *yn = sl.m_tab;
     if (p->backward_mode == SEMICRF_RECOMPUTE) {
-      // alpha between checkpoints, all segments of all sequences in parallel
+      // alpha between checkpoints (all segments of all sequences in parallel)
+      // and the beta chains
+      e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C, kcap_of(p->K), kP,
+                      SEMICRF_LOG, w.pr, s);
+      if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
       LChainArgs r{};
       r.mode = 1;
       r.dir = 0;
@@ -371,46 +409,61 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
       r.a_tab = w.a_tab;
       r.A_tab = w.A_tab;
       r.n_tab = w.n_tab;
+      const LChainArgs bb = beta_chain_args(p, w.pr, w.b_tab, w.B_tab, w.m_tab);
       L.a0 = r;
-      L.a1 = r;
       L.n1 = (int)p->batch * r.nint;
-      e = launch_lchain(L, L.n1, s);
+      if (lchain_ws_supported((int)p->C, (int)p->K)) {
+        L.a1 = r;
+        e = launch_lchain(L, L.n1, s);
+        if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+        LChainLaunch Lb = L;
+        Lb.a0 = bb;
+        Lb.a1 = bb;
+        Lb.n1 = (int)p->batch;
+        e = launch_lchain_ws(Lb, (int)p->batch, s);
+      } else {
+        L.a1 = bb;
+        e = launch_lchain(L, L.n1 + (int)p->batch, s);
+      }
       if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
-      ta = w.a_tab;
-      tA = w.A_tab;
-      tn = w.n_tab;
+      xa = w.a_tab;
+      xA = w.A_tab;
+      xn = w.n_tab;
+      ya = w.b_tab;
+      yA = w.B_tab;
+      yn = w.m_tab;
     }
-    LChainArgs bb{};
-    bb.mode = 0;
-    bb.dir = 1;
-    bb.cum = p->cum_scores;
-    bb.ps = p->proj_start;
-    bb.pe = p->proj_end;
-    bb.lengths = p->lengths;
-    bb.mx = w.pr.mx_b;
-    bb.colmax = w.pr.colmax_b;
-    bb.in_a = ta;
-    bb.in_A = tA;
-    bb.in_n = tn;
-    bb.logz_in = sl.logz;
-    bb.grad_output = grad_output;
-    bb.grad_cum = grad_cum;
-    bb.grad_ps = p->proj_start ? grad_proj_start : nullptr;
-    bb.grad_pe = p->proj_end ? grad_proj_end : nullptr;
-    bb.part_tr = w.part_tr;
-    bb.part_db = w.part_db;
-    bb.gws = w.gws;
-    L.a0 = bb;
-    L.a1 = bb;
-    L.n1 = (int)p->batch;
-    if (lchain_ws_supported((int)p->C, (int)p->K))
-      e = launch_lchain_ws(L, s);
-    else
-      e = launch_lchain(L, (int)p->batch, s);
-    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
-    return cuda_status(launch_lreduce((int)p->batch, (int)p->K, (int)p->C, w.part_tr,
-                                      w.part_db, grad_output, p->transition, grad_transition,
-                                      grad_duration_bias, s));
+    LMargArgs m{};
+    m.B = (int)p->batch;
+    m.T = (int)p->T;
+    m.K = (int)p->K;
+    m.C = (int)p->C;
+    m.kcap = kcap_of(p->K);
+    m.cum = p->cum_scores;
+    m.ps = p->proj_start;
+    m.pe = p->proj_end;
+    m.tr = p->transition;
+    m.db = p->duration_bias;
+    m.lengths = p->lengths;
+    m.logz = sl.logz;
+    m.grad_output = grad_output;
+    m.xa = xa;
+    m.xA = xA;
+    m.xn = xn;
+    m.ya = ya;
+    m.yA = yA;
+    m.yn = yn;
+    m.grad_cum = grad_cum;
+    m.grad_ps = p->proj_start ? grad_proj_start : nullptr;
+    m.grad_pe = p->proj_end ? grad_proj_end : nullptr;
+    m.la = w.la;
+    m.lb = w.lb;
+    m.part_tr = w.part_tr;
+    m.nchunk = w.mp.nchunk;
+    m.part_db = w.part_db;
+    m.nsplit = w.mp.nsplit;
+    m.cg = w.mp.cg;
+    return cuda_status(launch_lmarg(m, grad_transition, grad_duration_bias, s));
   }
   Carver cv(workspace);
   BwdLayout w = carve_bwd(cv, p);

@@ -126,33 +126,33 @@ bool chain_supported(int C, int K, int semiring, bool bp) {
 // ---------------------------------------------------------------------------
 // prep kernel: per-launch constants (same for every sequence)
 // ---------------------------------------------------------------------------
+// column maxima (over sources) of tr and tr^T, and duration-bias maxima
+__global__ void prep_max_kernel(const float* __restrict__ tr, const float* __restrict__ db, int K,
+                                int C, int kcap, int semiring, Prepared pr) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float mf = kNegInf, mb = kNegInf, md = kNegInf;
+  for (int r = 0; r < C; ++r) {
+    mf = fmaxf(mf, tr[r * C + c]);  // M_f[r][c] = tr[r][c]
+    mb = fmaxf(mb, tr[c * C + r]);  // M_b[r][c] = tr[c][r]
+  }
+  for (int k = 1; k <= kcap; ++k) md = fmaxf(md, db[(k < K - 1 ? k : K - 1) * C + c]);
+  pr.colmax_f[c] = semiring == 0 ? mf : 0.f;
+  pr.colmax_b[c] = semiring == 0 ? mb : 0.f;
+  pr.dbmax[c] = md;
+}
+
+// the tables, given the maxima
 __global__ void prep_kernel(const float* __restrict__ tr, const float* __restrict__ db, int K,
                             int C, int kcap, int kx, int semiring, Prepared pr) {
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   const int nth = gridDim.x * blockDim.x;
-  // column maxima (over sources) of tr and tr^T, and duration-bias maxima
-  for (int c = tid; c < C; c += nth) {
-    float mf = kNegInf, mb = kNegInf, md = kNegInf;
-    for (int r = 0; r < C; ++r) {
-      mf = fmaxf(mf, tr[r * C + c]);  // M_f[r][c] = tr[r][c]
-      mb = fmaxf(mb, tr[c * C + r]);  // M_b[r][c] = tr[c][r]
-    }
-    for (int k = 1; k <= kcap; ++k) md = fmaxf(md, db[(k < K - 1 ? k : K - 1) * C + c]);
-    pr.colmax_f[c] = semiring == 0 ? mf : 0.f;
-    pr.colmax_b[c] = semiring == 0 ? mb : 0.f;
-    pr.dbmax[c] = md;
-  }
   for (int i = tid; i < C * C; i += nth) {
     const int r = i / C, c = i % C;
     float vf = tr[r * C + c], vb = tr[c * C + r];
     if (semiring == 0) {
-      float mf = kNegInf, mb = kNegInf;
-      for (int q = 0; q < C; ++q) {
-        mf = fmaxf(mf, tr[q * C + c]);
-        mb = fmaxf(mb, tr[c * C + q]);
-      }
-      vf = __expf(vf - mf);
-      vb = __expf(vb - mb);
+      vf = __expf(vf - pr.colmax_f[c]);
+      vb = __expf(vb - pr.colmax_b[c]);
     }
     pr.mx_f[i] = vf;
     pr.mx_b[i] = vb;
@@ -162,11 +162,7 @@ __global__ void prep_kernel(const float* __restrict__ tr, const float* __restric
     float v = kNegInf;
     if (k >= 1 && k <= kcap) v = db[(k < K - 1 ? k : K - 1) * C + c];
     pr.dbl[i] = v;
-    if (semiring == 0) {
-      float md = kNegInf;
-      for (int q = 1; q <= kcap; ++q) md = fmaxf(md, db[(q < K - 1 ? q : K - 1) * C + c]);
-      pr.dbe[i] = (v == kNegInf) ? 0.f : __expf(v - md);
-    }
+    if (semiring == 0) pr.dbe[i] = (v == kNegInf) ? 0.f : __expf(v - pr.dbmax[c]);
   }
 }
 
@@ -174,6 +170,9 @@ cudaError_t launch_prep(const float* tr, const float* db, int K, int C, int kcap
                         int semiring, const Prepared& prep, cudaStream_t s) {
   const int kx = kcap + kPrepRowsExtra;
   (void)P;
+  prep_max_kernel<<<(C + 127) / 128, 128, 0, s>>>(tr, db, K, C, kcap, semiring, prep);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   int work = C * C > kx * C ? C * C : kx * C;
   int grid = (work + 255) / 256;
   if (grid > 1024) grid = 1024;

@@ -26,19 +26,17 @@
 // perturbation of tr/db, not an accumulating error).
 //
 // One CTA = one chain.  Per block of P targets:
-//   phase A (256 threads): [backward: gradients of the previous block]
-//           re-anchoring, the g/h factors, and the far sums over all sources
-//           before the block (P accumulators per (label, source chunk)).
+//   phase A (256 threads): re-anchoring, the g/h factors, and the far sums
+//           over all sources before the block (P accumulators per (label,
+//           source chunk)).
 //   phase B (C serial threads): the P targets in order -- near sources,
 //           the state, the float64 mat-vec, the new source.
-// The backward chain (dir = 1) consumes the alpha tables (a, A = exp(m - n)
-// and n per position) and accumulates, without atomics:
-//   Pstart[t,c] = exp(A + G - logZ), Pend[t,c] = exp(alpha + beta - logZ)
-//   grad_cum = g_b (Pend - Pstart), grad_ps = g_b Pstart, grad_pe = g_b Pend
-//   grad_tr[c',c] += exp(alpha[t,c'] + tr[c',c] + G[t,c] - logZ)
-//   grad_db[k,c]  += sum_targets (Pstart / S) * E[source] * Db[k]
-// (the last one is the share of each source in the target's k-sum), into
-// per-sequence float64 partials reduced over the batch afterwards.
+// The same kernel runs the alpha chain (dir = 0) and the beta chain (dir =
+// 1: the recurrence reversed, with tr^T and the projections swapped).  Both
+// write their tables (a = exp(x - n), A = exp(m - n) and n per position), from
+// which lmarg.cu derives every gradient.  This kernel serves any C <= 256,
+// checkpoint segments (mode 1) and the reference ring-checkpoint output; the
+// warp-specialised lchain_ws.cu is the fast path for whole chains at C <= 64.
 
 #include "semicrf_internal.cuh"
 
@@ -66,11 +64,11 @@ constexpr size_t kSmemMax = 227 * 1024;
 constexpr double kHi = 1e78, kLo = 1e-78;  // re-anchor when the newest source leaves this
 
 struct LPlan {
-  int C, CP, K, kcap, R, kx, nsplit, nw;  // nw: k-ranges of width LP for the db correlation
-  bool db_smem, acc_smem, mx_smem;
+  int C, CP, K, kcap, R, kx, nsplit;
+  bool db_smem, mx_smem;
   // byte offsets
-  int o_ring, o_dbe, o_mx, o_dbmax, o_colmax, o_ref, o_g, o_h, o_far, o_part, o_abuf, o_sa, o_sy,
-      o_ss, o_accdb, o_acctr, o_misc, o_flag, o_fac, o_pcu, o_pto, o_pso;
+  int o_ring, o_dbe, o_mx, o_dbmax, o_colmax, o_ref, o_g, o_h, o_far, o_part, o_abuf, o_misc,
+      o_flag, o_fac, o_pcu, o_pto, o_pso;
   int bytes;
 };
 
@@ -80,8 +78,7 @@ __host__ __device__ inline int lround_cp(int C) {
 
 __host__ __device__ inline int lblock(int C) { return lround_cp(C) == 256 ? 4 : kLP; }
 
-__host__ __device__ inline void lmake(LPlan& p, int C, int K, bool db_smem, bool acc_smem,
-                                      bool mx_smem) {
+__host__ __device__ inline void lmake(LPlan& p, int C, int K, bool db_smem, bool mx_smem) {
   const int kLP = lblock(C);  // targets per block for this label count
   p.C = C;
   p.CP = lround_cp(C);
@@ -90,9 +87,7 @@ __host__ __device__ inline void lmake(LPlan& p, int C, int K, bool db_smem, bool
   p.R = p.kcap + kLP;
   p.kx = p.kcap + kPrepRowsExtra;  // = kcap + 2*kLP + 1
   p.nsplit = kNT / C > 0 ? kNT / C : 1;
-  p.nw = (p.kcap + kLP - 1) / kLP;
   p.db_smem = db_smem;
-  p.acc_smem = acc_smem;
   p.mx_smem = mx_smem;
   int o = 0;
   auto take = [&](int n) {
@@ -111,11 +106,6 @@ __host__ __device__ inline void lmake(LPlan& p, int C, int K, bool db_smem, bool
   p.o_far = take(8 * kLP * p.CP);
   p.o_part = take(8 * p.nsplit * kLP * C);
   p.o_abuf = take(8 * p.CP);
-  p.o_sa = take(8 * kLP * p.CP);
-  p.o_sy = take(8 * kLP * p.CP);
-  p.o_ss = take(8 * kLP * p.CP);
-  p.o_accdb = acc_smem ? take(8 * p.kcap * C) : -1;
-  p.o_acctr = -1;
   p.o_misc = take(8 * 16);
   p.o_flag = take(4 * p.CP);
   p.o_fac = take(8 * p.CP);
@@ -127,26 +117,15 @@ __host__ __device__ inline void lmake(LPlan& p, int C, int K, bool db_smem, bool
 
 __host__ __device__ inline bool lchoose(LPlan& p, int C, int K) {
   const bool mx = C <= 128;
-  lmake(p, C, K, true, true, mx);
+  lmake(p, C, K, true, mx);
   if ((size_t)p.bytes <= kSmemMax) return true;
-  lmake(p, C, K, false, true, mx);
+  lmake(p, C, K, false, mx);
   if ((size_t)p.bytes <= kSmemMax) return true;
-  lmake(p, C, K, false, false, mx);
-  if ((size_t)p.bytes <= kSmemMax) return true;
-  lmake(p, C, K, false, false, false);
+  lmake(p, C, K, false, false);
   return (size_t)p.bytes <= kSmemMax;
 }
 
 }  // namespace
-
-// global scratch per CTA (arrays that did not fit in shared memory)
-size_t lchain_gws_doubles_per_cta(int C, int K) {
-  LPlan p;
-  if (!lchoose(p, C, K)) return 0;
-  size_t n = 0;
-  if (!p.acc_smem) n += (size_t)p.kcap * C;
-  return n;
-}
 
 bool lchain_supported(int C, int K) {
   LPlan p;
@@ -208,17 +187,12 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   double* far = reinterpret_cast<double*>(smraw + pl.o_far);
   double* part = reinterpret_cast<double*>(smraw + pl.o_part);
   double* abuf = reinterpret_cast<double*>(smraw + pl.o_abuf);
-  double* sa = reinterpret_cast<double*>(smraw + pl.o_sa);
-  double* sy = reinterpret_cast<double*>(smraw + pl.o_sy);
-  double* ss = reinterpret_cast<double*>(smraw + pl.o_ss);
   double* misc = reinterpret_cast<double*>(smraw + pl.o_misc);
   int* flag = reinterpret_cast<int*>(smraw + pl.o_flag);
   double* fac = reinterpret_cast<double*>(smraw + pl.o_fac);
   double* pcu = reinterpret_cast<double*>(smraw + pl.o_pcu);
   double* pto = reinterpret_cast<double*>(smraw + pl.o_pto);
   double* pso = reinterpret_cast<double*>(smraw + pl.o_pso);
-  double* accdb = pl.acc_smem ? reinterpret_cast<double*>(smraw + pl.o_accdb)
-                              : A.gws + (size_t)blockIdx.x * ((size_t)kcap * C);
 
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
   const float* ps_b = A.ps ? A.ps + (size_t)b * T * C : nullptr;
@@ -249,14 +223,10 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   if (pl.mx_smem)
     for (int i = tid; i < C * C; i += kNT) const_cast<float*>(mx)[i] = A.mx[i];
   const bool fwd_full = dir == 0 && A.mode == 0;
-  const bool bwd = dir == 1;
   float* const ref_ckpt = A.ref_ckpt;
   const int nref = A.nref, sref = A.sref, sint = A.sint, nint = A.nint;
   const bool write_saved = fwd_full && A.write_saved;
   double* const svbase = A.sv;
-  if (bwd) {
-    for (int i = tid; i < kcap * C; i += kNT) accdb[i] = 0.0;
-  }
   if (fwd_full && ref_ckpt) {
     float* rc = ref_ckpt + (size_t)b * nref * K * C;
     for (int i = tid; i < nref * K * C; i += kNT) rc[i] = (i < C) ? 0.f : kRefNegInf;
@@ -273,24 +243,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   double* atab_b = A.a_tab ? A.a_tab + (size_t)b * (T + 1) * C : nullptr;
   double* Atab_b = A.A_tab ? A.A_tab + (size_t)b * (T + 1) * C : nullptr;
   double* ntab_b = A.n_tab ? A.n_tab + (size_t)b * (T + 1) : nullptr;
-  // backward inputs (alpha tables of the same sequence)
-  const double* xa_b = bwd ? A.in_a + (size_t)b * (T + 1) * C : nullptr;
-  const double* ya_b = bwd ? A.in_A + (size_t)b * (T + 1) * C : nullptr;
-  const double* na_b = bwd ? A.in_n + (size_t)b * (T + 1) : nullptr;
-  const double logz = bwd ? A.logz_in[b] : 0.0;
-  const double gout = bwd ? (double)A.grad_output[b] : 0.0;
-  float* gcum_b = bwd ? A.grad_cum + (size_t)b * (T + 1) * C : nullptr;
-  float* gps_b = (bwd && A.grad_ps) ? A.grad_ps + (size_t)b * T * C : nullptr;
-  float* gpe_b = (bwd && A.grad_pe) ? A.grad_pe + (size_t)b * T * C : nullptr;
-  // grad_tr accumulators: thread owns pairs p = tid + q*kNT, q < TRQ
-  constexpr bool TR_REG = CP == 32;
-  constexpr int TRQ = TR_REG ? (CP * CP + kNT - 1) / kNT : 1;
-  double acctr[TRQ];
-#pragma unroll
-  for (int q = 0; q < TRQ; ++q) acctr[q] = 0.0;
-  double* ptr_b = bwd ? A.part_tr + (size_t)b * C * C : nullptr;
-  if (bwd && !TR_REG)
-    for (int i = tid; i < C * C; i += kNT) ptr_b[i] = 0.0;
 
   auto sync_serial = [&]() {
     if (SW == 1)
@@ -377,12 +329,12 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
         ref[c] = (ym0 > 0.0) ? log(ym0) + colmax[c] + so - csign * cu : 0.0;
         ring[0 * C + c] = (ym0 > 0.0) ? 1.0 : 0.0;
         const int t0 = cpos(0);
-        if (atab_b && dir == 0) atab_b[(size_t)t0 * C + c] = a0;
-        if (Atab_b && dir == 0) Atab_b[(size_t)t0 * C + c] = ym0 * ecol;
+        if (atab_b) atab_b[(size_t)t0 * C + c] = a0;
+        if (Atab_b) Atab_b[(size_t)t0 * C + c] = ym0 * ecol;
       }
       if (tid == 0) {
         misc[0] = 0.0;  // n of position u_begin
-        if (ntab_b && dir == 0) ntab_b[cpos(0)] = 0.0;
+        if (ntab_b) ntab_b[cpos(0)] = 0.0;
       }
       a_last = (dir == 0) ? a0 : 0.0;
     }
@@ -409,19 +361,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
     }
   }
   __syncthreads();
-  // backward: the position t = Lb (u = 0) gets Pend = exp(alpha[Lb] - logZ); rows
-  // beyond Lb have zero gradient.
-  if (bwd) {
-    const double f = exp(na_b[Lb] - logz);
-    for (int i = tid; i < (T + 1 - Lb) * C; i += kNT) {
-      const int t = Lb + i / C, cc = i % C;
-      float pend = 0.f;
-      if (t == Lb && Lb >= 1) pend = (float)(gout * xa_b[(size_t)Lb * C + cc] * f);
-      gcum_b[(size_t)t * C + cc] = pend;
-      if (gps_b && t < T) gps_b[(size_t)t * C + cc] = 0.f;
-      if (gpe_b && t >= 1) gpe_b[(size_t)(t - 1) * C + cc] = (t == Lb) ? pend : 0.f;
-    }
-  }
   // first block normaliser; re-anchor check of the newest source (as the
   // original run did at the end of the block that ended at u_begin)
   if (serial) {
@@ -437,75 +376,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
     }
   }
   __syncthreads();
-
-  // gradients of the targets of the block that just finished (backward only)
-  auto flush_grads = [&](int u0p, int nPp, double n_prev) {
-    // per-position terms and the transition outer products
-    for (int w = tid; w < nPp * C; w += kNT) {
-      const int i = w / C, cc = w % C;
-      const int u = u0p + i, t = Lb - u;
-      const double f = exp(na_b[t] + n_prev - logz);
-      const double pst = ya_b[(size_t)t * C + cc] * sa[i * CP + cc] * f;
-      const double pend = (t >= 1) ? xa_b[(size_t)t * C + cc] * sy[i * CP + cc] * f : 0.0;
-      gcum_b[(size_t)t * C + cc] = (float)(gout * (pend - pst));
-      if (gps_b) gps_b[(size_t)t * C + cc] = (float)(gout * pst);
-      if (gpe_b && t >= 1) gpe_b[(size_t)(t - 1) * C + cc] = (float)(gout * pend);
-      const double S = ss[i * CP + cc];
-      ss[i * CP + cc] = (S > 0.0) ? pst / S : 0.0;  // omega
-      sa[i * CP + cc] = sa[i * CP + cc] * f;        // a_beta * f for grad_tr
-    }
-    __syncthreads();
-    if (TR_REG) {
-#pragma unroll
-      for (int q = 0; q < TRQ; ++q) {
-        const int p = tid + q * kNT;
-        if (p < C * C) {
-          const int cs = p / C, cd = p % C;
-          double acc = acctr[q];
-          for (int i = 0; i < nPp; ++i) {
-            const int t = Lb - (u0p + i);
-            acc = fma(xa_b[(size_t)t * C + cs], sa[i * CP + cd], acc);
-          }
-          acctr[q] = acc;
-        }
-      }
-    } else {
-      for (int p = tid; p < C * C; p += kNT) {
-        const int cs = p / C, cd = p % C;
-        double acc = 0.0;
-        for (int i = 0; i < nPp; ++i) {
-          const int t = Lb - (u0p + i);
-          acc = fma(xa_b[(size_t)t * C + cs], sa[i * CP + cd], acc);
-        }
-        ptr_b[p] += acc;
-      }
-    }
-    // duration-bias correlation: item = (label, k-range of width LP)
-    for (int w = tid; w < pl.nw * C; w += kNT) {
-      const int cc = w % C, r = w / C;
-      const int k_lo = 1 + r * LP;
-      double acc[LP];
-#pragma unroll
-      for (int q = 0; q < LP; ++q) acc[q] = 0.0;
-      for (int i = 0; i < nPp; ++i) {
-        const int u = u0p + i;
-        const double om = ss[i * CP + cc];
-        if (om == 0.0) continue;
-#pragma unroll
-        for (int q = 0; q < LP; ++q) {
-          const int k = k_lo + q;
-          const int s = u - k;
-          if (k <= kcap && s >= 0) acc[q] = fma(om, ring[(s % R) * C + cc], acc[q]);
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < LP; ++q) {
-        const int k = k_lo + q;
-        if (k <= kcap) accdb[(k - 1) * C + cc] += acc[q] * (double)dbe[k * C + cc];
-      }
-    }
-    __syncthreads();
-  };
 
   auto prefetch = [&](int u0n, int tlo, int tstep) {
     if (u0n > u_end) return;
@@ -532,7 +402,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
     const double n_cur = misc[1];
 
     // ===== phase A =====
-    if (bwd && prev_u0 >= 0) flush_grads(prev_u0, prev_nP, prev_n);
     TIM_ADD(0);
     // re-anchor labels whose newest source drifted out of range (fac = that source)
     if (reinterpret_cast<volatile int*>(misc + 5)[0]) {
@@ -641,11 +510,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
             const int t = cpos(u);
             if (atab_b) atab_b[(size_t)t * C + c] = a;
             if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
-            if (bwd) {
-              sa[i * CP + c] = a;
-              sy[i * CP + c] = ym * ecol;
-              ss[i * CP + c] = S;
-            }
             if (fwd_full && ref_ckpt) {
               const int Sr = sref;
               const int ic = (u + Sr - 1) / Sr;
@@ -701,7 +565,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
     prev_n = n_cur;
   }
   TIM_FLUSH();
-  if (bwd && prev_u0 >= 0) flush_grads(prev_u0, prev_nP, prev_n);
 
   // ---- outputs ------------------------------------------------------------
   if (fwd_full) {
@@ -715,25 +578,6 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
         if (A.partition) A.partition[b] = (float)lz;
         if (A.logz) A.logz[b] = lz;
       }
-    }
-  }
-  if (bwd) {
-    if (TR_REG) {
-#pragma unroll
-      for (int q = 0; q < TRQ; ++q) {
-        const int p = tid + q * kNT;
-        if (p < C * C) ptr_b[p] = acctr[q];
-      }
-    }
-    for (int i = tid; i < K * C; i += kNT) {
-      const int k = i / C, cc = i % C;
-      double v = 0.0;
-      if (K == 1) {
-        v = (k == 0) ? accdb[cc] : 0.0;
-      } else if (k >= 1) {
-        v = accdb[(k - 1) * C + cc];
-      }
-      A.part_db[(size_t)b * K * C + i] = v;
     }
   }
 }
@@ -768,31 +612,5 @@ cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s) {
   }
 }
 
-// grad_tr = exp(tr) * sum_b g_b part_tr[b]; grad_db = sum_b g_b part_db[b]
-__global__ void lreduce_kernel(int B, int ntr, int ndb, const double* __restrict__ part_tr,
-                               const double* __restrict__ part_db, const float* __restrict__ g,
-                               const float* __restrict__ tr, float* __restrict__ grad_tr,
-                               float* __restrict__ grad_db) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < ntr) {
-    double acc = 0.0;
-    for (int b = 0; b < B; ++b) acc = fma((double)g[b], part_tr[(size_t)b * ntr + i], acc);
-    grad_tr[i] = (float)(acc * exp((double)tr[i]));
-  } else if (i < ntr + ndb) {
-    const int j = i - ntr;
-    double acc = 0.0;
-    for (int b = 0; b < B; ++b) acc = fma((double)g[b], part_db[(size_t)b * ndb + j], acc);
-    grad_db[j] = (float)acc;
-  }
-}
-
-cudaError_t launch_lreduce(int B, int K, int C, const double* part_tr, const double* part_db,
-                           const float* grad_output, const float* tr, float* grad_tr,
-                           float* grad_db, cudaStream_t s) {
-  const int ntr = C * C, ndb = K * C;
-  lreduce_kernel<<<(ntr + ndb + 255) / 256, 256, 0, s>>>(B, ntr, ndb, part_tr, part_db,
-                                                          grad_output, tr, grad_tr, grad_db);
-  return cudaGetLastError();
-}
 
 }  // namespace semicrf

@@ -8,11 +8,13 @@
 //       near sources (blocks tau-1 and tau), the state a, the float64 mat-vec
 //       and the new source E.  About a dozen dependent float64 operations
 //       plus one shared-memory broadcast per position.
-//   bulk warps      (the other 6-7 warps): while the serial warp works on
-//       block tau they prepare block tau+1 -- its normaliser, frame factors,
-//       g/h factors and the far part of every target's k-sum (all sources
-//       before block tau) -- and, in the backward, accumulate the gradients of
-//       block tau-1.
+//   bulk warps      (the other warps but the idle ones): while the serial
+//       warp works on block tau they prepare block tau+1 -- its normaliser,
+//       frame factors, g/h factors and the far part of every target's k-sum
+//       (all sources before block tau).
+// The same kernel runs the alpha chain (dir = 0) and the beta chain (dir = 1,
+// the recurrence reversed); both write their float64 tables, from which
+// lmarg.cu derives the gradients.
 // Hand-off uses named barriers (FULL[b]: bulk -> serial, DONE[b]: serial ->
 // bulk, double-buffered by block parity).
 //
@@ -64,15 +66,14 @@ __device__ __forceinline__ void bar_sync(int id, int n) {
 }
 
 struct WsPlan {
-  int C, CP, K, kcap, LP, R, kx, nbr, nbulk, nsplit, nw, nwt;
-  bool db_smem, acc_smem;
+  int C, CP, K, kcap, LP, R, kx, nbr, nbulk, nsplit, nwt;
+  bool db_smem;
   int o_ring, o_dbe, o_mx, o_dbmax, o_colmax, o_wring, o_lend, o_nring, o_ca, o_far, o_g,
-      o_h, o_wprev, o_sa, o_sy, o_ss, o_part, o_accdb, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_xs;
+      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm;
   int bytes;
 };
 
-__host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP, bool db_smem,
-                                        bool acc_smem) {
+__host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP, bool db_smem) {
   p.C = C;
   p.CP = CP;
   p.K = K;
@@ -85,10 +86,8 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP,
   while (p.nbr < nbr) p.nbr <<= 1;
   p.nbulk = kWsThreads - 2 * CP;  // warps sharing a sub-partition with a serial warp idle
   p.nsplit = p.nbulk / C > 0 ? p.nbulk / C : 1;
-  p.nw = (p.kcap + LP - 1) / LP;
   p.nwt = p.nbr;
   p.db_smem = db_smem;
-  p.acc_smem = acc_smem;
   int o = 0;
   auto take = [&](int n) {
     const int r = o;
@@ -108,17 +107,12 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP,
   p.o_g = take(8 * 2 * LP * CP);
   p.o_h = take(8 * 2 * LP * CP);
   p.o_wprev = take(8 * 2 * CP);
-  p.o_sa = take(8 * 2 * LP * CP);
-  p.o_sy = take(8 * 2 * LP * CP);
-  p.o_ss = take(8 * 2 * LP * CP);
   p.o_part = take(8 * p.nsplit * LP * C);
-  p.o_accdb = acc_smem ? take(8 * p.kcap * C) : -1;
   p.o_abuf = take(8 * CP);
   p.o_wt = take(8 * 2 * p.nwt * CP);  // W tables of the last two prepared blocks
   p.o_misc = take(8 * 16);
   p.o_edb = take(8 * CP);
   p.o_ecm = take(8 * CP);
-  p.o_xs = take(8 * 8 * CP);  // alpha rows of a flushed block (grad_tr)
   p.bytes = o;
 }
 
@@ -127,11 +121,9 @@ __host__ __device__ inline int ws_cp(int C) { return C <= 32 ? 32 : 64; }
 __host__ __device__ inline bool ws_choose(WsPlan& p, int C, int K) {
   if (C > 64) return false;
   const int CP = ws_cp(C);
-  ws_make(p, C, K, CP, 8, true, true);
+  ws_make(p, C, K, CP, 8, true);
   if ((size_t)p.bytes <= kWsSmemMax) return true;
-  ws_make(p, C, K, CP, 8, false, true);
-  if ((size_t)p.bytes <= kWsSmemMax) return true;
-  ws_make(p, C, K, CP, 8, false, false);
+  ws_make(p, C, K, CP, 8, false);
   return (size_t)p.bytes <= kWsSmemMax;
 }
 
@@ -140,12 +132,6 @@ __host__ __device__ inline bool ws_choose(WsPlan& p, int C, int K) {
 bool lchain_ws_supported(int C, int K) {
   WsPlan p;
   return ws_choose(p, C, K);
-}
-
-size_t lchain_ws_gws_doubles_per_cta(int C, int K) {
-  WsPlan p;
-  if (!ws_choose(p, C, K)) return 0;
-  return p.acc_smem ? 0 : (size_t)p.kcap * C;
 }
 
 // ---------------------------------------------------------------------------
@@ -163,12 +149,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   const bool idle = warp >= 4 && warp < 4 + SW;
   const int btid = (warp < 4) ? tid - CP : tid - 2 * CP;  // bulk thread index
   constexpr int NPART = NT - CP;  // threads taking part in FULL / DONE (serial + bulk)
-  const LChainArgs& A = L.a0;
-  const int b = blockIdx.x;
+  // CTAs [0, n1) take role a0, the rest role a1 (e.g. the alpha and beta
+  // chains of the same batch in one launch)
+  const bool role1 = (int)blockIdx.x >= L.n1;
+  const LChainArgs& A = role1 ? L.a1 : L.a0;
+  const int b = role1 ? (int)blockIdx.x - L.n1 : (int)blockIdx.x;
   if (b >= L.B) return;
   const int C = L.C, K = L.K, T = L.T;
   const int dir = A.dir;
-  const bool bwd = dir == 1;
   const double csign = dir == 0 ? 1.0 : -1.0;
   const long long lraw = A.lengths[b];
   const int Lb = lraw < 0 ? 0 : (lraw > T ? T : (int)lraw);
@@ -192,9 +180,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* gb = reinterpret_cast<double*>(smraw + pl.o_g);
   double* hb = reinterpret_cast<double*>(smraw + pl.o_h);
   double* wprev = reinterpret_cast<double*>(smraw + pl.o_wprev);  // [2][CP]
-  double* sab = reinterpret_cast<double*>(smraw + pl.o_sa);
-  double* syb = reinterpret_cast<double*>(smraw + pl.o_sy);
-  double* ssb = reinterpret_cast<double*>(smraw + pl.o_ss);
   double* part = reinterpret_cast<double*>(smraw + pl.o_part);
   double* abuf = reinterpret_cast<double*>(smraw + pl.o_abuf);
   // wt[(tau&1)][q][c] = W[(tau-q) -> tau, c]  (q = 0 .. nwt-1, 0 beyond the start)
@@ -203,9 +188,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* misc = reinterpret_cast<double*>(smraw + pl.o_misc);
   double* edb = reinterpret_cast<double*>(smraw + pl.o_edb);  // exp(dbmax)
   double* ecm = reinterpret_cast<double*>(smraw + pl.o_ecm);  // exp(colmax)
-  double* xs = reinterpret_cast<double*>(smraw + pl.o_xs);    // [LP][CP]
-  double* accdb = pl.acc_smem ? reinterpret_cast<double*>(smraw + pl.o_accdb)
-                              : A.gws + (size_t)b * ((size_t)kcap * C);
   auto lidx = [&](int gamma) { return (gamma + NBR) & (NBR - 1); };  // gamma >= -NBR
 
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
@@ -234,8 +216,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   for (int i = tid; i < C * C; i += NT) mx[i] = A.mx[i];
   if (dbe_s)
     for (int i = tid; i < pl.kx * C; i += NT) dbe_s[i] = L.dbe[i];
-  if (bwd)
-    for (int i = tid; i < kcap * C; i += NT) accdb[i] = 0.0;
   for (int i = tid; i < R * C; i += NT) ring[i] = 0.0;
   __syncthreads();
 
@@ -244,15 +224,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* atab_b = A.a_tab ? A.a_tab + (size_t)b * (T + 1) * C : nullptr;
   double* Atab_b = A.A_tab ? A.A_tab + (size_t)b * (T + 1) * C : nullptr;
   double* ntab_b = A.n_tab ? A.n_tab + (size_t)b * (T + 1) : nullptr;
-  const double* xa_b = bwd ? A.in_a + (size_t)b * (T + 1) * C : nullptr;
-  const double* ya_b = bwd ? A.in_A + (size_t)b * (T + 1) * C : nullptr;
-  const double* na_b = bwd ? A.in_n + (size_t)b * (T + 1) : nullptr;
-  const double logz = bwd ? A.logz_in[b] : 0.0;
-  const double gout = bwd ? (double)A.grad_output[b] : 0.0;
-  float* gcum_b = bwd ? A.grad_cum + (size_t)b * (T + 1) * C : nullptr;
-  float* gps_b = (bwd && A.grad_ps) ? A.grad_ps + (size_t)b * T * C : nullptr;
-  float* gpe_b = (bwd && A.grad_pe) ? A.grad_pe + (size_t)b * T * C : nullptr;
-  double* ptr_b = bwd ? A.part_tr + (size_t)b * C * C : nullptr;
 
   // ---- initial state (position u_begin = 0, "block -1") -----------------
   // frame of block -1: n = 0, anchor cA_{-1} = cum(0)
@@ -273,28 +244,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const double e0 = ym0 * exp(colmax[c] + soff_at(0, c));
       ring[0 * C + c] = e0;  // slot of position 0
       const int t0 = cpos(0);
-      if (atab_b && dir == 0) atab_b[(size_t)t0 * C + c] = a0;
-      if (Atab_b && dir == 0) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
+      if (atab_b) atab_b[(size_t)t0 * C + c] = a0;
+      if (Atab_b) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
       cA[1 * CP + c] = cumd(0, c);  // anchor of block -1 (parity of -1 is 1)
     }
     if (tid == 0) {
-      if (ntab_b && dir == 0) ntab_b[cpos(0)] = 0.0;
+      if (ntab_b) ntab_b[cpos(0)] = 0.0;
       nring[lidx(-1)] = 0.0;
       lend[lidx(-1)] = 0.0;  // log(max a[0]) = 0 forward; the backward starts from beta
     }
-  }
-  // backward: position t = Lb (u = 0) and rows beyond Lb
-  if (bwd) {
-    const double f = exp(na_b[Lb] - logz);
-    for (int i = tid; i < (T + 1 - Lb) * C; i += NT) {
-      const int t = Lb + i / C, cc = i % C;
-      float pend = 0.f;
-      if (t == Lb && Lb >= 1) pend = (float)(gout * xa_b[(size_t)Lb * C + cc] * f);
-      gcum_b[(size_t)t * C + cc] = pend;
-      if (gps_b && t < T) gps_b[(size_t)t * C + cc] = 0.f;
-      if (gpe_b && t >= 1) gpe_b[(size_t)(t - 1) * C + cc] = (t == Lb) ? pend : 0.f;
-    }
-    for (int i = tid; i < C * C; i += NT) ptr_b[i] = 0.0;
   }
   __syncthreads();
 
@@ -430,91 +388,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       WT_ADD(4);
     };
 
-    // gradients of block tau (backward)
-    auto flush = [&](int tau) {
-      const int bf = tau & 1;
-      const int u0 = u_begin + 1 + tau * LP;
-      const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
-      const double n_tau = nring[lidx(tau)];
-      const double* wcur = wt + (size_t)bf * NWT * CP;  // W[(tau-q) -> tau]
-      for (int w = btid; w < nP * C; w += NBT) {
-        const int i = w / C, cc = w % C;
-        const int u = u0 + i, t = Lb - u;
-        const double f = exp(na_b[t] + n_tau - logz);
-        const double sa = sab[(bf * LP + i) * CP + cc];
-        const double pst = ya_b[(size_t)t * C + cc] * sa * f;
-        const double pend = (t >= 1) ? xa_b[(size_t)t * C + cc] * syb[(bf * LP + i) * CP + cc] * f
-                                     : 0.0;
-        gcum_b[(size_t)t * C + cc] = (float)(gout * (pend - pst));
-        if (gps_b) gps_b[(size_t)t * C + cc] = (float)(gout * pst);
-        if (gpe_b && t >= 1) gpe_b[(size_t)(t - 1) * C + cc] = (float)(gout * pend);
-        const double S = ssb[(bf * LP + i) * CP + cc];
-        ssb[(bf * LP + i) * CP + cc] = (S > 0.0) ? pst / S : 0.0;  // omega
-        sab[(bf * LP + i) * CP + cc] = sa * f;
-      }
-      for (int w = btid; w < nP * C; w += NBT) {
-        const int i = w / C, cc = w % C;
-        xs[i * CP + cc] = xa_b[(size_t)(Lb - (u0 + i)) * C + cc];
-      }
-      bar_sync(kBarBulk, NBT);
-      // transition: part_tr[c',c] += sum_i a_alpha[t_i,c'] * (a_beta f)[i,c]
-      for (int p = btid; p < C * C; p += NBT) {
-        const int cs = p / C, cd = p % C;
-        double acc = 0.0;
-        for (int i = 0; i < nP; ++i) acc = fma(xs[i * CP + cs], sab[(bf * LP + i) * CP + cd], acc);
-        ptr_b[p] += acc;
-      }
-      // duration bias: accdb[k,c] += Db[k,c] * sum_i omega[i,c] * E[u_i - k, c] W.
-      // Item = (label, k-range [k_lo, k_lo+LP)); for target i the sources are
-      // u0+i-k_lo-q (q < LP): a window that slides up by one per target.
-      for (int w = btid; w < pl.nw * C; w += NBT) {
-        const int cc = w % C, r = w / C;
-        const int k_lo = 1 + r * LP;
-        double acc[LP], win[LP];
-        const int s0 = u0 - k_lo;  // source of lag 0 for target 0
-        int slot0 = s0 >= 0 ? s0 % R : 0;
-        {
-          int sl = slot0;
-#pragma unroll
-          for (int q = 0; q < LP; ++q) {
-            acc[q] = 0.0;
-            // window for target 0: sources u0 - k_lo - q
-            const int s = s0 - q;
-            double v = 0.0;
-            if (s >= 0 && k_lo + q <= kcap) {
-              const int beta = (s - u_begin - 1) >= 0 ? (s - u_begin - 1) / LP : -1;
-              v = ring[sl * C + cc] * wcur[(tau - beta) * CP + cc];
-            }
-            win[q] = v;
-            sl = (sl == 0) ? R - 1 : sl - 1;
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < LP; ++i) {
-          if (i < nP) {
-            const double om = ssb[(bf * LP + i) * CP + cc];
-#pragma unroll
-            for (int q = 0; q < LP; ++q) acc[q] = fma(om, win[(q + LP - i) % LP], acc[q]);
-            // slide: add source u0 + i + 1 - k_lo (lag q = 0 for target i+1)
-            const int s = s0 + i + 1;
-            slot0 = (slot0 + 1 == R) ? 0 : slot0 + 1;
-            double v = 0.0;
-            if (s >= 0 && i + 1 < nP) {
-              const int beta = (s - u_begin - 1) >= 0 ? (s - u_begin - 1) / LP : -1;
-              v = ring[slot0 * C + cc] * wcur[(tau - beta) * CP + cc];
-            }
-            win[(LP - 1 - i) % LP] = v;
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < LP; ++q) {
-          const int k = k_lo + q;
-          if (k <= kcap) accdb[(k - 1) * C + cc] += acc[q] * (double)dbe[k * C + cc];
-        }
-      }
-      bar_sync(kBarBulk, NBT);
-    };
-
     if (NB > 0) {
       prepare(0);
       bar_arrive(kBarFull0, NPART);
@@ -525,10 +398,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     for (int tau = 2; tau < NB + 2; ++tau) {
       WT_ADD(5);
+      // buffer (tau & 1) is free once the serial warp is done with block tau-2
       bar_sync(((tau - 2) & 1) ? kBarDone1 : kBarDone0, NPART);
       WT_ADD(0);
-      if (bwd) flush(tau - 2);
-      WT_ADD(1);
       if (tau < NB) {
         prepare(tau);
         bar_arrive((tau & 1) ? kBarFull1 : kBarFull0, NPART);
@@ -648,11 +520,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             const int t = cpos(u);
             if (atab_b) atab_b[(size_t)t * C + c] = a;
             if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
-            if (bwd) {
-              sab[(bf * LP + i) * CP + c] = a;
-              syb[(bf * LP + i) * CP + c] = ym * ecol;
-              ssb[(bf * LP + i) * CP + c] = S;
-            }
           }
           if (tid == 0 && ntab_b) ntab_b[cpos(u)] = n_tau;
           a_last = a;
@@ -684,45 +551,31 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
     }
   }
-  __syncthreads();
-  if (bwd) {
-    for (int i = tid; i < K * C; i += NT) {
-      const int k = i / C, cc = i % C;
-      double v = 0.0;
-      if (K == 1) {
-        v = (k == 0) ? accdb[cc] : 0.0;
-      } else if (k >= 1) {
-        v = accdb[(k - 1) * C + cc];
-      }
-      A.part_db[(size_t)b * K * C + i] = v;
-    }
-  }
 }
 
 // ---------------------------------------------------------------------------
 template <int CP>
-static cudaError_t launch_ws_cp(const LChainLaunch& L, size_t smem, cudaStream_t s) {
+static cudaError_t launch_ws_cp(const LChainLaunch& L, int grid, size_t smem, cudaStream_t s) {
   auto kern = lchain_ws_kernel<CP, 8>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<L.B, kWsThreads, smem, s>>>(L);
+  kern<<<grid, kWsThreads, smem, s>>>(L);
   return cudaGetLastError();
 }
 
-// one CTA per sequence; L.a0 is the (mode 0) role
 #ifdef SEMICRF_TIMING
 extern "C" int semicrf_debug_wstiming(unsigned long long* out) {
   return (int)cudaMemcpyFromSymbol(out, g_wstim, sizeof(g_wstim));
 }
 #endif
 
-cudaError_t launch_lchain_ws(const LChainLaunch& L, cudaStream_t s) {
-  if (L.B <= 0) return cudaSuccess;
+cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s) {
+  if (L.B <= 0 || grid <= 0) return cudaSuccess;
   WsPlan p;
   if (!ws_choose(p, L.C, L.K)) return cudaErrorInvalidValue;
-  if (ws_cp(L.C) == 32) return launch_ws_cp<32>(L, (size_t)p.bytes, s);
-  return launch_ws_cp<64>(L, (size_t)p.bytes, s);
+  if (ws_cp(L.C) == 32) return launch_ws_cp<32>(L, grid, (size_t)p.bytes, s);
+  return launch_ws_cp<64>(L, grid, (size_t)p.bytes, s);
 }
 
 }  // namespace semicrf

@@ -1,0 +1,361 @@
+// lmarg.cu -- log-semiring gradients from the alpha and beta chain tables.
+//
+// The backward of the streaming scan (pytorch_reference.py:276-525, the
+// marginals at :458-499) needs, per sequence b, the segment marginals
+//     P(t -> t+k, c) = exp(A[t,c] + ps[t,c] - cum[t,c] + db[min(k,K-1),c]
+//                          + cum[t+k,c] + pe[t+k-1,c] + beta[t+k,c] - logZ)
+// where A[t,c] = LSE_c' (alpha[t,c'] + tr[c',c]) and beta[s,c] is the
+// backward value of a segment ending at s with label c.  Both chains run
+// before this file (lchain_ws.cu / lchain.cu) and leave float64 tables with a
+// per-position normaliser n:
+//     alpha chain:  xa = exp(alpha - xn),  xA = exp(A - xn)
+//     beta  chain:  ya = exp(G - yn),      yA = exp(beta - yn)
+// with G[t,c] = ps[t,c] + LSE_k(db + cum[t+k] - cum[t] + pe[t+k-1] + beta[t+k]).
+// From these every gradient is a parallel map or reduction -- no serial
+// dependency is left:
+//   Pend[t,c]   = xa*yA*f_t,  Pstart[t,c] = xA*ya*f_t,  f_t = exp(xn+yn-logZ)
+//   grad_cum[t] = g (Pend - Pstart), grad_ps[t] = g Pstart, grad_pe[t-1] = g Pend
+//   grad_tr[c',c] = exp(tr[c',c]) sum_b g_b sum_t xa[t,c'] f_t ya[t,c]
+//   grad_db[k,c]  = exp(db[k,c]) sum_b g_b sum_t X[t,c] Y[t+k,c]
+// where X/Y split the segment marginal into a start and an end factor,
+// re-referenced per tile of targets so that both stay inside float64 range.
+// Partials are per (sequence, chunk) and summed in a fixed order: no atomics.
+
+#include "semicrf_internal.cuh"
+
+namespace semicrf {
+
+namespace {
+
+constexpr int kMT = 256;
+constexpr int kTT = 64;  // targets per correlation tile
+
+__device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
+  const long long l = lengths[b];
+  return l < 0 ? 0 : (l > T ? T : (int)l);
+}
+
+// ---- per-position marginals ------------------------------------------------
+__global__ void __launch_bounds__(kMT) lmarg_pos_kernel(const LMargArgs a) {
+  const int C = a.C, T = a.T;
+  const size_t per_b = (size_t)(T + 1) * C;
+  const size_t total = (size_t)a.B * per_b;
+  for (size_t i = (size_t)blockIdx.x * kMT + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * kMT) {
+    const int b = (int)(i / per_b);
+    const size_t r = i % per_b;
+    const int t = (int)(r / C), c = (int)(r % C);
+    const int Lb = seq_len(a.lengths, b, T);
+    const double g = (double)a.grad_output[b];
+    double pend = 0.0, pst = 0.0;
+    double la = -INFINITY, lb = -INFINITY;
+    if (Lb >= 1 && t <= Lb) {
+      const size_t row = (size_t)b * (T + 1) + t;
+      const double xn = a.xn[row], yn = a.yn[row];
+      const double f = exp(xn + yn - a.logz[b]);
+      if (t >= 1) pend = a.xa[i] * a.yA[i] * f;
+      if (t < Lb) pst = a.xA[i] * a.ya[i] * f;
+      const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
+      const double cu = (double)cum_b[(size_t)t * C + c];
+      if (t < Lb) {
+        const double ps = a.ps ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
+        const double v = a.xA[i];
+        la = (v > 0.0) ? log(v) + xn + ps - cu : -INFINITY;
+      }
+      if (t >= 1) {
+        const double pe = a.pe ? (double)a.pe[((size_t)b * T + t - 1) * C + c] : 0.0;
+        const double v = a.yA[i];
+        lb = (v > 0.0) ? log(v) + yn + cu + pe : -INFINITY;
+      }
+    }
+    a.grad_cum[i] = (float)(g * (pend - pst));
+    if (a.grad_ps && t < T) a.grad_ps[((size_t)b * T + t) * C + c] = (float)(g * pst);
+    if (a.grad_pe && t >= 1) a.grad_pe[((size_t)b * T + t - 1) * C + c] = (float)(g * pend);
+    a.la[i] = la;
+    a.lb[i] = lb;
+  }
+}
+
+// ---- transition partials: part_tr[b][chunk][c'][c] = sum_t xa f * ya --------
+// CTA = (pair block, chunk, sequence); 16x16 threads, each a RT x RT tile of
+// a (16 RT) x (16 RT) pair block; positions staged TS at a time.
+template <int RT>
+__global__ void __launch_bounds__(kMT) lmarg_tr_kernel(const LMargArgs a) {
+  constexpr int PB = 16 * RT;
+  constexpr int TS = 32;
+  __shared__ __align__(16) double xs[TS][PB];
+  __shared__ __align__(16) double ys[TS][PB];
+  __shared__ double fs[TS];
+  const int C = a.C, T = a.T;
+  const int npb = (C + PB - 1) / PB;
+  const int pr = blockIdx.x / npb, pc = blockIdx.x % npb;
+  const int ch = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int Lb = seq_len(a.lengths, b, T);
+  // targets t in [0, Lb-1]; chunk ch of nchunk
+  const int per = (T + a.nchunk - 1) / a.nchunk;
+  const int t_lo = ch * per;
+  const int t_hi = min(t_lo + per, Lb);
+  double acc[RT][RT];
+#pragma unroll
+  for (int i = 0; i < RT; ++i)
+#pragma unroll
+    for (int j = 0; j < RT; ++j) acc[i][j] = 0.0;
+  const double lz = a.logz[b];
+  const size_t rowb = (size_t)b * (T + 1);
+  for (int t0 = t_lo; t0 < t_hi; t0 += TS) {
+    const int n = min(TS, t_hi - t0);
+    __syncthreads();
+    if (tid < TS) fs[tid] = tid < n ? exp(a.xn[rowb + t0 + tid] + a.yn[rowb + t0 + tid] - lz) : 0.0;
+    __syncthreads();
+    for (int e = tid; e < TS * PB; e += kMT) {
+      const int i = e / PB, q = e % PB;
+      const int cs = pr * PB + q, cd = pc * PB + q;
+      double x = 0.0, y = 0.0;
+      if (i < n) {
+        const size_t row = (rowb + t0 + i) * C;
+        if (cs < C) x = a.xa[row + cs] * fs[i];
+        if (cd < C) y = a.ya[row + cd];
+      }
+      xs[i][q] = x;
+      ys[i][q] = y;
+    }
+    __syncthreads();
+    for (int i = 0; i < n; ++i) {
+      double xv[RT], yv[RT];
+#pragma unroll
+      for (int q = 0; q < RT; ++q) {
+        xv[q] = xs[i][ty * RT + q];
+        yv[q] = ys[i][tx * RT + q];
+      }
+#pragma unroll
+      for (int p = 0; p < RT; ++p)
+#pragma unroll
+        for (int q = 0; q < RT; ++q) acc[p][q] = fma(xv[p], yv[q], acc[p][q]);
+    }
+  }
+  double* out = a.part_tr + ((size_t)b * a.nchunk + ch) * C * C;
+#pragma unroll
+  for (int p = 0; p < RT; ++p)
+#pragma unroll
+    for (int q = 0; q < RT; ++q) {
+      const int cs = pr * PB + ty * RT + p, cd = pc * PB + tx * RT + q;
+      if (cs < C && cd < C) out[(size_t)cs * C + cd] = acc[p][q];
+    }
+}
+
+// ---- duration partials: part_db[b][split][k-1][c] = sum_t X[t,c] Y[t+k,c] ----
+// CTA = (label group, split, sequence).  Per tile of kTT targets t0.. and
+// label c, r = max_t la[t,c] over the tile:
+//     X[i] = exp(la[t0+i] - r),   Y[j] = exp(lb[t0+1+j] + r - logZ)
+// so X <= 1 and X[i] Y[i+k-1] = P(t0+i -> t0+i+k) / exp(db).  An item is a
+// (label, 8 consecutive k) pair; its window over Y slides by one per target.
+constexpr int kMaxItems = 8;  // items per thread (host guarantees the bound)
+
+__global__ void __launch_bounds__(kMT) lmarg_db_kernel(const LMargArgs a) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  const int C = a.C, T = a.T, kcap = a.kcap, CG = a.cg;
+  const int g0 = blockIdx.x * CG;
+  const int cgn = min(CG, C - g0);
+  const int sp = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x;
+  // Y rows read by a tile: up to kTT - 8 + (kcap + 7) - 1 + 15 < kTT + kcap + 16
+  const int ny = kTT + kcap + 16;
+  double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
+  double* Y = X + (size_t)kTT * CG;               // [ny][CG]
+  double* rr = Y + (size_t)ny * CG;               // [CG]
+  const int nkg = (kcap + 7) / 8;
+  const int nitems = cgn * nkg;
+  const int Lb = seq_len(a.lengths, b, T);
+  const int per = (Lb + a.nsplit - 1) / (a.nsplit > 0 ? a.nsplit : 1);
+  const int t_lo = sp * per;
+  const int t_hi = min(t_lo + per, Lb);  // targets t < Lb start a segment
+  const double lz = a.logz[b];
+  const size_t rowb = (size_t)b * (T + 1);
+  double acc[kMaxItems][8];
+#pragma unroll
+  for (int j = 0; j < kMaxItems; ++j)
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[j][q] = 0.0;
+
+  for (int t0 = t_lo; t0 < t_hi; t0 += kTT) {
+    const int n = min(kTT, t_hi - t0);
+    __syncthreads();
+    // per-label reference
+    for (int cc = tid; cc < cgn; cc += kMT) {
+      double r = -INFINITY;
+      for (int i = 0; i < n; ++i) r = fmax(r, a.la[(rowb + t0 + i) * C + g0 + cc]);
+      rr[cc] = r;
+    }
+    __syncthreads();
+    for (int e = tid; e < kTT * cgn; e += kMT) {
+      const int i = e / cgn, cc = e % cgn;
+      const double r = rr[cc];
+      double x = 0.0;
+      if (i < n && r > -INFINITY) {
+        const double l = a.la[(rowb + t0 + i) * C + g0 + cc];
+        x = (l > -INFINITY) ? exp(l - r) : 0.0;
+      }
+      X[i * CG + cc] = x;
+    }
+    for (int e = tid; e < ny * cgn; e += kMT) {
+      const int j = e / cgn, cc = e % cgn;
+      const int s = t0 + 1 + j;
+      const double r = rr[cc];
+      double y = 0.0;
+      if (s <= Lb && j < n - 1 + kcap && r > -INFINITY) {
+        const double l = a.lb[(rowb + s) * C + g0 + cc];
+        y = (l > -INFINITY) ? exp(fmin(l + r - lz, 700.0)) : 0.0;
+      }
+      Y[j * CG + cc] = y;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int jt = 0; jt < kMaxItems; ++jt) {
+      const int it = tid + jt * kMT;
+      if (it < nitems) {
+        const int cc = it % cgn, kg = it / cgn;
+        const int k_lo = 1 + 8 * kg;
+        // target i pairs with Y[i + k - 1]: for targets i0 .. i0+7 the window
+        // y[m] = Y[i0 + k_lo - 1 + m], m < 16, covers all 8 lags (X is zero
+        // beyond the last target, so whole groups of 8 are safe)
+        for (int i0 = 0; i0 < n; i0 += 8) {
+          double y[16], x[8];
+#pragma unroll
+          for (int m = 0; m < 16; ++m) y[m] = Y[(i0 + k_lo - 1 + m) * CG + cc];
+#pragma unroll
+          for (int d = 0; d < 8; ++d) x[d] = X[(i0 + d) * CG + cc];
+#pragma unroll
+          for (int d = 0; d < 8; ++d)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[jt][q] = fma(x[d], y[d + q], acc[jt][q]);
+        }
+      }
+    }
+  }
+  double* out = a.part_db + ((size_t)b * a.nsplit + sp) * (size_t)kcap * C;
+#pragma unroll
+  for (int jt = 0; jt < kMaxItems; ++jt) {
+    const int it = tid + jt * kMT;
+    if (it < nitems) {
+      const int cc = it % cgn, kg = it / cgn;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int k = 1 + 8 * kg + q;
+        if (k <= kcap) out[(size_t)(k - 1) * C + g0 + cc] = acc[jt][q];
+      }
+    }
+  }
+}
+
+// ---- fixed-order reduction over sequences and chunks -------------------------
+__global__ void __launch_bounds__(kMT) lmarg_reduce_kernel(const LMargArgs a, float* grad_tr,
+                                                            float* grad_db) {
+  const int C = a.C, K = a.K, kcap = a.kcap;
+  const int ntr = C * C, ndb = K * C;
+  for (int i = blockIdx.x * kMT + threadIdx.x; i < ntr + ndb; i += gridDim.x * kMT) {
+    if (i < ntr) {
+      double s = 0.0;
+      for (int b = 0; b < a.B; ++b) {
+        double sb = 0.0;
+        const double* p = a.part_tr + (size_t)b * a.nchunk * ntr + i;
+        for (int ch = 0; ch < a.nchunk; ++ch) sb += p[(size_t)ch * ntr];
+        s = fma((double)a.grad_output[b], sb, s);
+      }
+      grad_tr[i] = (float)(exp((double)a.tr[i]) * s);
+    } else {
+      const int j = (i - ntr) / C, c = (i - ntr) % C;
+      // duration index j collects k with min(k, K-1) == j
+      const int k = (K == 1) ? 1 : j;
+      double s = 0.0;
+      if (k >= 1 && k <= kcap) {
+        for (int b = 0; b < a.B; ++b) {
+          double sb = 0.0;
+          const double* p = a.part_db + (size_t)b * a.nsplit * kcap * C + (size_t)(k - 1) * C + c;
+          for (int sp = 0; sp < a.nsplit; ++sp) sb += p[(size_t)sp * kcap * C];
+          s = fma((double)a.grad_output[b], sb, s);
+        }
+        s *= exp((double)a.db[(size_t)j * C + c]);
+      }
+      grad_db[i - ntr] = (float)s;
+    }
+  }
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
+}
+
+}  // namespace
+
+LMargPlan lmarg_plan(int B, int T, int K, int C) {
+  LMargPlan p{};
+  const int kcap = K > 1 ? K - 1 : 1;
+  const int target = 2 * 148;
+  // transition partials
+  const int pb = C <= 32 ? 32 : 64;
+  const int npb = (C + pb - 1) / pb;
+  int nch = (target + B * npb * npb - 1) / (B * npb * npb);
+  const int maxch = (T + 255) / 256;
+  nch = nch < 1 ? 1 : (nch > maxch ? maxch : nch);
+  if (nch < 1) nch = 1;
+  p.nchunk = nch;
+  // duration partials: label group sized so staging fits and items <= 8/thread
+  const size_t budget = 160 * 1024;
+  int cg = (int)(budget / (8 * (size_t)(2 * kTT + kcap + 16)));
+  const int nkg = (kcap + 7) / 8;
+  const int cg_items = (kMaxItems * kMT) / nkg;
+  if (cg > cg_items) cg = cg_items;
+  if (cg > C) cg = C;
+  if (cg < 1) cg = 1;
+  p.cg = cg;
+  p.ncg = (C + cg - 1) / cg;
+  int nsp = (target + B * p.ncg - 1) / (B * p.ncg);
+  const int maxsp = (T + kTT - 1) / kTT;
+  nsp = nsp < 1 ? 1 : (nsp > maxsp ? maxsp : nsp);
+  p.nsplit = nsp;
+  p.db_smem = 8 * ((size_t)kTT * cg + (size_t)(kTT + kcap + 16) * cg + cg);
+  p.ok = (size_t)cg * nkg <= (size_t)kMaxItems * kMT && p.db_smem <= 227 * 1024;
+  return p;
+}
+
+cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cudaStream_t s) {
+  if (a.B <= 0) return cudaSuccess;
+  const LMargPlan p = lmarg_plan(a.B, a.T, a.K, a.C);
+  if (!p.ok || p.nchunk != a.nchunk || p.nsplit != a.nsplit || p.cg != a.cg)
+    return cudaErrorInvalidValue;
+  const size_t n = (size_t)a.B * (a.T + 1) * a.C;
+  int g = (int)((n + kMT - 1) / kMT);
+  const int gmax = sm_count() * 16;
+  if (g > gmax) g = gmax;
+  lmarg_pos_kernel<<<g, kMT, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (a.C <= 32) {
+    const int npb = (a.C + 31) / 32;
+    lmarg_tr_kernel<2><<<dim3(npb * npb, a.nchunk, a.B), kMT, 0, s>>>(a);
+  } else {
+    const int npb = (a.C + 63) / 64;
+    lmarg_tr_kernel<4><<<dim3(npb * npb, a.nchunk, a.B), kMT, 0, s>>>(a);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(lmarg_db_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)p.db_smem);
+  if (e != cudaSuccess) return e;
+  lmarg_db_kernel<<<dim3(p.ncg, a.nsplit, a.B), kMT, p.db_smem, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int nout = a.C * a.C + a.K * a.C;
+  lmarg_reduce_kernel<<<(nout + kMT - 1) / kMT, kMT, 0, s>>>(a, grad_tr, grad_db);
+  return cudaGetLastError();
+}
+
+}  // namespace semicrf

@@ -14,7 +14,7 @@
 //  - The scratch holds the forward's prepared constants (the exponentiated
 //    transition and duration tables, about 8*C*C + 8*(K+16)*C bytes).  It is
 //    kNoallocScratchBytes (1 MiB) large.  Every shape the scan accepts fits
-//    (the largest, C=256 with K=64, needs 675 KiB); a problem whose forward
+//    (the largest, at C=256, need under 700 KiB); a problem whose forward
 //    workspace (semicrf_forward_workspace_size) exceeds 1 MiB is rejected with
 //    SEMICRF_ERR_WORKSPACE before any CUDA call.
 //  - Nothing in the scratch has to start at zero: every byte the scan reads

@@ -107,7 +107,7 @@ struct ChainLaunch {
 // float64 linear-domain log-semiring chain (lchain.cu)
 struct LChainArgs {
   int mode;  // 0 = whole sequence, 1 = checkpoint segment (forward only)
-  int dir;   // 0 = forward (alpha), 1 = backward (beta + fused gradients)
+  int dir;   // 0 = forward (alpha), 1 = backward (beta)
   const float* cum;
   const float* ps;
   const float* pe;
@@ -125,24 +125,12 @@ struct LChainArgs {
   int nint;
   int sint;
   int write_saved;
-  // alpha tables written by the forward / the recompute: a = exp(alpha - n),
-  // A = exp(A - n), n per position, indexed by cum position t
+  // chain tables, indexed by cum position t: a = exp(x - n), A = exp(m - n)
+  // and the normaliser n per position (x = alpha, m = A for dir 0; x = G,
+  // m = beta for dir 1)
   double* a_tab;
   double* A_tab;
   double* n_tab;
-  // backward inputs
-  const double* in_a;
-  const double* in_A;
-  const double* in_n;
-  const double* logz_in;
-  const float* grad_output;
-  // backward outputs
-  float* grad_cum;
-  float* grad_ps;
-  float* grad_pe;
-  double* part_tr;  // (B, C*C) per-sequence, without exp(tr) and grad_output
-  double* part_db;  // (B, K*C) per-sequence, without grad_output
-  double* gws;      // per-CTA global scratch (lchain_gws_doubles_per_cta each)
 };
 struct LChainLaunch {
   int B, T, K, C;
@@ -154,16 +142,47 @@ struct LChainLaunch {
 };
 cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s);
 // warp-specialised variant for C <= 64, whole-sequence chains (mode 0) only
-cudaError_t launch_lchain_ws(const LChainLaunch& L, cudaStream_t s);
+cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s);
 bool lchain_ws_supported(int C, int K);
-size_t lchain_ws_gws_doubles_per_cta(int C, int K);
 bool lchain_supported(int C, int K);
 size_t lchain_saved_doubles(int C, int K);       // restart record per checkpoint
-size_t lchain_gws_doubles_per_cta(int C, int K);
-cudaError_t launch_lreduce(int B, int K, int C, const double* part_tr, const double* part_db,
-                           const float* grad_output, const float* tr, float* grad_tr,
-                           float* grad_db, cudaStream_t s);
 constexpr int kPrepRowsExtra = 17;  // dbl/dbe rows = kcap + kPrepRowsExtra
+
+// log-semiring gradients from the alpha and beta chain tables (lmarg.cu)
+struct LMargArgs {
+  int B, T, K, C, kcap;
+  const float* cum;
+  const float* ps;
+  const float* pe;
+  const float* tr;  // (C, C)
+  const float* db;  // (K, C)
+  const int64_t* lengths;
+  const double* logz;
+  const float* grad_output;
+  const double* xa;  // alpha chain: exp(alpha - xn), exp(A - xn), xn
+  const double* xA;
+  const double* xn;
+  const double* ya;  // beta chain: exp(G - yn), exp(beta - yn), yn
+  const double* yA;
+  const double* yn;
+  float* grad_cum;
+  float* grad_ps;
+  float* grad_pe;
+  double* la;       // (B, T+1, C) scratch: log start factor
+  double* lb;       // (B, T+1, C) scratch: log end factor
+  double* part_tr;  // (B, nchunk, C*C)
+  int nchunk;
+  double* part_db;  // (B, nsplit, kcap, C)
+  int nsplit;
+  int cg;           // labels per duration CTA
+};
+struct LMargPlan {
+  int nchunk, nsplit, cg, ncg;
+  size_t db_smem;
+  bool ok;
+};
+LMargPlan lmarg_plan(int B, int T, int K, int C);
+cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cudaStream_t s);
 
 // launchers (chain.cu)
 cudaError_t launch_prep(const float* tr, const float* db, int K, int C, int kcap, int P,

@@ -26,12 +26,14 @@ HAS_TRITON = True  # kept for API compatibility: the launcher names below exist
 class SemiCRFStreaming(torch.autograd.Function):
     """Streaming semi-CRF log-partition (or max score) with a checkpointed backward.
 
-    Forward: one CUDA chain per sequence keeps the O(K*C) ring on chip and
-    saves normalised ring checkpoints every S' (a multiple of the block size
-    >= S = max(K, sqrt(T*K))).  Backward: beta chains and alpha recomputes
-    between checkpoints run in one launch, then per-position marginals give
-    the gradients.  Shared-parameter gradients are sum_b grad_output[b] *
-    marginals_b (reference autograd.py:134-145).
+    Forward (log semiring): the alpha chain and the beta chain of every
+    sequence run side by side in one launch (one CTA per chain, the O(K*C)
+    ring on chip) and keep their float64 tables; when those tables would be
+    too large, the forward keeps normalised ring checkpoints every S' >= S =
+    max(K, sqrt(T*K)) instead and the backward recomputes alpha between them
+    and runs the beta chains.  Backward: every gradient is a parallel map or
+    reduction over the tables.  Shared-parameter gradients are
+    sum_b grad_output[b] * marginals_b (reference autograd.py:134-145).
     """
 
     @staticmethod
