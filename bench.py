@@ -203,6 +203,7 @@ def main():
     import torch.distributed as dist
 
     from torch_semimarkov_b200 import _lib, semi_crf_streaming_forward
+    from torch_semimarkov_b200.distributed import SharedGradReducer
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -218,7 +219,7 @@ def main():
     cum = cum_host.to(dev)
     lengths = lengths_h.to(dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    red = torch.empty(C * C + K * C + 1, dtype=torch.float32, device=dev)
+    reducer = SharedGradReducer(C, K, dev)
 
     def step(cum_in):
         cum_l = cum_in.detach().requires_grad_(True)
@@ -228,10 +229,9 @@ def main():
         loss = part.sum()
         loss.backward()
         if world > 1:
-            red[: C * C].copy_(tr_l.grad.flatten())
-            red[C * C: C * C + K * C].copy_(db_l.grad.flatten())
-            red[-1:].copy_(loss.detach().view(1))
-            dist.all_reduce(red)
+            # the step's one collective: [grad_tr | grad_db | loss] summed over ranks
+            gt, gd, lsum = reducer(tr_l.grad, db_l.grad, loss)
+            return lsum, gt, gd
         return loss, tr_l.grad, db_l.grad
 
     def barrier():

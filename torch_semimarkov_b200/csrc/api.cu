@@ -142,7 +142,7 @@ struct LBwdLayout {
   Prepared pr;
   double *a_tab, *A_tab, *n_tab;  // SEMICRF_RECOMPUTE: alpha tables
   double *b_tab, *B_tab, *m_tab;  // SEMICRF_RECOMPUTE: beta tables
-  double *la, *lb, *part_tr, *part_db;
+  double *la, *lb, *maX, *mbY, *part_tr, *part_db;
   LMargPlan mp;
 };
 
@@ -162,6 +162,8 @@ LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
   w.mp = lmarg_plan((int)p->batch, (int)p->T, (int)p->K, (int)p->C);
   w.la = cv.take<double>(n);
   w.lb = cv.take<double>(n);
+  w.maX = cv.take<double>((size_t)p->batch * w.mp.nblk * p->C);
+  w.mbY = cv.take<double>((size_t)p->batch * w.mp.nblk * p->C);
   w.part_tr = cv.take<double>((size_t)p->batch * w.mp.nchunk * p->C * p->C);
   w.part_db = cv.take<double>((size_t)p->batch * w.mp.nsplit * kcap_of(p->K) * p->C);
   return w;
@@ -458,6 +460,8 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     m.grad_pe = p->proj_end ? grad_proj_end : nullptr;
     m.la = w.la;
     m.lb = w.lb;
+    m.maX = w.maX;
+    m.mbY = w.mbY;
     m.part_tr = w.part_tr;
     m.nchunk = w.mp.nchunk;
     m.part_db = w.part_db;

@@ -28,7 +28,7 @@ namespace semicrf {
 namespace {
 
 constexpr int kMT = 256;
-constexpr int kTT = 64;  // targets per correlation tile
+constexpr int kTT = 64;  // positions per block (targets per correlation tile)
 
 __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
   const long long l = lengths[b];
@@ -144,74 +144,107 @@ __global__ void __launch_bounds__(kMT) lmarg_tr_kernel(const LMargArgs a) {
     }
 }
 
-// ---- duration partials: part_db[b][split][k-1][c] = sum_t X[t,c] Y[t+k,c] ----
-// CTA = (label group, split, sequence).  Per tile of kTT targets t0.. and
-// label c, r = max_t la[t,c] over the tile:
-//     X[i] = exp(la[t0+i] - r),   Y[j] = exp(lb[t0+1+j] + r - logZ)
-// so X <= 1 and X[i] Y[i+k-1] = P(t0+i -> t0+i+k) / exp(db).  An item is a
-// (label, 8 consecutive k) pair; its window over Y slides by one per target.
-constexpr int kMaxItems = 8;  // items per thread (host guarantees the bound)
+// ---- block-relative linear factors ----------------------------------------
+// Targets and sources are grouped in blocks of kTT positions.  Per (block,
+// label) with m = max over the block of the log factor, the tables are
+// rewritten in place as exp(l - m) (0 where l = -inf) and m is kept:
+//     la -> Xlin, maX;   lb -> Ylin, mbY.
+__global__ void __launch_bounds__(kMT) lmarg_blk_kernel(const LMargArgs a) {
+  const int C = a.C, T = a.T;
+  const int nblk = (T + 1 + kTT - 1) / kTT;
+  const size_t total = (size_t)a.B * nblk * C;
+  for (size_t i = (size_t)blockIdx.x * kMT + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * kMT) {
+    const int c = (int)(i % C);
+    const int blk = (int)((i / C) % nblk);
+    const int b = (int)(i / ((size_t)C * nblk));
+    const int t0 = blk * kTT, t1 = min(t0 + kTT, T + 1);
+    double* la = a.la + ((size_t)b * (T + 1)) * C + c;
+    double* lb = a.lb + ((size_t)b * (T + 1)) * C + c;
+    double ma = -INFINITY, mb = -INFINITY;
+    for (int t = t0; t < t1; ++t) {
+      ma = fmax(ma, la[(size_t)t * C]);
+      mb = fmax(mb, lb[(size_t)t * C]);
+    }
+    for (int t = t0; t < t1; ++t) {
+      const double x = la[(size_t)t * C], y = lb[(size_t)t * C];
+      la[(size_t)t * C] = (x > -INFINITY) ? exp(x - ma) : 0.0;
+      lb[(size_t)t * C] = (y > -INFINITY) ? exp(y - mb) : 0.0;
+    }
+    a.maX[i] = ma;
+    a.mbY[i] = mb;
+  }
+}
 
-__global__ void __launch_bounds__(kMT) lmarg_db_kernel(const LMargArgs a) {
+// ---- duration partials: part_db[b][split][k-1][c] = sum_t X[t,c] Y[t+k,c] ----
+// CTA = (label group, split, sequence); a split is a run of whole target
+// blocks.  For the target block tau (targets t0 = kTT*tau ..) and label c:
+//     X[i] = Xlin[t0+i],   Y[j] = Ylin[s] * exp(mbY[blk(s)] + maX[tau] - logZ)
+// for sources s = t0+1+j, so X[i] Y[i+k-1] = P(t0+i -> t0+i+k) / exp(db);
+// X <= 1 and Y is bounded by a segment marginal, so both stay in range, and a
+// source that underflows in Ylin is negligible beside its block's maximum.
+// An item is a (label, 8 consecutive k) pair: MI items per thread.
+template <int MI>
+__global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LMargArgs a) {
   extern __shared__ __align__(16) unsigned char smraw[];
   const int C = a.C, T = a.T, kcap = a.kcap, CG = a.cg;
   const int g0 = blockIdx.x * CG;
   const int cgn = min(CG, C - g0);
   const int sp = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x;
+  const int nblk = (T + 1 + kTT - 1) / kTT;
   // Y rows read by a tile: up to kTT - 8 + (kcap + 7) - 1 + 15 < kTT + kcap + 16
   const int ny = kTT + kcap + 16;
+  const int nq = ny / kTT + 2;  // source blocks a tile touches
   double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
   double* Y = X + (size_t)kTT * CG;               // [ny][CG]
-  double* rr = Y + (size_t)ny * CG;               // [CG]
+  double* G = Y + (size_t)ny * CG;                // [nq][CG]
   const int nkg = (kcap + 7) / 8;
   const int nitems = cgn * nkg;
   const int Lb = seq_len(a.lengths, b, T);
-  const int per = (Lb + a.nsplit - 1) / (a.nsplit > 0 ? a.nsplit : 1);
-  const int t_lo = sp * per;
-  const int t_hi = min(t_lo + per, Lb);  // targets t < Lb start a segment
+  const int ntile = (Lb + kTT - 1) / kTT;  // target blocks (targets t < Lb)
+  const int per = (ntile + a.nsplit - 1) / a.nsplit;
+  const int tau_lo = sp * per, tau_hi = min(tau_lo + per, ntile);
   const double lz = a.logz[b];
   const size_t rowb = (size_t)b * (T + 1);
-  double acc[kMaxItems][8];
+  const double* mx_b = a.maX + (size_t)b * nblk * C + g0;
+  const double* my_b = a.mbY + (size_t)b * nblk * C + g0;
+  double acc[MI][8];
 #pragma unroll
-  for (int j = 0; j < kMaxItems; ++j)
+  for (int j = 0; j < MI; ++j)
 #pragma unroll
     for (int q = 0; q < 8; ++q) acc[j][q] = 0.0;
 
-  for (int t0 = t_lo; t0 < t_hi; t0 += kTT) {
-    const int n = min(kTT, t_hi - t0);
+  for (int tau = tau_lo; tau < tau_hi; ++tau) {
+    const int t0 = tau * kTT;
+    const int n = min(kTT, Lb - t0);
     __syncthreads();
-    // per-label reference
-    for (int cc = tid; cc < cgn; cc += kMT) {
-      double r = -INFINITY;
-      for (int i = 0; i < n; ++i) r = fmax(r, a.la[(rowb + t0 + i) * C + g0 + cc]);
-      rr[cc] = r;
+    for (int e = tid; e < nq * cgn; e += kMT) {
+      const int q = e / cgn, cc = e % cgn;
+      const int beta = tau + q;
+      double gv = 0.0;
+      if (beta < nblk) {
+        const double rx = mx_b[(size_t)tau * C + cc], ry = my_b[(size_t)beta * C + cc];
+        if (rx > -INFINITY && ry > -INFINITY) gv = exp(fmin(ry + rx - lz, 700.0));
+      }
+      G[q * CG + cc] = gv;
     }
-    __syncthreads();
     for (int e = tid; e < kTT * cgn; e += kMT) {
       const int i = e / cgn, cc = e % cgn;
-      const double r = rr[cc];
-      double x = 0.0;
-      if (i < n && r > -INFINITY) {
-        const double l = a.la[(rowb + t0 + i) * C + g0 + cc];
-        x = (l > -INFINITY) ? exp(l - r) : 0.0;
-      }
-      X[i * CG + cc] = x;
+      X[i * CG + cc] = (i < n) ? a.la[(rowb + t0 + i) * C + g0 + cc] : 0.0;
     }
+    __syncthreads();
     for (int e = tid; e < ny * cgn; e += kMT) {
       const int j = e / cgn, cc = e % cgn;
       const int s = t0 + 1 + j;
-      const double r = rr[cc];
       double y = 0.0;
-      if (s <= Lb && j < n - 1 + kcap && r > -INFINITY) {
-        const double l = a.lb[(rowb + s) * C + g0 + cc];
-        y = (l > -INFINITY) ? exp(fmin(l + r - lz, 700.0)) : 0.0;
-      }
+      if (s <= Lb && j < n - 1 + kcap)
+        y = a.lb[(rowb + s) * C + g0 + cc] * G[(s / kTT - tau) * CG + cc];
       Y[j * CG + cc] = y;
     }
     __syncthreads();
 #pragma unroll
-    for (int jt = 0; jt < kMaxItems; ++jt) {
+    for (int jt = 0; jt < MI; ++jt) {
       const int it = tid + jt * kMT;
       if (it < nitems) {
         const int cc = it % cgn, kg = it / cgn;
@@ -235,7 +268,7 @@ __global__ void __launch_bounds__(kMT) lmarg_db_kernel(const LMargArgs a) {
   }
   double* out = a.part_db + ((size_t)b * a.nsplit + sp) * (size_t)kcap * C;
 #pragma unroll
-  for (int jt = 0; jt < kMaxItems; ++jt) {
+  for (int jt = 0; jt < MI; ++jt) {
     const int it = tid + jt * kMT;
     if (it < nitems) {
       const int cc = it % cgn, kg = it / cgn;
@@ -249,35 +282,45 @@ __global__ void __launch_bounds__(kMT) lmarg_db_kernel(const LMargArgs a) {
 }
 
 // ---- fixed-order reduction over sequences and chunks -------------------------
+// One warp per output: lane l sums the terms (b, chunk) = l, l+32, ... in
+// order, then a fixed shuffle tree adds the lanes.
 __global__ void __launch_bounds__(kMT) lmarg_reduce_kernel(const LMargArgs a, float* grad_tr,
                                                             float* grad_db) {
   const int C = a.C, K = a.K, kcap = a.kcap;
   const int ntr = C * C, ndb = K * C;
-  for (int i = blockIdx.x * kMT + threadIdx.x; i < ntr + ndb; i += gridDim.x * kMT) {
-    if (i < ntr) {
-      double s = 0.0;
-      for (int b = 0; b < a.B; ++b) {
-        double sb = 0.0;
-        const double* p = a.part_tr + (size_t)b * a.nchunk * ntr + i;
-        for (int ch = 0; ch < a.nchunk; ++ch) sb += p[(size_t)ch * ntr];
-        s = fma((double)a.grad_output[b], sb, s);
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * kMT + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * kMT) >> 5;
+  for (int o = warp; o < ntr + ndb; o += nwarps) {
+    double s = 0.0;
+    if (o < ntr) {
+      const int nterm = a.B * a.nchunk;
+      for (int q = lane; q < nterm; q += 32) {
+        const int b = q / a.nchunk;
+        s = fma((double)a.grad_output[b], a.part_tr[(size_t)q * ntr + o], s);
       }
-      grad_tr[i] = (float)(exp((double)a.tr[i]) * s);
     } else {
-      const int j = (i - ntr) / C, c = (i - ntr) % C;
+      const int j = (o - ntr) / C, c = (o - ntr) % C;
       // duration index j collects k with min(k, K-1) == j
       const int k = (K == 1) ? 1 : j;
-      double s = 0.0;
       if (k >= 1 && k <= kcap) {
-        for (int b = 0; b < a.B; ++b) {
-          double sb = 0.0;
-          const double* p = a.part_db + (size_t)b * a.nsplit * kcap * C + (size_t)(k - 1) * C + c;
-          for (int sp = 0; sp < a.nsplit; ++sp) sb += p[(size_t)sp * kcap * C];
-          s = fma((double)a.grad_output[b], sb, s);
+        const int nterm = a.B * a.nsplit;
+        for (int q = lane; q < nterm; q += 32) {
+          const int b = q / a.nsplit;
+          s = fma((double)a.grad_output[b],
+                  a.part_db[(size_t)q * kcap * C + (size_t)(k - 1) * C + c], s);
         }
-        s *= exp((double)a.db[(size_t)j * C + c]);
       }
-      grad_db[i - ntr] = (float)s;
+    }
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) s += __shfl_xor_sync(0xffffffffu, s, w);
+    if (lane == 0) {
+      if (o < ntr) {
+        grad_tr[o] = (float)(exp((double)a.tr[o]) * s);
+      } else {
+        const int j = (o - ntr) / C, c = (o - ntr) % C;
+        grad_db[o - ntr] = (float)(s * exp((double)a.db[(size_t)j * C + c]));
+      }
     }
   }
 }
@@ -298,31 +341,46 @@ int sm_count() {
 LMargPlan lmarg_plan(int B, int T, int K, int C) {
   LMargPlan p{};
   const int kcap = K > 1 ? K - 1 : 1;
-  const int target = 2 * 148;
+  const int sms = 148;
   // transition partials
   const int pb = C <= 32 ? 32 : 64;
   const int npb = (C + pb - 1) / pb;
-  int nch = (target + B * npb * npb - 1) / (B * npb * npb);
+  int nch = (2 * sms + B * npb * npb - 1) / (B * npb * npb);
   const int maxch = (T + 255) / 256;
-  nch = nch < 1 ? 1 : (nch > maxch ? maxch : nch);
+  if (nch > maxch) nch = maxch;
   if (nch < 1) nch = 1;
   p.nchunk = nch;
-  // duration partials: label group sized so staging fits and items <= 8/thread
-  const size_t budget = 160 * 1024;
-  int cg = (int)(budget / (8 * (size_t)(2 * kTT + kcap + 16)));
+  // duration partials: label group sized so that the staging fits two CTAs
+  // per SM with 4 items per thread where possible, else one CTA with 8
+  const int ny = kTT + kcap + 16;
+  const int nq = ny / kTT + 2;
+  const size_t per_label = 8 * (size_t)(kTT + ny + nq);
   const int nkg = (kcap + 7) / 8;
-  const int cg_items = (kMaxItems * kMT) / nkg;
-  if (cg > cg_items) cg = cg_items;
-  if (cg > C) cg = C;
+  auto fit = [&](size_t smem, int items) {
+    long cg = (long)(smem / per_label);
+    const long ci = (long)items * kMT / nkg;
+    if (cg > ci) cg = ci;
+    if (cg > C) cg = C;
+    return (int)cg;
+  };
+  int cg = fit(110 * 1024, 4);
+  p.mi = 4;
+  if (cg < 1 || (cg < C && fit(200 * 1024, 8) >= 2 * cg)) {
+    cg = fit(200 * 1024, 8);
+    p.mi = 8;
+  }
   if (cg < 1) cg = 1;
   p.cg = cg;
   p.ncg = (C + cg - 1) / cg;
+  const int target = (p.mi == 4 ? 4 : 2) * sms;
   int nsp = (target + B * p.ncg - 1) / (B * p.ncg);
   const int maxsp = (T + kTT - 1) / kTT;
-  nsp = nsp < 1 ? 1 : (nsp > maxsp ? maxsp : nsp);
+  if (nsp > maxsp) nsp = maxsp;
+  if (nsp < 1) nsp = 1;
   p.nsplit = nsp;
-  p.db_smem = 8 * ((size_t)kTT * cg + (size_t)(kTT + kcap + 16) * cg + cg);
-  p.ok = (size_t)cg * nkg <= (size_t)kMaxItems * kMT && p.db_smem <= 227 * 1024;
+  p.nblk = (T + 1 + kTT - 1) / kTT;
+  p.db_smem = per_label * cg;
+  p.ok = (size_t)cg * nkg <= (size_t)p.mi * kMT && p.db_smem <= 227 * 1024;
   return p;
 }
 
@@ -331,12 +389,18 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   const LMargPlan p = lmarg_plan(a.B, a.T, a.K, a.C);
   if (!p.ok || p.nchunk != a.nchunk || p.nsplit != a.nsplit || p.cg != a.cg)
     return cudaErrorInvalidValue;
+  const int gmax = sm_count() * 16;
   const size_t n = (size_t)a.B * (a.T + 1) * a.C;
   int g = (int)((n + kMT - 1) / kMT);
-  const int gmax = sm_count() * 16;
   if (g > gmax) g = gmax;
   lmarg_pos_kernel<<<g, kMT, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t nb = (size_t)a.B * p.nblk * a.C;
+  g = (int)((nb + kMT - 1) / kMT);
+  if (g > gmax) g = gmax;
+  lmarg_blk_kernel<<<g, kMT, 0, s>>>(a);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (a.C <= 32) {
     const int npb = (a.C + 31) / 32;
@@ -347,14 +411,24 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(lmarg_db_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)p.db_smem);
-  if (e != cudaSuccess) return e;
-  lmarg_db_kernel<<<dim3(p.ncg, a.nsplit, a.B), kMT, p.db_smem, s>>>(a);
+  const dim3 gdb(p.ncg, a.nsplit, a.B);
+  if (p.mi == 4) {
+    e = cudaFuncSetAttribute(lmarg_db_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)p.db_smem);
+    if (e != cudaSuccess) return e;
+    lmarg_db_kernel<4><<<gdb, kMT, p.db_smem, s>>>(a);
+  } else {
+    e = cudaFuncSetAttribute(lmarg_db_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)p.db_smem);
+    if (e != cudaSuccess) return e;
+    lmarg_db_kernel<8><<<gdb, kMT, p.db_smem, s>>>(a);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int nout = a.C * a.C + a.K * a.C;
-  lmarg_reduce_kernel<<<(nout + kMT - 1) / kMT, kMT, 0, s>>>(a, grad_tr, grad_db);
+  g = (nout * 32 + kMT - 1) / kMT;
+  if (g > gmax) g = gmax;
+  lmarg_reduce_kernel<<<g, kMT, 0, s>>>(a, grad_tr, grad_db);
   return cudaGetLastError();
 }
 

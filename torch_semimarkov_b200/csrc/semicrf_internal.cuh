@@ -168,8 +168,10 @@ struct LMargArgs {
   float* grad_cum;
   float* grad_ps;
   float* grad_pe;
-  double* la;       // (B, T+1, C) scratch: log start factor
-  double* lb;       // (B, T+1, C) scratch: log end factor
+  double* la;       // (B, T+1, C) scratch: log start factor, then block-relative linear
+  double* lb;       // (B, T+1, C) scratch: log end factor, then block-relative linear
+  double* maX;      // (B, nblk, C) block maxima of la
+  double* mbY;      // (B, nblk, C) block maxima of lb
   double* part_tr;  // (B, nchunk, C*C)
   int nchunk;
   double* part_db;  // (B, nsplit, kcap, C)
@@ -177,7 +179,7 @@ struct LMargArgs {
   int cg;           // labels per duration CTA
 };
 struct LMargPlan {
-  int nchunk, nsplit, cg, ncg;
+  int nchunk, nsplit, cg, ncg, mi, nblk;
   size_t db_smem;
   bool ok;
 };
