@@ -41,7 +41,7 @@ UNIT = "positions/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -78,7 +78,7 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -330,11 +330,13 @@ def main():
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    # algorithmic bytes of one forward launch: cum_scores read by each of the
-    # two chains, their float64 tables written (2C+1 doubles per position and
-    # chain), log Z and the partition written
+    # algorithmic bytes of one forward launch over the actual lengths (rows
+    # 0..L of each sequence): cum_scores read by each of the two chains, their
+    # float64 tables written (2C+1 doubles per row and chain), log Z and the
+    # partition written
     lsum = int(lengths_h.sum())
-    bytes_fwd = 2 * 4 * B * (T + 1) * C + 2 * 8 * B * (T + 1) * (2 * C + 1) + B * (4 + 8)
+    rows = lsum + B
+    bytes_fwd = 2 * (4 * C + 8 * (2 * C + 1)) * rows + B * (4 + 8)
     achieved = bytes_fwd / t_fwd / 1e9
     # float64 FMAs of the factorised recurrence per forward launch: per
     # position and chain, the C x C mat-vec and the (K-1) x C duration sums
@@ -366,8 +368,8 @@ def main():
                              "ns_per_position_step": t_fwd / T * 1e9,
                              "ctas": 2 * B, "sms": torch.cuda.get_device_properties(dev)
                              .multi_processor_count},
-        # per step: forward = prep (2) + chains (1); backward = pos, tr, db, reduce
-        "gpu_launches": 7 * args.steps,
+        # per step: forward = prep (2) + chains (1); backward = pos, blk, tr, db, reduce
+        "gpu_launches": 8 * args.steps,
         "clocks": clocks,
     }
     if viterbi:
