@@ -334,3 +334,40 @@ def test_decode_batch_vs_oracle(oracle):
         seg_sum = float(sv[b, : ns[b]].sum())
         assert abs(seg_sum - sc64[b]) <= 1e-5 * abs(sc64[b]) + 1e-3
     assert same >= B - 1, f"only {same}/{B} segmentations identical"
+
+
+# score-only max-semiring forward (no autograd): the warp chain for C <= 32 and
+# K-1 <= 64, the block chain otherwise
+MAX_FWD_CASES = [
+    # B, T, K, C, gen, proj
+    (4, 300, 33, 16, "cfg5", None),
+    (3, 200, 9, 5, "default", "both"),
+    (2, 100, 1, 3, "default", None),
+    (2, 150, 65, 32, "default", None),
+    (3, 120, 100, 24, "default", None),
+    (2, 90, 12, 40, "default", None),
+]
+
+
+@pytest.mark.parametrize("case", MAX_FWD_CASES)
+def test_max_forward_no_grad_vs_oracle(case, oracle):
+    from inputs import make_streaming_inputs
+
+    from torch_semimarkov_b200 import semi_crf_streaming_forward
+
+    B, T, K, C, gen, proj = case
+    dev = _dev()
+    inp = make_streaming_inputs(B, T, K, C, seed=7 + T + K + C, gen=gen, proj=proj)
+    rng = np.random.default_rng(K)
+    lengths = np.concatenate([[T], rng.integers(0, T + 1, size=B - 1)])
+    np_in = {k: (None if v is None else v.numpy()) for k, v in inp.items()}
+    ref, _, _ = oracle.forward(np_in["cum_scores"], np_in["transition"], np_in["duration_bias"],
+                               lengths, K, "max", np_in["proj_start"], np_in["proj_end"],
+                               threads=4)
+    with torch.no_grad():
+        got = semi_crf_streaming_forward(
+            inp["cum_scores"].to(dev), inp["transition"].to(dev), inp["duration_bias"].to(dev),
+            torch.as_tensor(lengths).to(dev), K, semiring="max",
+            proj_start=None if inp["proj_start"] is None else inp["proj_start"].to(dev),
+            proj_end=None if inp["proj_end"] is None else inp["proj_end"].to(dev))
+    assert_close_rel(got.cpu().numpy(), ref, what="max score")

@@ -209,6 +209,7 @@ struct VitLayout {
   Prepared pr;
   int16_t* bp_k;
   uint8_t* bp_c;
+  uint16_t* bp;  // packed backpointers of the warp chain
   int* final_c;
 };
 
@@ -218,11 +219,27 @@ VitLayout carve_vit(Carver& cv, const semicrf_problem* p) {
   const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
   w.bp_k = cv.take<int16_t>(n);
   w.bp_c = cv.take<uint8_t>(n);
+  w.bp = cv.take<uint16_t>(n);
   w.final_c = cv.take<int>(p->batch);
   return w;
 }
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? SEMICRF_OK : SEMICRF_ERR_CUDA; }
+
+VChainArgs vchain_args(const semicrf_problem* p) {
+  VChainArgs v{};
+  v.B = (int)p->batch;
+  v.T = (int)p->T;
+  v.K = (int)p->K;
+  v.C = (int)p->C;
+  v.cum = p->cum_scores;
+  v.tr = p->transition;
+  v.db = p->duration_bias;
+  v.ps = p->proj_start;
+  v.pe = p->proj_end;
+  v.lengths = p->lengths;
+  return v;
+}
 
 }  // namespace
 
@@ -272,6 +289,13 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
   if (workspace_bytes < semicrf_forward_workspace_size(p) || !workspace)
     return SEMICRF_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->semiring == SEMICRF_MAX && !saved && !ring_checkpoints &&
+      vchain_supported((int)p->batch, (int)p->C, (int)p->K)) {
+    // score only: one warp per sequence, no prepared tables needed
+    VChainArgs v = vchain_args(p);
+    v.partition = partition;
+    return cuda_status(launch_vchain(v, s));
+  }
   Carver cv(workspace);
   Prepared pr = carve_prep(cv, (int)p->C, (int)p->K);
   cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
@@ -558,8 +582,35 @@ int semicrf_viterbi(const semicrf_problem* p, int64_t max_traceback_length, floa
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   Carver cv(workspace);
   VitLayout w = carve_vit(cv, p);
-  cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
-                              kcap_of(p->K), kP, SEMICRF_MAX, w.pr, s);
+  cudaError_t e;
+  if (vchain_supported((int)p->batch, (int)p->C, (int)p->K)) {
+    // warp chain; the backtrace walks packed backpointers staged in shared
+    // memory when one sequence's fit, else the separate arrays in global memory
+    const bool packed = p->T <= 32767 && backtrace_packed_smem((int)p->T, (int)p->C) <= 200 * 1024;
+    VChainArgs v = vchain_args(p);
+    v.partition = scores;
+    v.final_c = w.final_c;
+    if (packed) {
+      v.bp = w.bp;
+    } else {
+      v.bp_k = w.bp_k;
+      v.bp_c = w.bp_c;
+    }
+    e = launch_vchain(v, s);
+    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+    if (packed)
+      return cuda_status(launch_backtrace_packed(
+          (int)p->batch, (int)p->T, (int)p->K, (int)p->C, p->cum_scores, p->transition,
+          p->duration_bias, p->lengths, max_traceback_length, w.bp, w.final_c, seg_start, seg_end,
+          seg_label, seg_score, nseg, s));
+    return cuda_status(launch_backtrace((int)p->batch, (int)p->T, (int)p->K, (int)p->C,
+                                        p->cum_scores, p->transition, p->duration_bias,
+                                        p->lengths, max_traceback_length, w.bp_k, w.bp_c,
+                                        w.final_c, seg_start, seg_end, seg_label, seg_score,
+                                        nseg, s));
+  }
+  e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C, kcap_of(p->K), kP,
+                  SEMICRF_MAX, w.pr, s);
   if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
   ChainLaunch L = base_launch(p, w.pr);
   ChainArgs a = base_args(p);

@@ -66,36 +66,41 @@ __device__ __forceinline__ void bar_sync(int id, int n) {
 }
 
 struct WsPlan {
-  int C, CP, K, kcap, LP, R, kx, nbr, nbulk, nsplit, nwt;
-  bool db_smem;
-  int o_ring, o_dbe, o_mx, o_dbmax, o_colmax, o_wring, o_lend, o_nring, o_ca, o_far, o_g,
-      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm;
+  int C, Cs, CP, K, kcap, LP, R, NR, kx, nbr, nbulk, np, nsplit, nwt;
+  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_wring, o_lend, o_nring, o_ca, o_far, o_g,
+      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast;
   int bytes;
 };
 
-__host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP, bool db_smem) {
+// Shared-memory layout.  The source ring has R = NR*LP slots (at least
+// kcap + 2*LP) of Cs = C rounded up to even labels: position u lives in slot
+// (u - 1) mod R, so every block of LP sources occupies LP consecutive slots
+// and a label pair is one 16-byte load.
+__host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP) {
   p.C = C;
+  p.Cs = C + (C & 1);
   p.CP = CP;
   p.K = K;
   p.kcap = K > 1 ? K - 1 : 1;
   p.LP = LP;
-  p.R = p.kcap + 2 * LP;
+  p.NR = (p.kcap + 2 * LP + LP - 1) / LP;
+  p.R = p.NR * LP;
   p.kx = p.kcap + kPrepRowsExtra;
-  int nbr = (p.R + LP - 1) / LP + 4;  // blocks whose frame factors are kept (power of 2)
+  int nbr = p.NR + 4;  // blocks whose frame factors are kept (power of 2)
   p.nbr = 1;
   while (p.nbr < nbr) p.nbr <<= 1;
   p.nbulk = kWsThreads - 2 * CP;  // warps sharing a sub-partition with a serial warp idle
-  p.nsplit = p.nbulk / C > 0 ? p.nbulk / C : 1;
-  p.nwt = p.nbr;
-  p.db_smem = db_smem;
+  p.np = p.Cs / 2;
+  p.nsplit = p.nbulk / p.np > 0 ? p.nbulk / p.np : 1;
+  p.nwt = (p.kcap + LP - 1) / LP + 4;  // source blocks a k-window reaches, plus margin
   int o = 0;
   auto take = [&](int n) {
     const int r = o;
     o += (n + 15) & ~15;
     return r;
   };
-  p.o_ring = take(8 * p.R * C);
-  p.o_dbe = db_smem ? take(4 * p.kx * C) : -1;
+  p.o_ring = take(8 * p.R * p.Cs);
+  p.o_dbd = take(8 * p.kx * p.Cs);  // Db = exp(db - dbmax) as doubles
   p.o_mx = take(4 * C * C);
   p.o_dbmax = take(8 * CP);
   p.o_colmax = take(8 * CP);
@@ -107,12 +112,13 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP,
   p.o_g = take(8 * 2 * LP * CP);
   p.o_h = take(8 * 2 * LP * CP);
   p.o_wprev = take(8 * 2 * CP);
-  p.o_part = take(8 * p.nsplit * LP * C);
+  p.o_part = take(8 * p.nsplit * LP * p.Cs);
   p.o_abuf = take(8 * CP);
   p.o_wt = take(8 * 2 * p.nwt * CP);  // W tables of the last two prepared blocks
   p.o_misc = take(8 * 16);
   p.o_edb = take(8 * CP);
   p.o_ecm = take(8 * CP);
+  p.o_alast = take(8 * 2 * CP);  // state at the end of the last two blocks (scale)
   p.bytes = o;
 }
 
@@ -120,10 +126,7 @@ __host__ __device__ inline int ws_cp(int C) { return C <= 32 ? 32 : 64; }
 
 __host__ __device__ inline bool ws_choose(WsPlan& p, int C, int K) {
   if (C > 64) return false;
-  const int CP = ws_cp(C);
-  ws_make(p, C, K, CP, 8, true);
-  if ((size_t)p.bytes <= kWsSmemMax) return true;
-  ws_make(p, C, K, CP, 8, false);
+  ws_make(p, C, K, ws_cp(C), 8);
   return (size_t)p.bytes <= kWsSmemMax;
 }
 
@@ -165,10 +168,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 
   WsPlan pl;
   ws_choose(pl, C, K);
-  const int kcap = pl.kcap, R = pl.R, NBR = pl.nbr;
-  double* ring = reinterpret_cast<double*>(smraw + pl.o_ring);
-  float* dbe_s = pl.db_smem ? reinterpret_cast<float*>(smraw + pl.o_dbe) : nullptr;
-  const float* dbe = pl.db_smem ? dbe_s : L.dbe;
+  const int kcap = pl.kcap, R = pl.R, NR = pl.NR, NBR = pl.nbr, Cs = pl.Cs;
+  double* ring = reinterpret_cast<double*>(smraw + pl.o_ring);  // [R][Cs]
+  double* dbd = reinterpret_cast<double*>(smraw + pl.o_dbd);    // [kx][Cs]
   float* mx = reinterpret_cast<float*>(smraw + pl.o_mx);
   double* dbmax = reinterpret_cast<double*>(smraw + pl.o_dbmax);
   double* colmax = reinterpret_cast<double*>(smraw + pl.o_colmax);
@@ -188,6 +190,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* misc = reinterpret_cast<double*>(smraw + pl.o_misc);
   double* edb = reinterpret_cast<double*>(smraw + pl.o_edb);  // exp(dbmax)
   double* ecm = reinterpret_cast<double*>(smraw + pl.o_ecm);  // exp(colmax)
+  double* alast = reinterpret_cast<double*>(smraw + pl.o_alast);  // [2][CP]
   auto lidx = [&](int gamma) { return (gamma + NBR) & (NBR - 1); };  // gamma >= -NBR
 
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
@@ -214,9 +217,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     ecm[i] = i < C ? exp((double)A.colmax[i]) : 0.0;
   }
   for (int i = tid; i < C * C; i += NT) mx[i] = A.mx[i];
-  if (dbe_s)
-    for (int i = tid; i < pl.kx * C; i += NT) dbe_s[i] = L.dbe[i];
-  for (int i = tid; i < R * C; i += NT) ring[i] = 0.0;
+  for (int i = tid; i < pl.kx * Cs; i += NT) {
+    const int k = i / Cs, cc = i % Cs;
+    dbd[i] = cc < C ? (double)L.dbe[k * C + cc] : 0.0;
+  }
+  for (int i = tid; i < R * Cs; i += NT) ring[i] = 0.0;
   __syncthreads();
 
   const int c = tid;  // serial lane label
@@ -242,7 +247,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     if (cv) {
       const double e0 = ym0 * exp(colmax[c] + soff_at(0, c));
-      ring[0 * C + c] = e0;  // slot of position 0
+      ring[(R - 1) * Cs + c] = e0;  // slot of position 0
       const int t0 = cpos(0);
       if (atab_b) atab_b[(size_t)t0 * C + c] = a0;
       if (Atab_b) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
@@ -263,12 +268,44 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     // =====================================================================
     // bulk warps
     // =====================================================================
+    // This thread's (target, label) elements of a block for the g/h step,
+    // fixed for the whole chain, and their cum values prefetched one block
+    // ahead so that no global-load latency sits inside prepare().
+    constexpr int kMaxE = (LP * CP + NBT - 1) / NBT;
+    int e_i[kMaxE], e_c[kMaxE];
+    double pre[kMaxE];
+#pragma unroll
+    for (int r = 0; r < kMaxE; ++r) {
+      const int w = btid + r * NBT;
+      e_i[r] = (w < LP * C) ? w / C : -1;
+      e_c[r] = (w < LP * C) ? w % C : 0;
+      pre[r] = 0.0;
+    }
+    auto prefetch_cum = [&](int tau) {
+      const int u0 = u_begin + 1 + tau * LP;
+#pragma unroll
+      for (int r = 0; r < kMaxE; ++r)
+        pre[r] = (e_i[r] >= 0 && u0 + e_i[r] <= u_end) ? cumd(u0 + e_i[r], e_c[r]) : 0.0;
+    };
+    // frame-table entries this thread updates: label wc, blocks q = wq0 + m*wqs
+    const int QW = min(NWT, (kcap + LP - 1) / LP + 4);  // blocks a k-window reaches
+    const int wc = btid % C, wq0 = btid / C, wqs = NBT / C > 0 ? NBT / C : 1;
+    const bool wact = btid < wqs * C;
+
     // prepare(tau): frame, factors and far sums of block tau into buffer tau&1
     auto prepare = [&](int tau) {
       const int bf = tau & 1;
       const int u0 = u_begin + 1 + tau * LP;
       const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
-      // normaliser prediction from the scales measured two blocks back
+      // scale at the end of block tau-2 (the serial warp left its state in
+      // alast), then the normaliser prediction for this block
+      if (tau >= 2 && btid < 32) {
+        double m = 0.0;
+        for (int c2 = btid; c2 < C; c2 += 32) m = fmax(m, alast[((tau - 2) & 1) * CP + c2]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (btid == 0) lend[lidx(tau - 2)] = nring[lidx(tau - 2)] + (m > 0.0 ? log(m) : 0.0);
+      }
       if (btid == 0) {
         double n;
         if (tau < 2) {
@@ -282,8 +319,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
         nring[lidx(tau)] = n;
       }
-      // anchors of this block
-      for (int i = btid; i < C; i += NBT) cA[bf * CP + i] = cumd(u0, i);
+      // anchors of this block: the cum values of its first position
+#pragma unroll
+      for (int r = 0; r < kMaxE; ++r)
+        if (e_i[r] == 0) cA[bf * CP + e_c[r]] = pre[r];
       bar_sync(kBarBulk, NBT);
       const double n_tau = nring[lidx(tau)];
       const double n_prev = nring[lidx(tau - 1)];
@@ -295,87 +334,107 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         wprev[bf * CP + i] = w;
       }
       bar_sync(kBarBulk, NBT);
-      {
+      if (wact) {
         double* wcur = wt + (size_t)bf * NWT * CP;
         const double* wold = wt + (size_t)(bf ^ 1) * NWT * CP;
-        for (int w = btid; w < NWT * C; w += NBT) {
-          const int q = w / C, cc = w % C;
+        const double wl = wring[lidx(tau - 1) * CP + wc];
+        for (int q = wq0; q < QW; q += wqs) {
           double v;
           if (q == 0) {
             v = 1.0;
           } else if (tau == 0) {
-            v = (q == 1) ? wring[lidx(-1) * CP + cc] : 0.0;  // only block -1 exists
+            v = (q == 1) ? wl : 0.0;  // only block -1 exists
           } else {
-            v = wold[(q - 1) * CP + cc] * wring[lidx(tau - 1) * CP + cc];
+            v = wold[(q - 1) * CP + wc] * wl;
           }
-          wcur[q * CP + cc] = v;
+          wcur[q * CP + wc] = v;
         }
       }
       // g / h of the targets: g = exp(toff + dbmax + d), h = exp(colmax + soff - d)
       const bool noproj = ps_b == nullptr && pe_b == nullptr;
-      for (int w = btid; w < nP * C; w += NBT) {
-        const int i = w / C, cc = w % C;
-        const int u = u0 + i;
-        const double d = csign * (cumd(u, cc) - cA[bf * CP + cc]);
-        if (noproj) {
-          const double e = exp(fmin(fmax(d, -650.0), 650.0));
-          gb[(bf * LP + i) * CP + cc] = edb[cc] * e;
-          hb[(bf * LP + i) * CP + cc] = ecm[cc] / e;
-        } else {
-          gb[(bf * LP + i) * CP + cc] = exp(fmin(toff_at(u, cc) + dbmax[cc] + d, 700.0));
-          hb[(bf * LP + i) * CP + cc] = exp(fmin(colmax[cc] + soff_at(u, cc) - d, 700.0));
+#pragma unroll
+      for (int r = 0; r < kMaxE; ++r) {
+        const int i = e_i[r], cc = e_c[r];
+        if (i >= 0 && i < nP) {
+          const int u = u0 + i;
+          const double d = csign * (pre[r] - cA[bf * CP + cc]);
+          if (noproj) {
+            const double e = exp(fmin(fmax(d, -650.0), 650.0));
+            gb[(bf * LP + i) * CP + cc] = edb[cc] * e;
+            hb[(bf * LP + i) * CP + cc] = ecm[cc] / e;
+          } else {
+            gb[(bf * LP + i) * CP + cc] = exp(fmin(toff_at(u, cc) + dbmax[cc] + d, 700.0));
+            hb[(bf * LP + i) * CP + cc] = exp(fmin(colmax[cc] + soff_at(u, cc) - d, 700.0));
+          }
         }
       }
+      // the next block's cum values: the loads complete during the far sums
+      prefetch_cum(tau + 1);
       bar_sync(kBarBulk, NBT);
       WT_ADD(2);
       // far sums over sources s in [s_lo, s_hi], s_hi = u0-LP-1 (end of block tau-2).
-      // Chunks are whole source blocks, so the frame factor is one lookup per block.
-      const int s_hi = u0 - LP - 1;
+      // Source block q (q >= 2 blocks back) holds positions sb = u0 - q*LP ..
+      // sb + LP - 1 in ring slots ((tau - q) mod NR)*LP ..; for target i and
+      // source r the duration is q*LP + i - r, so one block contributes an
+      // LP x LP tile from a window of 2*LP-1 Db values.  An item is a label
+      // pair and a chunk of consecutive source blocks; the frame factor W is
+      // one lookup per source block.
       const int s_lo = (u0 - kcap) > 0 ? (u0 - kcap) : 0;
-      const int ns = s_hi - s_lo + 1;
-      const int nsplit = pl.nsplit;
+      const int qmax = (u0 - s_lo + LP - 1) / LP;  // the block holding s_lo
+      const int nq = qmax - 1;                      // blocks q = 2 .. qmax
+      const int nsplit = pl.nsplit, np = pl.np;
       const double* wcur = wt + (size_t)bf * NWT * CP;
-      if (ns > 0) {
-        const int nblk_src = (ns + LP - 1) / LP + 1;  // source blocks touched (upper bound)
-        const int bpc = (nblk_src + nsplit - 1) / nsplit;  // source blocks per chunk
-        for (int w = btid; w < C * nsplit; w += NBT) {
-          const int cc = w % C, j = w / C;
-          double acc[LP];
+      if (nq > 0) {
+        const int bpc = (nq + nsplit - 1) / nsplit;  // source blocks per chunk
+        for (int w = btid; w < np * nsplit; w += NBT) {
+          const int c0 = 2 * (w % np), j = w / np;
+          double acc[LP][2];
 #pragma unroll
-          for (int i = 0; i < LP; ++i) acc[i] = 0.0;
-          // source blocks q = 2 + j*bpc .. 2 + (j+1)*bpc - 1 back from tau (q=2 ends at s_hi)
-          const int q0 = 2 + j * bpc;
-          int s_top = s_hi - (q0 - 2) * LP;
-          if (s_top >= s_lo) {
-            double win[LP];
+          for (int i = 0; i < LP; ++i) acc[i][0] = acc[i][1] = 0.0;
+          const int qa = 2 + j * bpc, qb = min(qa + bpc - 1, qmax);
+          for (int q = qa; q <= qb; ++q) {
+            const int sb = u0 - q * LP;
+            int bq = (tau - q) % NR;
+            if (bq < 0) bq += NR;
+            const double2* rp = reinterpret_cast<const double2*>(ring + (size_t)bq * LP * Cs + c0);
+            const double2 Wq = *reinterpret_cast<const double2*>(wcur + q * CP + c0);
+            double x[LP][2];
 #pragma unroll
-            for (int i = 0; i < LP; ++i) win[i] = (double)dbe[(u0 - s_top + i) * C + cc];
-            int slot = s_top % R;
-            for (int q = q0; q < q0 + bpc && s_top - (q - q0) * LP >= s_lo; ++q) {
-              const double W = (q < NWT) ? wcur[q * CP + cc] : 0.0;
-              const int sb = s_top - (q - q0) * LP;  // newest source of this block
-#pragma unroll
-              for (int r = 0; r < LP; ++r) {
-                const int s = sb - r;
-                const double x = (s >= s_lo) ? ring[slot * C + cc] * W : 0.0;
-#pragma unroll
-                for (int i = 0; i < LP; ++i) acc[i] = fma(x, win[(r + i) % LP], acc[i]);
-                int kn = u0 - s + LP;
-                if (kn > pl.kx - 1) kn = pl.kx - 1;
-                win[r % LP] = (double)dbe[kn * C + cc];
-                slot = (slot == 0) ? R - 1 : slot - 1;
-              }
+            for (int r = 0; r < LP; ++r) {
+              const double2 e = rp[(size_t)r * (Cs / 2)];
+              const bool ok = sb + r >= s_lo;
+              x[r][0] = ok ? e.x * Wq.x : 0.0;
+              x[r][1] = ok ? e.y * Wq.y : 0.0;
             }
+            // Db window: durations q*LP - (LP-1) .. q*LP + (LP-1)
+            const double2* dp = reinterpret_cast<const double2*>(dbd + (size_t)(q * LP - (LP - 1)) * Cs + c0);
+            double d[2 * LP - 1][2];
+#pragma unroll
+            for (int m = 0; m < 2 * LP - 1; ++m) {
+              const double2 v = dp[(size_t)m * (Cs / 2)];
+              d[m][0] = v.x;
+              d[m][1] = v.y;
+            }
+#pragma unroll
+            for (int r = 0; r < LP; ++r)
+#pragma unroll
+              for (int i = 0; i < LP; ++i) {
+                acc[i][0] = fma(x[r][0], d[LP - 1 + i - r][0], acc[i][0]);
+                acc[i][1] = fma(x[r][1], d[LP - 1 + i - r][1], acc[i][1]);
+              }
           }
 #pragma unroll
-          for (int i = 0; i < LP; ++i) part[(j * LP + i) * C + cc] = acc[i];
+          for (int i = 0; i < LP; ++i) {
+            part[(j * LP + i) * Cs + c0] = acc[i][0];
+            part[(j * LP + i) * Cs + c0 + 1] = acc[i][1];
+          }
         }
         bar_sync(kBarBulk, NBT);
         WT_ADD(3);
         for (int w = btid; w < LP * C; w += NBT) {
           const int i = w / C, cc = w % C;
           double s = 0.0;
-          for (int j = 0; j < nsplit; ++j) s += part[(j * LP + i) * C + cc];
+          for (int j = 0; j < nsplit; ++j) s += part[(j * LP + i) * Cs + cc];
           farb[(bf * LP + i) * CP + cc] = s;
         }
       } else {
@@ -388,6 +447,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       WT_ADD(4);
     };
 
+    prefetch_cum(0);
     if (NB > 0) {
       prepare(0);
       bar_arrive(kBarFull0, NPART);
@@ -418,7 +478,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const double ecol = cv ? exp(colmax[c]) : 0.0;
     double dbk[2 * LP];  // Db[k] for k = 0 .. 2LP-1 (index 0 unused)
 #pragma unroll
-    for (int k = 0; k < 2 * LP; ++k) dbk[k] = (cv && k >= 1) ? (double)dbe[k * C + c] : 0.0;
+    for (int k = 0; k < 2 * LP; ++k) dbk[k] = (cv && k >= 1) ? dbd[k * Cs + c] : 0.0;
     auto sync_serial = [&]() {
       if (SW == 1)
         __syncwarp();
@@ -452,16 +512,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       sync_serial();
       return ((y[0] + y[1]) + (y[2] + y[3])) + ((y[4] + y[5]) + (y[6] + y[7]));
     };
-    auto group_maxd = [&](double v) -> double {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (SW == 1) return v;
-      if (lane == 0) misc[8 + warp] = v;
-      bar_sync(kBarSerial, CP);
-      double r = fmax(misc[8], misc[9]);
-      bar_sync(kBarSerial, CP);
-      return r;
-    };
     auto group_sumd = [&](double v) -> double {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -477,7 +527,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     double ep[LP];
 #pragma unroll
     for (int j = 0; j < LP; ++j) ep[j] = 0.0;
-    ep[LP - 1] = cv ? ring[0 * C + c] : 0.0;  // position 0
+    ep[LP - 1] = cv ? ring[(R - 1) * Cs + c] : 0.0;  // position 0
     double a_last = a0;
     double n_last = 0.0;
     for (int tau = 0; tau < NB; ++tau) {
@@ -489,47 +539,59 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
       const double n_tau = nring[lidx(tau)];
       const double wp = cv ? wprev[bf * CP + c] : 0.0;
+      // this block's far sums and g factors, loaded once: the bulk warps keep
+      // the shared-memory pipe busy, so a load issued per position would pay
+      // that queueing on the critical path every time
+      double fr[LP], gr[LP];
+#pragma unroll
+      for (int i = 0; i < LP; ++i) {
+        fr[i] = cv ? farb[(bf * LP + i) * CP + c] : 0.0;
+        gr[i] = cv ? gb[(bf * LP + i) * CP + c] : 0.0;
+      }
 #pragma unroll
       for (int j = 0; j < LP; ++j) ep[j] *= wp;
       double ec[LP];
 #pragma unroll
       for (int i = 0; i < LP; ++i) ec[i] = 0.0;
-      int slot = u0 % R;
+      int slot = (tau % NR) * LP;  // slot of position u0: (u0 - 1) mod R
 #pragma unroll
       for (int i = 0; i < LP; ++i) {
         if (i < nP) {
           const int u = u0 + i;
           double S = 0.0, a = 0.0;
           if (cv) {
-            double pp[4] = {farb[(bf * LP + i) * CP + c], 0.0, 0.0, 0.0};
+            double pp[4] = {fr[i], 0.0, 0.0, 0.0};
 #pragma unroll
             for (int j = 0; j < LP; ++j) pp[j & 3] = fma(ep[j], dbk[LP + i - j], pp[j & 3]);
 #pragma unroll
             for (int j = 0; j + 1 < i; ++j) pp[(j + 1) & 3] = fma(ec[j], dbk[i - j], pp[(j + 1) & 3]);
             const double part0 = (pp[0] + pp[1]) + (pp[2] + pp[3]);
             S = (i >= 1) ? fma(ec[i - 1], dbk[1], part0) : part0;
-            a = (S > 0.0) ? gb[(bf * LP + i) * CP + c] * S : 0.0;
+            a = (S > 0.0) ? gr[i] * S : 0.0;
           }
           WT_ADD(9);
+          // h is needed right after the mat-vec: load it before, so its
+          // latency overlaps the mat-vec's
+          const double hcur = cv ? hb[(bf * LP + i) * CP + c] : 0.0;
           const double ym = matvec(a);
           WT_ADD(10);
           if (cv) {
-            const double e = (ym > 0.0) ? ym * hb[(bf * LP + i) * CP + c] : 0.0;
+            const double e = (ym > 0.0) ? ym * hcur : 0.0;
             ec[i] = e;
-            ring[slot * C + c] = e;
+            ring[slot * Cs + c] = e;
             const int t = cpos(u);
             if (atab_b) atab_b[(size_t)t * C + c] = a;
             if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
           }
           if (tid == 0 && ntab_b) ntab_b[cpos(u)] = n_tau;
           a_last = a;
-          slot = (slot + 1 == R) ? 0 : slot + 1;
+          ++slot;
           WT_ADD(11);
         }
       }
-      // scale at the end of the block, for the bulk's normaliser prediction
-      const double m = group_maxd(cv ? a_last : 0.0);
-      if (tid == 0) lend[lidx(tau)] = n_tau + (m > 0.0 ? log(m) : 0.0);
+      // the state at the end of the block: the bulk derives the block's scale
+      // from it for its normaliser prediction
+      alast[bf * CP + c] = cv ? a_last : 0.0;
       n_last = n_tau;
       // the near window of the next block is this block (padded with zeros)
 #pragma unroll

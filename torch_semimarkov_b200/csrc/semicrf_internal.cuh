@@ -220,7 +220,33 @@ cudaError_t launch_marginals_impl(const MargArgs& a, int semiring, float* alse, 
 cudaError_t launch_reduce_shared(const MargArgs& a, float* grad_tr, float* grad_db,
                                  cudaStream_t s);
 
+// vchain.cu: max-semiring chain for C <= 32, one warp per sequence
+struct VChainArgs {
+  int B, T, K, C;
+  const float* cum;
+  const float* tr;
+  const float* db;
+  const float* ps;
+  const float* pe;
+  const int64_t* lengths;
+  float* partition;  // (B) score, may be null
+  double* logz;      // (B) score in float64, may be null
+  int* final_c;      // (B) first maximising final label, may be null
+  int16_t* bp_k;     // (B, T+1, C) winning duration, may be null
+  uint8_t* bp_c;     // (B, T+1, C) winning source label, may be null
+  uint16_t* bp;      // (B, T+1, C) packed: duration | (source label at the start) << 8
+};
+bool vchain_supported(int B, int C, int K);
+cudaError_t launch_vchain(const VChainArgs& a, cudaStream_t s);
+
 // viterbi.cu
+// backtrace over the packed backpointers of vchain.cu
+size_t backtrace_packed_smem(int T, int C);
+cudaError_t launch_backtrace_packed(int B, int T, int K, int C, const float* cum,
+                                    const float* tr, const float* db, const int64_t* lengths,
+                                    int64_t max_len, const uint16_t* bp, const int* final_c,
+                                    int32_t* seg_start, int32_t* seg_end, int32_t* seg_label,
+                                    double* seg_score, int32_t* nseg, cudaStream_t s);
 cudaError_t launch_backtrace(int B, int T, int K, int C, const float* cum, const float* tr,
                              const float* db, const int64_t* lengths, int64_t max_len,
                              const int16_t* bp_k, const uint8_t* bp_c, const int* final_c,
