@@ -52,11 +52,19 @@ __device__ unsigned long long g_wstim[256][16];
 
 namespace {
 
-constexpr int kWsThreads = 256;
+constexpr int kWsThreads = 256;  // 2 warps per SM sub-partition
 constexpr size_t kWsSmemMax = 227 * 1024;
 
 enum : int { kBarFull0 = 1, kBarFull1 = 2, kBarDone0 = 3, kBarDone1 = 4, kBarBulk = 5,
              kBarSerial = 6 };
+
+// log(m) to within ln 2, from the exponent bits (m > 0; 0 otherwise): enough
+// for a normaliser, which only keeps the linear-domain values in range
+__device__ __forceinline__ double log_scale(double m) {
+  if (!(m > 0.0)) return 0.0;
+  const long long bits = __double_as_longlong(m);
+  return (double)((int)((bits >> 52) & 0x7ff) - 1023) * 0.6931471805599453;
+}
 
 __device__ __forceinline__ void bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -67,7 +75,7 @@ __device__ __forceinline__ void bar_sync(int id, int n) {
 
 struct WsPlan {
   int C, Cs, CP, K, kcap, LP, R, NR, kx, nbr, nbulk, np, nsplit, nwt;
-  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_wring, o_lend, o_nring, o_ca, o_far, o_g,
+  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_wring, o_nring, o_ca, o_far, o_g,
       o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast;
   int bytes;
 };
@@ -89,7 +97,8 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   int nbr = p.NR + 4;  // blocks whose frame factors are kept (power of 2)
   p.nbr = 1;
   while (p.nbr < nbr) p.nbr <<= 1;
-  p.nbulk = kWsThreads - 2 * CP;  // warps sharing a sub-partition with a serial warp idle
+  // every warp on a sub-partition that hosts a serial warp idles
+  p.nbulk = kWsThreads - (kWsThreads / 128) * CP;
   p.np = p.Cs / 2;
   p.nsplit = p.nbulk / p.np > 0 ? p.nbulk / p.np : 1;
   p.nwt = (p.kcap + LP - 1) / LP + 4;  // source blocks a k-window reaches, plus margin
@@ -105,7 +114,6 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_dbmax = take(8 * CP);
   p.o_colmax = take(8 * CP);
   p.o_wring = take(8 * p.nbr * CP);
-  p.o_lend = take(8 * (p.nbr + 2));
   p.o_nring = take(8 * (p.nbr + 2));
   p.o_ca = take(8 * 2 * CP);
   p.o_far = take(8 * 2 * LP * CP);
@@ -118,7 +126,7 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_misc = take(8 * 16);
   p.o_edb = take(8 * CP);
   p.o_ecm = take(8 * CP);
-  p.o_alast = take(8 * 2 * CP);  // state at the end of the last two blocks (scale)
+  p.o_alast = take(8 * 2 * CP);  // the state at the end of the last two blocks
   p.bytes = o;
 }
 
@@ -146,12 +154,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   constexpr int NT = kWsThreads;
   // Warps w and w+4 share a sub-partition.  The serial warps are 0..SW-1;
   // warps 4..4+SW-1 stay idle so that nothing competes with the critical path.
-  constexpr int NBT = NT - 2 * CP;
+  constexpr int NBT = NT - (NT / 128) * CP;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool serial = tid < CP;
-  const bool idle = warp >= 4 && warp < 4 + SW;
-  const int btid = (warp < 4) ? tid - CP : tid - 2 * CP;  // bulk thread index
-  constexpr int NPART = NT - CP;  // threads taking part in FULL / DONE (serial + bulk)
+  // warp w runs on sub-partition w % 4: the serial warps' sub-partitions
+  // carry nothing else
+  const bool idle = !serial && (warp & 3) < SW;
+  const int btid = ((warp >> 2) * (4 - SW) + ((warp & 3) - SW)) * 32 + lane;  // bulk index
+  constexpr int NPART = CP + NBT;  // threads taking part in FULL / DONE (serial + bulk)
   // CTAs [0, n1) take role a0, the rest role a1 (e.g. the alpha and beta
   // chains of the same batch in one launch)
   const bool role1 = (int)blockIdx.x >= L.n1;
@@ -169,13 +179,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   WsPlan pl;
   ws_choose(pl, C, K);
   const int kcap = pl.kcap, R = pl.R, NR = pl.NR, NBR = pl.nbr, Cs = pl.Cs;
+  // which side reduces the block-end state to a scale (the one with slack)
+  const bool serial_scale = kcap >= 64;
   double* ring = reinterpret_cast<double*>(smraw + pl.o_ring);  // [R][Cs]
   double* dbd = reinterpret_cast<double*>(smraw + pl.o_dbd);    // [kx][Cs]
   float* mx = reinterpret_cast<float*>(smraw + pl.o_mx);
   double* dbmax = reinterpret_cast<double*>(smraw + pl.o_dbmax);
   double* colmax = reinterpret_cast<double*>(smraw + pl.o_colmax);
   double* wring = reinterpret_cast<double*>(smraw + pl.o_wring);  // w_gamma, index (gamma+1) mod NBR
-  double* lend = reinterpret_cast<double*>(smraw + pl.o_lend);    // log scale at block end
   double* nring = reinterpret_cast<double*>(smraw + pl.o_nring);  // n_gamma
   double* cA = reinterpret_cast<double*>(smraw + pl.o_ca);        // [2][CP] anchors (bulk)
   double* farb = reinterpret_cast<double*>(smraw + pl.o_far);     // [2][LP][CP]
@@ -190,7 +201,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* misc = reinterpret_cast<double*>(smraw + pl.o_misc);
   double* edb = reinterpret_cast<double*>(smraw + pl.o_edb);  // exp(dbmax)
   double* ecm = reinterpret_cast<double*>(smraw + pl.o_ecm);  // exp(colmax)
-  double* alast = reinterpret_cast<double*>(smraw + pl.o_alast);  // [2][CP]
+  double* alast = reinterpret_cast<double*>(smraw + pl.o_alast);  // [2 blocks][CP]
   auto lidx = [&](int gamma) { return (gamma + NBR) & (NBR - 1); };  // gamma >= -NBR
 
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
@@ -256,7 +267,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     if (tid == 0) {
       if (ntab_b) ntab_b[cpos(0)] = 0.0;
       nring[lidx(-1)] = 0.0;
-      lend[lidx(-1)] = 0.0;  // log(max a[0]) = 0 forward; the backward starts from beta
     }
   }
   __syncthreads();
@@ -287,6 +297,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int r = 0; r < kMaxE; ++r)
         pre[r] = (e_i[r] >= 0 && u0 + e_i[r] <= u_end) ? cumd(u0 + e_i[r], e_c[r]) : 0.0;
     };
+    double lend3 = 0.0;  // scale at the end of block tau-3 (block -1: 0)
     // frame-table entries this thread updates: label wc, blocks q = wq0 + m*wqs
     const int QW = min(NWT, (kcap + LP - 1) / LP + 4);  // blocks a k-window reaches
     const int wc = btid % C, wq0 = btid / C, wqs = NBT / C > 0 ? NBT / C : 1;
@@ -297,41 +308,39 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int bf = tau & 1;
       const int u0 = u_begin + 1 + tau * LP;
       const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
-      // scale at the end of block tau-2 (the serial warp left its state in
-      // alast), then the normaliser prediction for this block
-      if (tau >= 2 && btid < 32) {
-        double m = 0.0;
-        for (int c2 = btid; c2 < C; c2 += 32) m = fmax(m, alast[((tau - 2) & 1) * CP + c2]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (btid == 0) lend[lidx(tau - 2)] = nring[lidx(tau - 2)] + (m > 0.0 ? log(m) : 0.0);
-      }
-      if (btid == 0) {
-        double n;
-        if (tau < 2) {
-          n = lend[lidx(-1)];
+      // normaliser prediction for this block from the scales at the end of
+      // blocks tau-2 and tau-3; every bulk warp derives it from the state the
+      // serial warp left in alast
+      double n_tau = 0.0;
+      if (tau >= 2) {
+        const double* al = alast + ((tau - 2) & 1) * CP;
+        double m;
+        if (serial_scale) {
+          m = SW > 1 ? fmax(al[0], al[1]) : al[0];
         } else {
-          const double l2 = lend[lidx(tau - 2)];
-          const double l3 = lend[lidx(tau - 3)];
-          double gr = l2 - l3;
-          gr = fmin(fmax(gr, -150.0), 150.0);
-          n = l2 + 2.0 * gr;
-        }
-        nring[lidx(tau)] = n;
-      }
-      // anchors of this block: the cum values of its first position
+          m = fmax(al[lane], CP > 32 ? al[(lane + 32) & (CP - 1)] : 0.0);
 #pragma unroll
-      for (int r = 0; r < kMaxE; ++r)
-        if (e_i[r] == 0) cA[bf * CP + e_c[r]] = pre[r];
-      bar_sync(kBarBulk, NBT);
-      const double n_tau = nring[lidx(tau)];
-      const double n_prev = nring[lidx(tau - 1)];
-      // w_{tau-1}: frame tau-1 -> tau, and this block's W table
-      for (int i = btid; i < C; i += NBT) {
-        const double w = exp(fmin(fmax(n_prev - n_tau + csign * (cA[bf * CP + i] - cA[(bf ^ 1) * CP + i]),
-                                       -700.0), 700.0));
-        wring[lidx(tau - 1) * CP + i] = w;
-        wprev[bf * CP + i] = w;
+          for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+        }
+        const double l2 = nring[lidx(tau - 2)] + log_scale(m);
+        const double gr = fmin(fmax(l2 - lend3, -150.0), 150.0);
+        n_tau = l2 + 2.0 * gr;
+        lend3 = l2;
+      }
+      if (btid == 0) nring[lidx(tau)] = n_tau;
+      const double n_prev = nring[lidx(tau - 1)];  // written by prepare(tau-1)
+      // anchors (the cum values of the block's first position) and w_{tau-1}
+      // (frame tau-1 -> tau), by the threads that hold those cum values
+#pragma unroll
+      for (int r = 0; r < kMaxE; ++r) {
+        if (e_i[r] == 0) {
+          const int cc = e_c[r];
+          cA[bf * CP + cc] = pre[r];
+          const double w = exp(fmin(fmax(n_prev - n_tau + csign * (pre[r] - cA[(bf ^ 1) * CP + cc]),
+                                         -700.0), 700.0));
+          wring[lidx(tau - 1) * CP + cc] = w;
+          wprev[bf * CP + cc] = w;
+        }
       }
       bar_sync(kBarBulk, NBT);
       if (wact) {
@@ -359,9 +368,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           const int u = u0 + i;
           const double d = csign * (pre[r] - cA[bf * CP + cc]);
           if (noproj) {
-            const double e = exp(fmin(fmax(d, -650.0), 650.0));
-            gb[(bf * LP + i) * CP + cc] = edb[cc] * e;
-            hb[(bf * LP + i) * CP + cc] = ecm[cc] / e;
+            const double dc = fmin(fmax(d, -650.0), 650.0);
+            gb[(bf * LP + i) * CP + cc] = edb[cc] * exp(dc);
+            hb[(bf * LP + i) * CP + cc] = ecm[cc] * exp(-dc);
           } else {
             gb[(bf * LP + i) * CP + cc] = exp(fmin(toff_at(u, cc) + dbmax[cc] + d, 700.0));
             hb[(bf * LP + i) * CP + cc] = exp(fmin(colmax[cc] + soff_at(u, cc) - d, 700.0));
@@ -376,9 +385,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // Source block q (q >= 2 blocks back) holds positions sb = u0 - q*LP ..
       // sb + LP - 1 in ring slots ((tau - q) mod NR)*LP ..; for target i and
       // source r the duration is q*LP + i - r, so one block contributes an
-      // LP x LP tile from a window of 2*LP-1 Db values.  An item is a label
-      // pair and a chunk of consecutive source blocks; the frame factor W is
-      // one lookup per source block.
+      // LP x LP tile from a window of 2*LP-1 Db values, and block q+1's window
+      // shares LP-1 of them.  An item is a label pair and a chunk of
+      // consecutive source blocks; the frame factor W is one lookup per block.
       const int s_lo = (u0 - kcap) > 0 ? (u0 - kcap) : 0;
       const int qmax = (u0 - s_lo + LP - 1) / LP;  // the block holding s_lo
       const int nq = qmax - 1;                      // blocks q = 2 .. qmax
@@ -392,6 +401,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
           for (int i = 0; i < LP; ++i) acc[i][0] = acc[i][1] = 0.0;
           const int qa = 2 + j * bpc, qb = min(qa + bpc - 1, qmax);
+          double d[2 * LP - 1][2];
+          if (qa <= qb) {
+            const double2* dp = reinterpret_cast<const double2*>(dbd + (size_t)(qa * LP - (LP - 1)) * Cs + c0);
+#pragma unroll
+            for (int m = 0; m < 2 * LP - 1; ++m) {
+              const double2 v = dp[(size_t)m * (Cs / 2)];
+              d[m][0] = v.x;
+              d[m][1] = v.y;
+            }
+          }
           for (int q = qa; q <= qb; ++q) {
             const int sb = u0 - q * LP;
             int bq = (tau - q) % NR;
@@ -406,15 +425,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               x[r][0] = ok ? e.x * Wq.x : 0.0;
               x[r][1] = ok ? e.y * Wq.y : 0.0;
             }
-            // Db window: durations q*LP - (LP-1) .. q*LP + (LP-1)
-            const double2* dp = reinterpret_cast<const double2*>(dbd + (size_t)(q * LP - (LP - 1)) * Cs + c0);
-            double d[2 * LP - 1][2];
-#pragma unroll
-            for (int m = 0; m < 2 * LP - 1; ++m) {
-              const double2 v = dp[(size_t)m * (Cs / 2)];
-              d[m][0] = v.x;
-              d[m][1] = v.y;
-            }
 #pragma unroll
             for (int r = 0; r < LP; ++r)
 #pragma unroll
@@ -422,6 +432,20 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                 acc[i][0] = fma(x[r][0], d[LP - 1 + i - r][0], acc[i][0]);
                 acc[i][1] = fma(x[r][1], d[LP - 1 + i - r][1], acc[i][1]);
               }
+            if (q < qb) {
+#pragma unroll
+              for (int m = 0; m < LP - 1; ++m) {
+                d[m][0] = d[m + LP][0];
+                d[m][1] = d[m + LP][1];
+              }
+              const double2* dn = reinterpret_cast<const double2*>(dbd + (size_t)((q + 1) * LP) * Cs + c0);
+#pragma unroll
+              for (int m = LP - 1; m < 2 * LP - 1; ++m) {
+                const double2 v = dn[(size_t)(m - (LP - 1)) * (Cs / 2)];
+                d[m][0] = v.x;
+                d[m][1] = v.y;
+              }
+            }
           }
 #pragma unroll
           for (int i = 0; i < LP; ++i) {
@@ -539,9 +563,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
       const double n_tau = nring[lidx(tau)];
       const double wp = cv ? wprev[bf * CP + c] : 0.0;
-      // this block's far sums and g factors, loaded once: the bulk warps keep
-      // the shared-memory pipe busy, so a load issued per position would pay
-      // that queueing on the critical path every time
+      // this block's far sums and g factors, loaded once per block rather than
+      // once per position on the critical path
       double fr[LP], gr[LP];
 #pragma unroll
       for (int i = 0; i < LP; ++i) {
@@ -589,9 +612,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           WT_ADD(11);
         }
       }
-      // the state at the end of the block: the bulk derives the block's scale
-      // from it for its normaliser prediction
-      alast[bf * CP + c] = cv ? a_last : 0.0;
+      // the state at the end of the block, from which the bulk derives the
+      // block's scale for its normaliser prediction: its per-warp maxima when
+      // the bulk is the busier side (long duration windows), else the state
+      if (serial_scale) {
+        double mm = cv ? a_last : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mm = fmax(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        if (lane == 0) alast[bf * CP + warp] = mm;
+      } else {
+        alast[bf * CP + c] = cv ? a_last : 0.0;
+      }
       n_last = n_tau;
       // the near window of the next block is this block (padded with zeros)
 #pragma unroll
