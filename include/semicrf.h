@@ -76,7 +76,16 @@ typedef struct semicrf_problem {
                                      SEMICRF_RECOMPUTE: ring checkpoints every
                                        S' >= S, O(B*T/S*K*C) memory, alpha is
                                        recomputed segment-parallel */
-    int32_t reserved;
+    int32_t chunk_warmup;         /* time chunking of the log-semiring chains
+                                     when the forward keeps SEMICRF_KEEP_ALPHA
+                                     state: 0 = automatic (when the batch
+                                     leaves SMs idle), -1 = never, > 0 = force
+                                     it with this many warm-up positions.
+                                     Chunks start early from a guessed state
+                                     and are accepted only where their state
+                                     matches the previous chunk's to 1e-10 in
+                                     projective distance; other sequences are
+                                     recomputed as one chain. */
 } semicrf_problem;
 
 enum semicrf_backward_mode { SEMICRF_KEEP_ALPHA = 0, SEMICRF_RECOMPUTE = 1 };
@@ -141,11 +150,10 @@ size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_
  * a device buffer (a JNI/cgo/N-API runtime with no device allocator, which
  * must not call cudaMalloc on its request path).  Results equal
  * semicrf_forward's partition for the same problem.
- *  - Scratch: a fixed 1 MiB device array inside the library, one per
- *    device; every accepted shape fits (the largest, at C=256, need
- *    under 700 KiB).  A problem whose semicrf_forward_workspace_size
- *    exceeds 1 MiB is rejected with SEMICRF_ERR_WORKSPACE (before any CUDA
- *    call).
+ *  - Scratch: a fixed 2 MiB device array inside the library, one per
+ *    device; every accepted shape fits (the largest, at C=256, need about
+ *    1.3 MiB).  A problem whose semicrf_forward_workspace_size exceeds
+ *    2 MiB is rejected with SEMICRF_ERR_WORKSPACE (before any CUDA call).
  *  - Nothing in the scratch needs to start at zero (each call writes what it
  *    reads, in stream order).
  *  - Calls on one device share that scratch: overlapping calls (different

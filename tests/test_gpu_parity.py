@@ -279,11 +279,18 @@ def _random_vs_oracle(case, oracle):
     from torch_semimarkov_b200 import semi_crf_streaming_forward
 
     B, T, K, C, gen, proj, semiring = case
-    dev = _dev()
     inp = make_streaming_inputs(B, T, K, C, seed=100 + T + K + C, gen=gen, proj=proj)
     rng = np.random.default_rng(T)
     lengths = np.concatenate([[T], rng.integers(max(1, T // 3), T + 1, size=B - 1)])
     gout = rng.uniform(0.5, 1.5, size=B)
+    _check_vs_oracle(inp, lengths, gout, K, semiring, oracle)
+
+
+def _check_vs_oracle(inp, lengths, gout, K, semiring, oracle):
+    """Forward + backward through semi_crf_streaming_forward vs the float64 oracle."""
+    from torch_semimarkov_b200 import semi_crf_streaming_forward
+
+    dev = _dev()
     np_in = {k: (None if v is None else v.numpy()) for k, v in inp.items()}
     part_ref, grads_ref = oracle.forward_backward(
         np_in["cum_scores"], np_in["transition"], np_in["duration_bias"], lengths, K, gout,
@@ -371,3 +378,41 @@ def test_max_forward_no_grad_vs_oracle(case, oracle):
             proj_start=None if inp["proj_start"] is None else inp["proj_start"].to(dev),
             proj_end=None if inp["proj_end"] is None else inp["proj_end"].to(dev))
     assert_close_rel(got.cpu().numpy(), ref, what="max score")
+
+
+# time-chunked chains (keep mode, batches that leave SMs idle): chunks start
+# early from a guessed state and are joined after a projective check; a short
+# forced warm-up exercises the serial rerun of sequences that do not join
+CHUNK_CASES = [
+    # B, T, K, C, gen, proj, env
+    (1, 5000, 20, 8, "cfg3", None, "auto"),
+    (2, 4000, 33, 24, "cfg2", "both", "auto"),
+    (1, 3000, 20, 8, "default", None, "8"),
+    (1, 12000, 1000, 8, "cfg3", None, "auto"),
+]
+
+
+@pytest.mark.parametrize("case", CHUNK_CASES)
+def test_chunked_chains_vs_oracle(case, oracle, monkeypatch):
+    B, T, K, C, gen, proj, env = case
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_CHUNKS", env)
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_BACKWARD", "keep")
+    from torch_semimarkov_b200 import _lib
+
+    lib = _lib.load()
+    dev = _dev()
+    from inputs import make_streaming_inputs
+
+    inp = make_streaming_inputs(B, T, K, C, seed=31 + T, gen=gen, proj=proj)
+    prob = _lib.Problem(inp["cum_scores"].to(dev), inp["transition"].to(dev),
+                        inp["duration_bias"].to(dev), torch.full((B,), T).to(dev), K, "log",
+                        None if inp["proj_start"] is None else inp["proj_start"].to(dev),
+                        None if inp["proj_end"] is None else inp["proj_end"].to(dev))
+    # the plan really chunks (the saved state then carries the hand-off buffers)
+    prob_off = _lib.SemicrfProblem.from_buffer_copy(prob.c)
+    prob_off.chunk_warmup = -1
+    import ctypes
+
+    assert lib.semicrf_saved_size(prob.cref) > lib.semicrf_saved_size(ctypes.byref(prob_off))
+    gout = np.random.default_rng(T).uniform(0.5, 1.5, size=B)
+    _check_vs_oracle(inp, np.full(B, T), gout, K, "log", oracle)

@@ -36,6 +36,18 @@ KEEP_ALPHA, RECOMPUTE = 0, 1
 KEEP_ALPHA_MAX_BYTES = 16 << 30
 
 
+def chunk_warmup_from_env() -> int:
+    """Time chunking of the log-semiring chains (semicrf_problem.chunk_warmup):
+    TORCH_SEMIMARKOV_B200_CHUNKS=off disables it, =<n> forces it with an
+    n-position warm-up; unset or auto lets the library decide."""
+    env = os.environ.get("TORCH_SEMIMARKOV_B200_CHUNKS", "").lower()
+    if env in ("", "auto"):
+        return 0
+    if env == "off":
+        return -1
+    return max(1, int(env))
+
+
 def backward_mode_for(B: int, T: int, C: int) -> int:
     env = os.environ.get("TORCH_SEMIMARKOV_B200_BACKWARD", "").lower()
     if env == "recompute":
@@ -82,7 +94,7 @@ class SemicrfProblem(ctypes.Structure):
         ("proj_end", ctypes.c_void_p),
         ("checkpoint_interval", ctypes.c_int64),
         ("backward_mode", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("chunk_warmup", ctypes.c_int32),
     ]
 
 
@@ -227,7 +239,8 @@ class Problem:
             lengths=self.lengths.data_ptr(),
             proj_start=None if self.ps is None else self.ps.data_ptr(),
             proj_end=None if self.pe is None else self.pe.data_ptr(),
-            checkpoint_interval=S, backward_mode=self.backward_mode, reserved=0)
+            checkpoint_interval=S, backward_mode=self.backward_mode,
+            chunk_warmup=chunk_warmup_from_env())
 
     @property
     def cref(self):

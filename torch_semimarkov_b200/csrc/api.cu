@@ -63,15 +63,20 @@ int validate(const semicrf_problem* p) {
   return SEMICRF_OK;
 }
 
-Prepared carve_prep(Carver& cv, int C, int K) {
+Prepared carve_prep(Carver& cv, int C, int K, int semiring) {
   Prepared pr{};
   const int kx = kcap_of(K) + kPrepRowsExtra;
-  pr.mx_f = cv.take<float>((size_t)C * C);
-  pr.mx_b = cv.take<float>((size_t)C * C);
+  if (semiring == SEMICRF_LOG) {
+    pr.mxd_f = cv.take<double>((size_t)C * C);
+    pr.mxd_b = cv.take<double>((size_t)C * C);
+    pr.dbed = cv.take<double>((size_t)kx * C);
+  } else {
+    pr.mx_f = cv.take<float>((size_t)C * C);
+    pr.mx_b = cv.take<float>((size_t)C * C);
+  }
   pr.colmax_f = cv.take<float>(C);
   pr.colmax_b = cv.take<float>(C);
   pr.dbl = cv.take<float>((size_t)kx * C);
-  pr.dbe = cv.take<float>((size_t)kx * C);
   pr.dbmax = cv.take<float>(C);
   pr.kx = kx;
   return pr;
@@ -88,7 +93,17 @@ struct SavedLayout {
   double* b_tab;   // ... and the beta chain's tables
   double* B_tab;
   double* m_tab;
+  ChunkPlan cp;    // time chunks of the two chains (keep mode)
+  double *hand_a, *hand_b, *rdiff, *dofs;
+  int *okf, *fail;
 };
+
+ChunkPlan keep_chunk_plan(const semicrf_problem* p) {
+  if (p->semiring != SEMICRF_LOG || p->backward_mode != SEMICRF_KEEP_ALPHA ||
+      !lchain_ws_supported((int)p->C, (int)p->K))
+    return ChunkPlan{1, (int)p->T, 0};
+  return chunk_plan((int)p->batch, (int)p->T, (int)p->K, (int)p->C, 2, p->chunk_warmup);
+}
 
 SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
   SavedLayout s{};
@@ -108,6 +123,17 @@ SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
     s.b_tab = cv.take<double>(n);
     s.B_tab = cv.take<double>(n);
     s.m_tab = cv.take<double>(B * (p->T + 1));
+    s.cp = keep_chunk_plan(p);
+    if (s.cp.nchunk > 1) {
+      const size_t nh = chunk_hand_doubles((int)B, (int)p->K, (int)C, s.cp);
+      const size_t nc = B * s.cp.nchunk;
+      s.hand_a = cv.take<double>(nh);
+      s.hand_b = cv.take<double>(nh);
+      s.rdiff = cv.take<double>(2 * nc);
+      s.dofs = cv.take<double>(2 * nc);
+      s.okf = cv.take<int>(2 * nc);
+      s.fail = cv.take<int>(2 * B);
+    }
   }
   return s;
 }
@@ -148,7 +174,7 @@ struct LBwdLayout {
 
 LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
   LBwdLayout w{};
-  w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  w.pr = carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
   const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
   const size_t nt = (size_t)p->batch * (p->T + 1);
   if (p->backward_mode == SEMICRF_RECOMPUTE) {
@@ -169,6 +195,53 @@ LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
   return w;
 }
 
+// Both chains of every sequence in time chunks (one CTA per chunk and chain),
+// then the boundary check and offset fix-up per chain, then a serial rerun of
+// any sequence whose chunks did not join.
+cudaError_t chunked_chains(const semicrf_problem* p, LChainLaunch L, const SavedLayout& sl,
+                           cudaStream_t s) {
+  const int B = (int)p->batch, P = sl.cp.nchunk;
+  for (LChainArgs* a : {&L.a0, &L.a1}) {
+    a->nchunk = P;
+    a->chunk_len = sl.cp.len;
+    a->warm = sl.cp.warm;
+  }
+  L.a0.hand = sl.hand_a;
+  L.a1.hand = sl.hand_b;
+  L.n1 = B * P;
+  cudaError_t e = launch_lchain_ws(L, 2 * B * P, s);
+  if (e != cudaSuccess) return e;
+  for (int role = 0; role < 2; ++role) {
+    ChunkFix f{};
+    f.B = B;
+    f.T = (int)p->T;
+    f.K = (int)p->K;
+    f.C = (int)p->C;
+    f.dir = role;
+    f.cp = sl.cp;
+    f.lengths = p->lengths;
+    f.hand = role ? sl.hand_b : sl.hand_a;
+    f.rdiff = sl.rdiff + (size_t)role * B * P;
+    f.okf = sl.okf + (size_t)role * B * P;
+    f.D = sl.dofs + (size_t)role * B * P;
+    f.fail = sl.fail + (size_t)role * B;
+    f.n_tab = role ? sl.m_tab : sl.n_tab;
+    f.logz = role ? nullptr : L.a0.logz;
+    f.partition = role ? nullptr : L.a0.partition;
+    e = launch_chunk_fix(f, s);
+    if (e != cudaSuccess) return e;
+  }
+  // sequences whose chunks did not join: each chain again, whole
+  for (LChainArgs* a : {&L.a0, &L.a1}) {
+    a->nchunk = 1;
+    a->hand = nullptr;
+  }
+  L.a0.only = sl.fail;
+  L.a1.only = sl.fail + B;
+  L.n1 = B;
+  return launch_lchain_ws(L, 2 * B, s);
+}
+
 // the beta chain (dir 1) of a log-semiring problem, writing its tables
 LChainArgs beta_chain_args(const semicrf_problem* p, const Prepared& pr, double* b_tab,
                            double* B_tab, double* m_tab) {
@@ -179,7 +252,7 @@ LChainArgs beta_chain_args(const semicrf_problem* p, const Prepared& pr, double*
   a.ps = p->proj_start;
   a.pe = p->proj_end;
   a.lengths = p->lengths;
-  a.mx = pr.mx_b;
+  a.mx = pr.mxd_b;
   a.colmax = pr.colmax_b;
   a.a_tab = b_tab;
   a.A_tab = B_tab;
@@ -189,7 +262,7 @@ LChainArgs beta_chain_args(const semicrf_problem* p, const Prepared& pr, double*
 
 BwdLayout carve_bwd(Carver& cv, const semicrf_problem* p) {
   BwdLayout w{};
-  w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  w.pr = carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
   const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
   const size_t nt = (size_t)p->batch * (p->T + 1);
   w.xa = cv.take<float>(n);
@@ -215,7 +288,7 @@ struct VitLayout {
 
 VitLayout carve_vit(Carver& cv, const semicrf_problem* p) {
   VitLayout w{};
-  w.pr = carve_prep(cv, (int)p->C, (int)p->K);
+  w.pr = carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
   const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
   w.bp_k = cv.take<int16_t>(n);
   w.bp_c = cv.take<uint8_t>(n);
@@ -274,7 +347,7 @@ size_t semicrf_saved_size(const semicrf_problem* p) {
 size_t semicrf_forward_workspace_size(const semicrf_problem* p) {
   if (validate_shape(p) != SEMICRF_OK) return 0;
   Carver cv(nullptr);
-  carve_prep(cv, (int)p->C, (int)p->K);
+  carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
   return cv.bytes();
 }
 
@@ -297,7 +370,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     return cuda_status(launch_vchain(v, s));
   }
   Carver cv(workspace);
-  Prepared pr = carve_prep(cv, (int)p->C, (int)p->K);
+  Prepared pr = carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
   cudaError_t e = launch_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
                               kcap_of(p->K), kP, p->semiring, pr, s);
   if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
@@ -307,7 +380,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     L.T = (int)p->T;
     L.K = (int)p->K;
     L.C = (int)p->C;
-    L.dbe = pr.dbe;
+    L.dbe = pr.dbed;
     L.dbmax = pr.dbmax;
     LChainArgs a{};
     a.mode = 0;
@@ -316,7 +389,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     a.ps = p->proj_start;
     a.pe = p->proj_end;
     a.lengths = p->lengths;
-    a.mx = pr.mx_f;
+    a.mx = pr.mxd_f;
     a.colmax = pr.colmax_f;
     a.partition = partition;
     a.ref_ckpt = ring_checkpoints;
@@ -343,6 +416,8 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
         L.a0.n_tab = sl.n_tab;
         L.a1 = beta_chain_args(p, pr, sl.b_tab, sl.B_tab, sl.m_tab);
         grid = 2 * (int)p->batch;
+        if (sl.cp.nchunk > 1 && !L.a0.ref_ckpt)
+          return cuda_status(chunked_chains(p, L, sl, s));
       }
     }
     if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_ws_supported((int)p->C, (int)p->K))
@@ -410,7 +485,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     L.T = (int)p->T;
     L.K = (int)p->K;
     L.C = (int)p->C;
-    L.dbe = w.pr.dbe;
+    L.dbe = w.pr.dbed;
     L.dbmax = w.pr.dbmax;
     const double *xa = sl.a_tab, *xA = sl.A_tab, *xn = sl.n_tab;
     const double *ya = sl.b_tab, *yA = sl.B_tab, *yn = sl.m_tab;
@@ -427,7 +502,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
       r.ps = p->proj_start;
       r.pe = p->proj_end;
       r.lengths = p->lengths;
-      r.mx = w.pr.mx_f;
+      r.mx = w.pr.mxd_f;
       r.colmax = w.pr.colmax_f;
       r.sv = sl.sv;
       r.sint = sint_of(p);

@@ -149,20 +149,23 @@ __global__ void prep_kernel(const float* __restrict__ tr, const float* __restric
   const int nth = gridDim.x * blockDim.x;
   for (int i = tid; i < C * C; i += nth) {
     const int r = i / C, c = i % C;
-    float vf = tr[r * C + c], vb = tr[c * C + r];
+    const float vf = tr[r * C + c], vb = tr[c * C + r];
     if (semiring == 0) {
-      vf = __expf(vf - pr.colmax_f[c]);
-      vb = __expf(vb - pr.colmax_b[c]);
+      // float64: a float32 exp would perturb every weight by ~6e-8, which
+      // long sequences turn into visible gradient error
+      pr.mxd_f[i] = exp((double)vf - (double)pr.colmax_f[c]);
+      pr.mxd_b[i] = exp((double)vb - (double)pr.colmax_b[c]);
+    } else {
+      pr.mx_f[i] = vf;
+      pr.mx_b[i] = vb;
     }
-    pr.mx_f[i] = vf;
-    pr.mx_b[i] = vb;
   }
   for (int i = tid; i < kx * C; i += nth) {
     const int k = i / C, c = i % C;
     float v = kNegInf;
     if (k >= 1 && k <= kcap) v = db[(k < K - 1 ? k : K - 1) * C + c];
     pr.dbl[i] = v;
-    if (semiring == 0) pr.dbe[i] = (v == kNegInf) ? 0.f : __expf(v - pr.dbmax[c]);
+    if (semiring == 0) pr.dbed[i] = (v == kNegInf) ? 0.0 : exp((double)v - (double)pr.dbmax[c]);
   }
 }
 

@@ -96,8 +96,8 @@ __host__ __device__ inline void lmake(LPlan& p, int C, int K, bool db_smem, bool
     return r;
   };
   p.o_ring = take(8 * p.R * C);
-  p.o_dbe = db_smem ? take(4 * p.kx * C) : -1;
-  p.o_mx = mx_smem ? take(4 * C * C) : -1;
+  p.o_dbe = db_smem ? take(8 * p.kx * C) : -1;
+  p.o_mx = mx_smem ? take(8 * C * C) : -1;
   p.o_dbmax = take(8 * p.CP);
   p.o_colmax = take(8 * p.CP);
   p.o_ref = take(8 * p.CP);
@@ -177,8 +177,8 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   lchoose(pl, C, K);
   const int kcap = pl.kcap, R = pl.R;
   double* ring = reinterpret_cast<double*>(smraw + pl.o_ring);
-  const float* dbe = pl.db_smem ? reinterpret_cast<float*>(smraw + pl.o_dbe) : L.dbe;
-  const float* mx = pl.mx_smem ? reinterpret_cast<float*>(smraw + pl.o_mx) : A.mx;
+  const double* dbe = pl.db_smem ? reinterpret_cast<double*>(smraw + pl.o_dbe) : L.dbe;
+  const double* mx = pl.mx_smem ? reinterpret_cast<double*>(smraw + pl.o_mx) : A.mx;
   double* dbmax = reinterpret_cast<double*>(smraw + pl.o_dbmax);
   double* colmax = reinterpret_cast<double*>(smraw + pl.o_colmax);
   double* ref = reinterpret_cast<double*>(smraw + pl.o_ref);
@@ -219,9 +219,9 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   }
   if (pl.db_smem)
     for (int i = tid; i < pl.kx * C; i += kNT)
-      const_cast<float*>(dbe)[i] = L.dbe[i];
+      const_cast<double*>(dbe)[i] = L.dbe[i];
   if (pl.mx_smem)
-    for (int i = tid; i < C * C; i += kNT) const_cast<float*>(mx)[i] = A.mx[i];
+    for (int i = tid; i < C * C; i += kNT) const_cast<double*>(mx)[i] = A.mx[i];
   const bool fwd_full = dir == 0 && A.mode == 0;
   float* const ref_ckpt = A.ref_ckpt;
   const int nref = A.nref, sref = A.sref, sint = A.sint, nint = A.nint;
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   const bool cv = serial && c < C;
   double dbj[LP + 1];
 #pragma unroll
-  for (int j = 0; j <= LP; ++j) dbj[j] = (cv && j >= 1) ? (double)dbe[j * C + c] : 0.0;
+  for (int j = 0; j <= LP; ++j) dbj[j] = (cv && j >= 1) ? dbe[j * C + c] : 0.0;
 
   double* atab_b = A.a_tab ? A.a_tab + (size_t)b * (T + 1) * C : nullptr;
   double* Atab_b = A.A_tab ? A.A_tab + (size_t)b * (T + 1) * C : nullptr;
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
   constexpr int MXR = (CP == 32) ? 32 : 1;
   double mxr[MXR];
 #pragma unroll
-  for (int q = 0; q < MXR; ++q) mxr[q] = (CP == 32 && cv && q < C) ? (double)mx[q * C + c] : 0.0;
+  for (int q = 0; q < MXR; ++q) mxr[q] = (CP == 32 && cv && q < C) ? mx[q * C + c] : 0.0;
   const double ecol = cv ? exp(colmax[c]) : 0.0;
   auto matvec = [&](double a) -> double {
     abuf[c] = cv ? a : 0.0;
@@ -299,12 +299,12 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
     } else if (cv) {
       int q = 0;
       for (; q + 4 <= C; q += 4) {
-        y[0] = fma(abuf[q + 0], (double)mx[(q + 0) * C + c], y[0]);
-        y[1] = fma(abuf[q + 1], (double)mx[(q + 1) * C + c], y[1]);
-        y[2] = fma(abuf[q + 2], (double)mx[(q + 2) * C + c], y[2]);
-        y[3] = fma(abuf[q + 3], (double)mx[(q + 3) * C + c], y[3]);
+        y[0] = fma(abuf[q + 0], mx[(q + 0) * C + c], y[0]);
+        y[1] = fma(abuf[q + 1], mx[(q + 1) * C + c], y[1]);
+        y[2] = fma(abuf[q + 2], mx[(q + 2) * C + c], y[2]);
+        y[3] = fma(abuf[q + 3], mx[(q + 3) * C + c], y[3]);
       }
-      for (; q < C; ++q) y[0] = fma(abuf[q], (double)mx[q * C + c], y[0]);
+      for (; q < C; ++q) y[0] = fma(abuf[q], mx[q * C + c], y[0]);
     }
     sync_serial();
     return ((y[0] + y[1]) + (y[2] + y[3])) + ((y[4] + y[5]) + (y[6] + y[7]));
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
         for (int i = 0; i < LP; ++i) {
           int k = u0 - s_top + i;
           if (k > pl.kx - 1) k = pl.kx - 1;
-          win[i] = (double)dbe[k * C + cc];
+          win[i] = dbe[k * C + cc];
         }
         int slot = s_top % R;
         for (int base = 0; base < n; base += LP) {
@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
             for (int i = 0; i < LP; ++i) acc[i] = fma(E, win[(r + i) % LP], acc[i]);
             int kn = u0 - s + LP;
             if (kn > pl.kx - 1) kn = pl.kx - 1;
-            win[r % LP] = (double)dbe[kn * C + cc];
+            win[r % LP] = dbe[kn * C + cc];
             slot = (slot == 0) ? R - 1 : slot - 1;
           }
         }

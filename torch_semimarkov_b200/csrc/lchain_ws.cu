@@ -75,7 +75,7 @@ __device__ __forceinline__ void bar_sync(int id, int n) {
 
 struct WsPlan {
   int C, Cs, CP, K, kcap, LP, R, NR, kx, nbr, nbulk, np, nsplit, nwt;
-  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_wring, o_nring, o_ca, o_far, o_g,
+  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_nring, o_ca, o_far, o_g,
       o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast;
   int bytes;
 };
@@ -110,10 +110,9 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   };
   p.o_ring = take(8 * p.R * p.Cs);
   p.o_dbd = take(8 * p.kx * p.Cs);  // Db = exp(db - dbmax) as doubles
-  p.o_mx = take(4 * C * C);
+  p.o_mx = take(8 * C * C);
   p.o_dbmax = take(8 * CP);
   p.o_colmax = take(8 * CP);
-  p.o_wring = take(8 * p.nbr * CP);
   p.o_nring = take(8 * (p.nbr + 2));
   p.o_ca = take(8 * 2 * CP);
   p.o_far = take(8 * 2 * LP * CP);
@@ -122,7 +121,7 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_wprev = take(8 * 2 * CP);
   p.o_part = take(8 * p.nsplit * LP * p.Cs);
   p.o_abuf = take(8 * CP);
-  p.o_wt = take(8 * 2 * p.nwt * CP);  // W tables of the last two prepared blocks
+  p.o_wt = take(8 * 2 * p.nwt * p.Cs);  // W tables of the last two prepared blocks
   p.o_misc = take(8 * 16);
   p.o_edb = take(8 * CP);
   p.o_ecm = take(8 * CP);
@@ -166,14 +165,22 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   // chains of the same batch in one launch)
   const bool role1 = (int)blockIdx.x >= L.n1;
   const LChainArgs& A = role1 ? L.a1 : L.a0;
-  const int b = role1 ? (int)blockIdx.x - L.n1 : (int)blockIdx.x;
+  const int cta = role1 ? (int)blockIdx.x - L.n1 : (int)blockIdx.x;
+  const int nch = A.nchunk > 1 ? A.nchunk : 1;
+  const int b = cta / nch, jc = cta % nch;  // sequence and time chunk
   if (b >= L.B) return;
+  if (A.only && !A.only[b]) return;
   const int C = L.C, K = L.K, T = L.T;
   const int dir = A.dir;
   const double csign = dir == 0 ? 1.0 : -1.0;
   const long long lraw = A.lengths[b];
   const int Lb = lraw < 0 ? 0 : (lraw > T ? T : (int)lraw);
-  const int u_begin = 0, u_end = Lb;
+  // chunk jc > 0 starts A.warm positions before its first output position
+  // u_out + 1, from a uniform state (the warm-up); chunk 0 is the exact start
+  const int u_out = jc > 0 ? jc * A.chunk_len : -1;
+  if (jc > 0 && u_out >= Lb) return;  // nothing of this sequence left
+  const int u_begin = jc > 0 ? u_out - A.warm : 0;
+  const int u_end = (jc + 1 < nch && (jc + 1) * A.chunk_len < Lb) ? (jc + 1) * A.chunk_len : Lb;
   const int NB = (u_end - u_begin + LP - 1) / LP;  // target blocks
 
   WsPlan pl;
@@ -183,10 +190,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   const bool serial_scale = kcap >= 64;
   double* ring = reinterpret_cast<double*>(smraw + pl.o_ring);  // [R][Cs]
   double* dbd = reinterpret_cast<double*>(smraw + pl.o_dbd);    // [kx][Cs]
-  float* mx = reinterpret_cast<float*>(smraw + pl.o_mx);
+  double* mx = reinterpret_cast<double*>(smraw + pl.o_mx);
   double* dbmax = reinterpret_cast<double*>(smraw + pl.o_dbmax);
   double* colmax = reinterpret_cast<double*>(smraw + pl.o_colmax);
-  double* wring = reinterpret_cast<double*>(smraw + pl.o_wring);  // w_gamma, index (gamma+1) mod NBR
   double* nring = reinterpret_cast<double*>(smraw + pl.o_nring);  // n_gamma
   double* cA = reinterpret_cast<double*>(smraw + pl.o_ca);        // [2][CP] anchors (bulk)
   double* farb = reinterpret_cast<double*>(smraw + pl.o_far);     // [2][LP][CP]
@@ -230,7 +236,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   for (int i = tid; i < C * C; i += NT) mx[i] = A.mx[i];
   for (int i = tid; i < pl.kx * Cs; i += NT) {
     const int k = i / Cs, cc = i % Cs;
-    dbd[i] = cc < C ? (double)L.dbe[k * C + cc] : 0.0;
+    dbd[i] = cc < C ? L.dbe[k * C + cc] : 0.0;
   }
   for (int i = tid; i < R * Cs; i += NT) ring[i] = 0.0;
   __syncthreads();
@@ -241,8 +247,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* Atab_b = A.A_tab ? A.A_tab + (size_t)b * (T + 1) * C : nullptr;
   double* ntab_b = A.n_tab ? A.n_tab + (size_t)b * (T + 1) : nullptr;
 
-  // ---- initial state (position u_begin = 0, "block -1") -----------------
-  // frame of block -1: n = 0, anchor cA_{-1} = cum(0)
+  // ---- initial state (position u_begin, "block -1") ----------------------
+  // frame of block -1: n = 0, anchor cA_{-1} = cum(u_begin)
   double a0 = 0.0;
   if (serial) {
     double ym0;
@@ -257,19 +263,38 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       ym0 = cv ? exp(-colmax[c]) : 0.0;  // beta[Lb] = 0
     }
     if (cv) {
-      const double e0 = ym0 * exp(colmax[c] + soff_at(0, c));
-      ring[(R - 1) * Cs + c] = e0;  // slot of position 0
-      const int t0 = cpos(0);
-      if (atab_b) atab_b[(size_t)t0 * C + c] = a0;
-      if (Atab_b) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
-      cA[1 * CP + c] = cumd(0, c);  // anchor of block -1 (parity of -1 is 1)
+      const double e0 = ym0 * exp(colmax[c] + soff_at(u_begin, c));
+      ring[(R - 1) * Cs + c] = e0;  // slot of position u_begin
+      const int t0 = cpos(u_begin);
+      if (jc == 0 && atab_b) atab_b[(size_t)t0 * C + c] = a0;
+      if (jc == 0 && Atab_b) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
+      cA[1 * CP + c] = cumd(u_begin, c);  // anchor of block -1 (parity of -1 is 1)
     }
     if (tid == 0) {
-      if (ntab_b) ntab_b[cpos(0)] = 0.0;
+      if (jc == 0 && ntab_b) ntab_b[cpos(u_begin)] = 0.0;
       nring[lidx(-1)] = 0.0;
     }
   }
   __syncthreads();
+
+  // log sources (log E + n of the block) of the kcap positions ending at ux,
+  // for the chunk hand-off: [kcap][C], row r = position ux - r
+  auto export_state = [&](int kind, int ux, int t0, int nt) {
+    double* out = A.hand + (((size_t)b * nch + jc) * 2 + kind) * (size_t)kcap * C;
+    for (int i = t0; i < kcap * C; i += nt) {
+      const int s = ux - i / C, cc = i % C;
+      double v = -INFINITY;
+      if (s >= u_begin) {
+        const int rel = s - u_begin - 1;  // -1: the start position (block -1)
+        const int slot = rel >= 0 ? rel % R : R - 1;
+        const double e = ring[(size_t)slot * Cs + cc];
+        if (e > 0.0) v = log(e) + nring[lidx(rel >= 0 ? rel / LP : -1)];
+      }
+      out[i] = v;
+    }
+  };
+  // block whose last position is u_out (the end of the warm-up)
+  const int tau_out = (jc > 0 && A.hand) ? (u_out - u_begin) / LP - 1 : -10;
 
   WT_DECL
   if (idle) {
@@ -338,15 +363,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           cA[bf * CP + cc] = pre[r];
           const double w = exp(fmin(fmax(n_prev - n_tau + csign * (pre[r] - cA[(bf ^ 1) * CP + cc]),
                                          -700.0), 700.0));
-          wring[lidx(tau - 1) * CP + cc] = w;
           wprev[bf * CP + cc] = w;
         }
       }
       bar_sync(kBarBulk, NBT);
       if (wact) {
-        double* wcur = wt + (size_t)bf * NWT * CP;
-        const double* wold = wt + (size_t)(bf ^ 1) * NWT * CP;
-        const double wl = wring[lidx(tau - 1) * CP + wc];
+        double* wcur = wt + (size_t)bf * NWT * Cs;
+        const double* wold = wt + (size_t)(bf ^ 1) * NWT * Cs;
+        const double wl = wprev[bf * CP + wc];  // w_{tau-1}
         for (int q = wq0; q < QW; q += wqs) {
           double v;
           if (q == 0) {
@@ -354,9 +378,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           } else if (tau == 0) {
             v = (q == 1) ? wl : 0.0;  // only block -1 exists
           } else {
-            v = wold[(q - 1) * CP + wc] * wl;
+            v = wold[(q - 1) * Cs + wc] * wl;
           }
-          wcur[q * CP + wc] = v;
+          wcur[q * Cs + wc] = v;
         }
       }
       // g / h of the targets: g = exp(toff + dbmax + d), h = exp(colmax + soff - d)
@@ -388,11 +412,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // LP x LP tile from a window of 2*LP-1 Db values, and block q+1's window
       // shares LP-1 of them.  An item is a label pair and a chunk of
       // consecutive source blocks; the frame factor W is one lookup per block.
-      const int s_lo = (u0 - kcap) > 0 ? (u0 - kcap) : 0;
+      const int s_lo = (u0 - kcap) > u_begin ? (u0 - kcap) : u_begin;
       const int qmax = (u0 - s_lo + LP - 1) / LP;  // the block holding s_lo
       const int nq = qmax - 1;                      // blocks q = 2 .. qmax
       const int nsplit = pl.nsplit, np = pl.np;
-      const double* wcur = wt + (size_t)bf * NWT * CP;
+      const double* wcur = wt + (size_t)bf * NWT * Cs;
       if (nq > 0) {
         const int bpc = (nq + nsplit - 1) / nsplit;  // source blocks per chunk
         for (int w = btid; w < np * nsplit; w += NBT) {
@@ -416,7 +440,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             int bq = (tau - q) % NR;
             if (bq < 0) bq += NR;
             const double2* rp = reinterpret_cast<const double2*>(ring + (size_t)bq * LP * Cs + c0);
-            const double2 Wq = *reinterpret_cast<const double2*>(wcur + q * CP + c0);
+            const double2 Wq = *reinterpret_cast<const double2*>(wcur + q * Cs + c0);
             double x[LP][2];
 #pragma unroll
             for (int r = 0; r < LP; ++r) {
@@ -485,6 +509,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // buffer (tau & 1) is free once the serial warp is done with block tau-2
       bar_sync(((tau - 2) & 1) ? kBarDone1 : kBarDone0, NPART);
       WT_ADD(0);
+      // the warm-up is over: hand off this chunk's guess of the state
+      if (tau - 2 == tau_out) export_state(0, u_out, btid, NBT);
       if (tau < NB) {
         prepare(tau);
         bar_arrive((tau & 1) ? kBarFull1 : kBarFull0, NPART);
@@ -498,7 +524,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     double mxr[CP == 32 ? 32 : 1];
 #pragma unroll
     for (int q = 0; q < (CP == 32 ? 32 : 1); ++q)
-      mxr[q] = (CP == 32 && cv && q < C) ? (double)mx[q * C + c] : 0.0;
+      mxr[q] = (CP == 32 && cv && q < C) ? mx[q * C + c] : 0.0;
     const double ecol = cv ? exp(colmax[c]) : 0.0;
     double dbk[2 * LP];  // Db[k] for k = 0 .. 2LP-1 (index 0 unused)
 #pragma unroll
@@ -529,8 +555,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         for (int q = 0; q < CP / 2; ++q) {
           const double2 v = ab2[q];
           const int q0 = 2 * q, q1 = 2 * q + 1;
-          y[q0 & 7] = fma(v.x, q0 < C ? (double)mx[q0 * C + c] : 0.0, y[q0 & 7]);
-          y[q1 & 7] = fma(v.y, q1 < C ? (double)mx[q1 * C + c] : 0.0, y[q1 & 7]);
+          y[q0 & 7] = fma(v.x, q0 < C ? mx[q0 * C + c] : 0.0, y[q0 & 7]);
+          y[q1 & 7] = fma(v.y, q1 < C ? mx[q1 * C + c] : 0.0, y[q1 & 7]);
         }
       }
       sync_serial();
@@ -603,10 +629,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             ec[i] = e;
             ring[slot * Cs + c] = e;
             const int t = cpos(u);
-            if (atab_b) atab_b[(size_t)t * C + c] = a;
-            if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
+            if (u > u_out) {
+              if (atab_b) atab_b[(size_t)t * C + c] = a;
+              if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
+            }
           }
-          if (tid == 0 && ntab_b) ntab_b[cpos(u)] = n_tau;
+          if (tid == 0 && ntab_b && u > u_out) ntab_b[cpos(u)] = n_tau;
           a_last = a;
           ++slot;
           WT_ADD(11);
@@ -634,8 +662,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       bar_arrive(bf ? kBarDone1 : kBarDone0, NPART);
     }
     WT_FLUSH(8);
-    // forward output: logZ = n(Lb) + log sum_c a[Lb,c]
-    if (dir == 0) {
+    // forward output: logZ = n(Lb) + log sum_c a[Lb,c] (the chunk that ends
+    // the sequence; a later chunk fix-up adds the chunk's offset)
+    if (dir == 0 && u_end == Lb) {
       const double s = group_sumd(cv ? a_last : 0.0);
       if (tid == 0) {
         const double lz = (Lb == 0 || !(s > 0.0)) ? (double)kRefNegInf : n_last + log(s);
@@ -643,6 +672,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (A.logz) A.logz[b] = lz;
       }
     }
+  }
+  // hand off the state at the end of a chunk that does not end the sequence
+  if (A.hand && u_end < Lb) {
+    __syncthreads();
+    export_state(1, u_end, tid, NT);
   }
 }
 

@@ -12,11 +12,11 @@
 //
 // Limits and rules:
 //  - The scratch holds the forward's prepared constants (the exponentiated
-//    transition and duration tables, about 8*C*C + 8*(K+16)*C bytes).  It is
-//    kNoallocScratchBytes (1 MiB) large.  Every shape the scan accepts fits
-//    (the largest, at C=256, need under 700 KiB); a problem whose forward
-//    workspace (semicrf_forward_workspace_size) exceeds 1 MiB is rejected with
-//    SEMICRF_ERR_WORKSPACE before any CUDA call.
+//    transition and duration tables, about 16*C*C + 8*(K+16)*C bytes in the
+//    log semiring).  It is kNoallocScratchBytes (2 MiB) large.  Every shape the
+//    scan accepts fits (the largest, at C=256, need about 1.3 MiB); a problem
+//    whose forward workspace (semicrf_forward_workspace_size) exceeds 2 MiB is
+//    rejected with SEMICRF_ERR_WORKSPACE before any CUDA call.
 //  - Nothing in the scratch has to start at zero: every byte the scan reads
 //    is first written by the preparation kernel of the same call, earlier on
 //    the same stream.
@@ -35,7 +35,7 @@
 
 namespace {
 
-constexpr size_t kNoallocScratchBytes = size_t(1) << 20;
+constexpr size_t kNoallocScratchBytes = size_t(2) << 20;
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];

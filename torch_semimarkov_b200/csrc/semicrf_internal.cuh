@@ -50,9 +50,13 @@ __device__ __forceinline__ void named_barrier(int id, int nthreads) {
 // ---------------------------------------------------------------------------
 struct Prepared {
   // mat-vec operand for the forward chain (M = transition) and the backward
-  // chain (M = transition^T).  Log semiring: exp(M - colmax); max: M.
+  // chain (M = transition^T): max semiring M (float32); log semiring
+  // exp(M - colmax) in float64 (mxd_*), together with dbed = exp(dbl - dbmax)
   float* mx_f;
   float* mx_b;
+  double* mxd_f;
+  double* mxd_b;
+  double* dbed;     // (KX, C), log semiring
   float* colmax_f;  // (C)
   float* colmax_b;
   float* dbl;       // (KX, C): log duration bias by duration k, -inf outside 1..kcap
@@ -112,7 +116,7 @@ struct LChainArgs {
   const float* ps;
   const float* pe;
   const int64_t* lengths;
-  const float* mx;       // exp(M - colmax), float32 (C*C)
+  const double* mx;      // exp(M - colmax), float64 (C*C)
   const float* colmax;   // (C)
   // forward outputs
   float* partition;
@@ -131,10 +135,21 @@ struct LChainArgs {
   double* a_tab;
   double* A_tab;
   double* n_tab;
+  // time chunks (lchain_ws only): the chain of a sequence is split into
+  // nchunk chunks of chunk_len positions (u); chunk j > 0 starts warm
+  // positions early from a uniform state and writes outputs only past
+  // j*chunk_len.  hand receives, per (sequence, chunk), the log sources of the
+  // last kcap positions at j*chunk_len (kind 0) and at the chunk's end (kind
+  // 1): [B][nchunk][2][kcap][C].
+  int nchunk;
+  int chunk_len;
+  int warm;
+  double* hand;
+  const int* only;  // if set, only sequences b with only[b] != 0 run
 };
 struct LChainLaunch {
   int B, T, K, C;
-  const float* dbe;    // (kx, C) exp(db - dbmax), zero outside durations 1..kcap
+  const double* dbe;   // (kx, C) exp(db - dbmax), zero outside durations 1..kcap
   const float* dbmax;  // (C)
   int n1;              // CTAs [0, n1) run a0, the rest a1
   LChainArgs a0;
@@ -143,6 +158,32 @@ struct LChainLaunch {
 cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s);
 // warp-specialised variant for C <= 64, whole-sequence chains (mode 0) only
 cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s);
+
+// time chunking of the float64 chains (lchunk.cu)
+struct ChunkPlan {
+  int nchunk, len, warm;
+};
+// chunks for B sequences (times nroles chains each) of length T; nchunk = 1
+// means no chunking.  warm_override > 0 forces chunking with that warm-up.
+ChunkPlan chunk_plan(int B, int T, int K, int C, int nroles, int warm_override);
+size_t chunk_hand_doubles(int B, int K, int C, const ChunkPlan& cp);
+// compares the boundary states, accumulates the per-chunk log offsets D, and
+// adds them to the tables (n_tab) and log Z; sequences whose states do not
+// agree get fail[b] = 1 and are left for a serial rerun
+struct ChunkFix {
+  int B, T, K, C, dir;
+  ChunkPlan cp;
+  const int64_t* lengths;
+  const double* hand;
+  double* rdiff;  // [B][nchunk]
+  int* okf;       // [B][nchunk]
+  double* D;      // [B][nchunk]
+  int* fail;      // [B]
+  double* n_tab;  // (B, T+1) or null
+  double* logz;   // (B) or null
+  float* partition;
+};
+cudaError_t launch_chunk_fix(const ChunkFix& f, cudaStream_t s);
 bool lchain_ws_supported(int C, int K);
 bool lchain_supported(int C, int K);
 size_t lchain_saved_doubles(int C, int K);       // restart record per checkpoint
