@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--no-viterbi", action="store_true")
     # smaller per-rank batches / sequences, e.g. for profiler captures of one
     # kernel; the benchmark line is only the configuration-2 number at the defaults
+    # only the configuration-5 Viterbi sub-benchmark (e.g. for a profiler)
+    ap.add_argument("--viterbi-only", action="store_true")
     ap.add_argument("--batch", type=int, default=B)
     ap.add_argument("--seq-len", type=int, default=T)
     return ap.parse_args()
@@ -208,6 +210,11 @@ def main():
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.viterbi_only:
+        if rank == 0:
+            flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+            print(json.dumps(bench_viterbi(dev, flush)), flush=True)
+        return
     if world > 1:
         import datetime
 
@@ -329,8 +336,13 @@ def main():
     del saved
 
     viterbi = None
+    others = {}
     if not args.no_viterbi and rank == 0:
         viterbi = bench_viterbi(dev, flush)
+        others["chromosome"] = bench_fwd_bwd(dev, flush, "cfg3", 1, 1_000_000, 1000, 8,
+                                             "cfg3: B=1 T=1e6 K=1000 C=8, one GPU")
+        others["large_C"] = bench_fwd_bwd(dev, flush, "cfg4", 32, 4096, 64, 256,
+                                          "cfg4: B=32 T=4096 K=64 C=256")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -397,9 +409,45 @@ def main():
     }
     if viterbi:
         line["viterbi"] = viterbi
+    line.update(others)
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def bench_fwd_bwd(dev, flush, gen, Bc, Tc, Kc, Cc, label):
+    """fwd+bwd positions/s of another configuration (inputs resident)."""
+    import torch
+
+    from inputs import config_lengths, make_streaming_inputs
+    from torch_semimarkov_b200 import semi_crf_streaming_forward
+
+    inp = make_streaming_inputs(Bc, Tc, Kc, Cc, seed=3, gen=gen)
+    cum = inp["cum_scores"].to(dev)
+    tr = inp["transition"].to(dev)
+    db = inp["duration_bias"].to(dev)
+    lengths = torch.full((Bc,), Tc, dtype=torch.int64, device=dev)
+
+    def one():
+        c = cum.detach().requires_grad_(True)
+        t = tr.detach().requires_grad_(True)
+        d = db.detach().requires_grad_(True)
+        semi_crf_streaming_forward(c, t, d, lengths, Kc).sum().backward()
+
+    for _ in range(2):
+        one()
+    ms = []
+    for _ in range(3):
+        flush.zero_()
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        one()
+        b_.record()
+        torch.cuda.synchronize()
+        ms.append(a.elapsed_time(b_))
+    t = statistics.mean(ms) / 1e3
+    return {"metric": "fwd+bwd positions/s", "value": Bc * Tc / t, "unit": UNIT,
+            "ms": t * 1e3, "config": label}
 
 
 def bench_viterbi(dev, flush):
