@@ -41,7 +41,7 @@ def assert_grad_close(got, ref, rtol=RTOL, floor=1e-6, what=""):
     assert err <= rtol * scale + floor, f"{what}: ||d||inf={err:.3e} ||ref||inf={scale:.3e}"
 
 
-STREAM = [n for n in golden_names("stream_") + golden_names("cfg") if "kcc" not in n]
+STREAM = golden_names("stream_") + golden_names("cfg")
 
 
 @pytest.mark.parametrize("name", STREAM)
@@ -79,7 +79,8 @@ def test_streaming_forward_backward_vs_reference(name):
 
 
 @pytest.mark.parametrize("name", ["stream_basic", "stream_ckpt_div", "stream_zero_len",
-                                  "stream_k1", "stream_c24", "stream_basic_max"])
+                                  "stream_k1", "stream_c24", "stream_basic_max", "stream_kcc",
+                                  "stream_kcc_max"])
 def test_ring_checkpoints_layout_and_values(name):
     from torch_semimarkov_b200 import launch_streaming_triton_kernel
 
@@ -273,13 +274,34 @@ def test_random_vs_oracle_recompute(case, oracle, monkeypatch):
     _random_vs_oracle(case, oracle)
 
 
-def _random_vs_oracle(case, oracle):
+# (K, C, C) transitions (kcc.cu): both semirings, projections, K > T, C = 1,
+# C > 32 (several row tiles of the transition marginals) and C*C too large for
+# the shared-memory copies of the transition factors
+KCC_CASES = [
+    (3, 60, 6, 5, "default", None, "log"),
+    (2, 80, 12, 24, "cfg2", "both", "log"),
+    (2, 50, 5, 40, "default", "start", "log"),
+    (2, 40, 4, 100, "default", None, "log"),
+    (3, 70, 9, 7, "cfg5", "end", "max"),
+    (2, 30, 40, 3, "default", None, "log"),
+    (2, 50, 2, 1, "default", None, "log"),
+    (2, 300, 64, 16, "default", None, "log"),
+    (2, 64, 33, 9, "default", "both", "max"),
+]
+
+
+@pytest.mark.parametrize("case", KCC_CASES)
+def test_kcc_transitions_vs_oracle(case, oracle):
+    _random_vs_oracle(case, oracle, kcc=True)
+
+
+def _random_vs_oracle(case, oracle, kcc=False):
     from inputs import make_streaming_inputs
 
     from torch_semimarkov_b200 import semi_crf_streaming_forward
 
     B, T, K, C, gen, proj, semiring = case
-    inp = make_streaming_inputs(B, T, K, C, seed=100 + T + K + C, gen=gen, proj=proj)
+    inp = make_streaming_inputs(B, T, K, C, seed=100 + T + K + C, gen=gen, proj=proj, kcc=kcc)
     rng = np.random.default_rng(T)
     lengths = np.concatenate([[T], rng.integers(max(1, T // 3), T + 1, size=B - 1)])
     gout = rng.uniform(0.5, 1.5, size=B)

@@ -141,3 +141,28 @@ def test_lib_has_no_oracle_dependency():
             if f.endswith((".py", ".cu", ".cuh", ".h")):
                 txt = open(os.path.join(dirpath, f)).read()
                 assert "oracle" not in txt.lower().replace("oracles", ""), f
+
+
+def test_kcc_shapes_and_sizes():
+    """(K, C, C) transitions: accepted shapes, saved tables, rejections."""
+    from torch_semimarkov_b200 import _lib
+
+    lib = _lib.load()
+    B, T, K, C = 2, 100, 6, 5
+    p = _problem(batch=B, T=T, K=K, C=C, transition_ndim=3)
+    # saved: log Z, log alpha, the row maxima of alpha and log beta (float64)
+    n = B * (T + 1)
+    assert lib.semicrf_saved_size(ctypes.byref(p)) >= 8 * (B + 2 * n * C + n)
+    # forward workspace: exp(tr) factors in both directions plus three (K, C) tables
+    assert lib.semicrf_forward_workspace_size(ctypes.byref(p)) >= 8 * (2 * K * C * C + 3 * K * C)
+    assert lib.semicrf_backward_workspace_size(ctypes.byref(p)) >= 8 * 2 * n * C
+    # transition[k] is read for k = 1 .. K-1, so K = 1 has no usable matrix
+    p1 = _problem(batch=B, T=T, K=1, C=C, transition_ndim=3, checkpoint_interval=10)
+    assert lib.semicrf_forward_workspace_size(ctypes.byref(p1)) == 0
+    assert lib.semicrf_forward(ctypes.byref(p1), None, None, 0, None, None, 0, None) == 2
+    # the Viterbi head takes (C, C) transitions only
+    pv = _problem(batch=B, T=T, K=K, C=C, transition_ndim=3, semiring=1)
+    assert lib.semicrf_viterbi_workspace_size(ctypes.byref(pv)) == 0
+    # a ring window too large for one CTA's shared memory is refused up front
+    big = _problem(batch=B, T=T, K=2000, C=64, transition_ndim=3, checkpoint_interval=2000)
+    assert lib.semicrf_forward(ctypes.byref(big), None, None, 0, None, None, 0, None) == 2

@@ -44,9 +44,10 @@ int validate_shape(const semicrf_problem* p) {
   if (p->transition_ndim != 2 && p->transition_ndim != 3) return SEMICRF_ERR_INVALID_ARGUMENT;
   if (p->checkpoint_interval < p->K) return SEMICRF_ERR_INVALID_ARGUMENT;
   if (p->C > 256 || p->T > (int64_t)1 << 30 || p->K > 32767) return SEMICRF_ERR_UNSUPPORTED;
-  if (p->transition_ndim == 3) return SEMICRF_ERR_UNSUPPORTED;
   if (p->backward_mode != SEMICRF_KEEP_ALPHA && p->backward_mode != SEMICRF_RECOMPUTE)
     return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (p->transition_ndim == 3)  // duration-dependent transitions: kcc.cu
+    return kcc_supported((int)p->C, (int)p->K) ? SEMICRF_OK : SEMICRF_ERR_UNSUPPORTED;
   if (p->semiring == SEMICRF_LOG && !lchain_supported((int)p->C, (int)p->K))
     return SEMICRF_ERR_UNSUPPORTED;
   if (p->semiring == SEMICRF_LOG && !lmarg_plan(1, 1, (int)p->K, (int)p->C).ok)
@@ -110,7 +111,13 @@ SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
   const size_t B = p->batch, C = p->C;
   const size_t kc = kcap_of(p->K), nint = nint_of(p);
   s.logz = cv.take<double>(B);
-  if (p->semiring == SEMICRF_MAX) {
+  if (p->transition_ndim == 3) {
+    // (K, C, C): log alpha, its row maxima and log beta, whatever the mode
+    const size_t n = B * (p->T + 1) * C;
+    s.a_tab = cv.take<double>(n);
+    s.n_tab = cv.take<double>(B * (p->T + 1));
+    s.b_tab = cv.take<double>(n);
+  } else if (p->semiring == SEMICRF_MAX) {
     s.sv_f = cv.take<float>(B * nint * (kc * C + 2 * C));
     s.sv_d = cv.take<double>(B * nint * kc);
   } else if (p->backward_mode == SEMICRF_RECOMPUTE) {
@@ -299,6 +306,45 @@ VitLayout carve_vit(Carver& cv, const semicrf_problem* p) {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? SEMICRF_OK : SEMICRF_ERR_CUDA; }
 
+// (K, C, C) transitions: prepared factors, then (backward) the marginal terms
+struct KccLayout {
+  KccPrep pr;
+  double *st, *et, *pend, *part_tr;
+  int nslice;
+};
+
+KccLayout carve_kcc(Carver& cv, const semicrf_problem* p, bool backward) {
+  KccLayout w{};
+  const int K = (int)p->K, C = (int)p->C;
+  w.pr = kcc_prep_carve(cv.take<double>(kcc_prep_doubles(K, C)), K, C);
+  if (!backward) return w;
+  const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
+  w.st = cv.take<double>(n);
+  w.et = cv.take<double>(n);
+  w.pend = p->semiring == SEMICRF_MAX ? cv.take<double>(n) : nullptr;
+  w.nslice = kcc_tr_slices((int)p->batch, K, C);
+  w.part_tr = cv.take<double>((size_t)w.nslice * C * (size_t)(K - 1) * C);
+  return w;
+}
+
+KccArgs kcc_args(const semicrf_problem* p, const KccPrep& pr) {
+  KccArgs a{};
+  a.B = (int)p->batch;
+  a.T = (int)p->T;
+  a.K = (int)p->K;
+  a.C = (int)p->C;
+  a.kcap = kcap_of(p->K);
+  a.semiring = p->semiring;
+  a.cum = p->cum_scores;
+  a.tr = p->transition;
+  a.db = p->duration_bias;
+  a.ps = p->proj_start;
+  a.pe = p->proj_end;
+  a.lengths = p->lengths;
+  a.pr = pr;
+  return a;
+}
+
 VChainArgs vchain_args(const semicrf_problem* p) {
   VChainArgs v{};
   v.B = (int)p->batch;
@@ -347,7 +393,10 @@ size_t semicrf_saved_size(const semicrf_problem* p) {
 size_t semicrf_forward_workspace_size(const semicrf_problem* p) {
   if (validate_shape(p) != SEMICRF_OK) return 0;
   Carver cv(nullptr);
-  carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
+  if (p->transition_ndim == 3)
+    carve_kcc(cv, p, false);
+  else
+    carve_prep(cv, (int)p->C, (int)p->K, p->semiring);
   return cv.bytes();
 }
 
@@ -362,6 +411,29 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
   if (workspace_bytes < semicrf_forward_workspace_size(p) || !workspace)
     return SEMICRF_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->transition_ndim == 3) {
+    // (K, C, C): the alpha chain, and beside it the beta chain when a
+    // backward will follow (both tables are kept)
+    Carver cv(workspace);
+    KccLayout w = carve_kcc(cv, p, false);
+    cudaError_t e = launch_kcc_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
+                                    p->semiring, w.pr, s);
+    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+    KccArgs a = kcc_args(p, w.pr);
+    a.partition = partition;
+    a.ref_ckpt = ring_checkpoints;
+    a.nref = (int)num_ring_checkpoints;
+    a.sref = (int)p->checkpoint_interval;
+    if (saved) {
+      Carver sc(saved);
+      SavedLayout sl = carve_saved(sc, p);
+      a.logz = sl.logz;
+      a.alpha = sl.a_tab;
+      a.amax = sl.n_tab;
+      a.beta = sl.b_tab;
+    }
+    return cuda_status(launch_kcc_chains(a, saved ? 2 : 1, s));
+  }
   if (p->semiring == SEMICRF_MAX && !saved && !ring_checkpoints &&
       vchain_supported((int)p->batch, (int)p->C, (int)p->K)) {
     // score only: one warp per sequence, no prepared tables needed
@@ -453,7 +525,9 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
 size_t semicrf_backward_workspace_size(const semicrf_problem* p) {
   if (validate_shape(p) != SEMICRF_OK) return 0;
   Carver cv(nullptr);
-  if (p->semiring == SEMICRF_LOG)
+  if (p->transition_ndim == 3)
+    carve_kcc(cv, p, true);
+  else if (p->semiring == SEMICRF_LOG)
     carve_lbwd(cv, p);
   else
     carve_bwd(cv, p);
@@ -474,6 +548,30 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
   if (workspace_bytes < semicrf_backward_workspace_size(p) || !workspace)
     return SEMICRF_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->transition_ndim == 3) {
+    Carver cv(workspace);
+    KccLayout w = carve_kcc(cv, p, true);
+    Carver sc(const_cast<void*>(saved));
+    SavedLayout sl = carve_saved(sc, p);
+    cudaError_t e = launch_kcc_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
+                                    p->semiring, w.pr, s);
+    if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+    KccArgs a = kcc_args(p, w.pr);
+    a.logz = sl.logz;
+    a.alpha = sl.a_tab;
+    a.amax = sl.n_tab;
+    a.beta = sl.b_tab;
+    a.grad_output = grad_output;
+    a.grad_cum = grad_cum;
+    a.grad_ps = p->proj_start ? grad_proj_start : nullptr;
+    a.grad_pe = p->proj_end ? grad_proj_end : nullptr;
+    a.st = w.st;
+    a.et = w.et;
+    a.pend = w.pend;
+    a.part_tr = w.part_tr;
+    a.nslice = w.nslice;
+    return cuda_status(launch_kcc_grads(a, grad_transition, grad_duration_bias, s));
+  }
   if (p->semiring == SEMICRF_LOG) {
     Carver cv(workspace);
     LBwdLayout w = carve_lbwd(cv, p);
@@ -636,7 +734,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
 }
 
 size_t semicrf_viterbi_workspace_size(const semicrf_problem* p) {
-  if (validate_shape(p) != SEMICRF_OK) return 0;
+  if (validate_shape(p) != SEMICRF_OK || p->transition_ndim != 2) return 0;
   Carver cv(nullptr);
   carve_vit(cv, p);
   return cv.bytes();
@@ -647,6 +745,7 @@ int semicrf_viterbi(const semicrf_problem* p, int64_t max_traceback_length, floa
                     int32_t* nseg, void* workspace, size_t workspace_bytes, void* stream) {
   int st = validate(p);
   if (st != SEMICRF_OK) return st;
+  if (p->transition_ndim != 2) return SEMICRF_ERR_UNSUPPORTED;  // nn.py:460 takes (C, C)
   if (p->batch == 0) return SEMICRF_OK;
   if (p->semiring != SEMICRF_MAX) return SEMICRF_ERR_SEMIRING;
   if (p->proj_start || p->proj_end) return SEMICRF_ERR_UNSUPPORTED;  // nn.py:479 has none

@@ -280,6 +280,51 @@ struct VChainArgs {
 bool vchain_supported(int B, int C, int K);
 cudaError_t launch_vchain(const VChainArgs& a, cudaStream_t s);
 
+// kcc.cu -- duration-dependent transitions, transition of shape (K, C, C)
+struct KccPrep {
+  double* ef;   // (K, C, C) exp(tr[k][c',c] - tf[k][c])        (forward chain, marginals)
+  double* eb;   // (K, C, C) [k][c2][c] = exp(tr[k][c,c2] - tb[k][c])   (beta chain)
+  double* tf;   // (K, C) max over c' of tr[k][c',c]
+  double* tb;   // (K, C) max over c2 of tr[k][c,c2]
+  double* tdf;  // (K, C) log semiring: tf + db; max semiring: db
+};
+struct KccArgs {
+  int B, T, K, C, kcap, semiring;
+  const float* cum;
+  const float* tr;
+  const float* db;
+  const float* ps;
+  const float* pe;
+  const int64_t* lengths;
+  KccPrep pr;
+  // chain outputs: log tables (B, T+1, C), row maxima of alpha (B, T+1)
+  double* alpha;
+  double* amax;
+  double* beta;
+  double* logz;
+  float* partition;
+  float* ref_ckpt;
+  int nref, sref;
+  // backward
+  const float* grad_output;
+  float* grad_cum;
+  float* grad_ps;
+  float* grad_pe;
+  double* st;       // (B, T+1, C) start terms of the marginals
+  double* et;       // (B, T+1, C) end terms of the marginals
+  double* pend;     // max semiring: end marginals (B, T+1, C)
+  double* part_tr;  // (nslice, C, kcap*C) partial sums of the transition marginals
+  int nslice;
+};
+bool kcc_supported(int C, int K);
+size_t kcc_prep_doubles(int K, int C);
+KccPrep kcc_prep_carve(double* base, int K, int C);
+int kcc_tr_slices(int B, int K, int C);
+cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, int semiring,
+                            const KccPrep& pr, cudaStream_t s);
+cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s);
+cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, cudaStream_t s);
+
 // viterbi.cu
 // backtrace over the packed backpointers of vchain.cu
 size_t backtrace_packed_smem(int T, int C);
