@@ -40,7 +40,7 @@ REF_SRC = os.environ.get("TORCH_SEMIMARKOV_REF_SRC", "/root/reference/src")
 if REF_SRC not in sys.path:
     sys.path.insert(0, REF_SRC)
 
-from torch_semimarkov import SemiMarkovCRFHead  # noqa: E402
+from torch_semimarkov import SemiMarkovCRFHead, UncertaintySemiMarkovCRFHead  # noqa: E402
 from torch_semimarkov.helpers import score_gold_vectorized  # noqa: E402
 from torch_semimarkov.streaming import (  # noqa: E402
     semi_crf_streaming_forward,
@@ -221,6 +221,56 @@ def run_head_case(name, spec):
 
 
 # ---------------------------------------------------------------------------
+# Uncertainty cases (reference uncertainty.py, float32 CPU path)
+# ---------------------------------------------------------------------------
+
+UNCERT_CASES = {
+    "uncert_basic": dict(B=3, T=40, K=6, C=4, lengths=[40, 25, 9], seed=51),
+    "uncert_proj": dict(B=2, T=60, K=8, C=5, lengths=[60, 33], seed=52, hidden=16),
+}
+
+
+def run_uncert_case(name, spec):
+    t0 = time.time()
+    B, T, K, C = spec["B"], spec["T"], spec["K"], spec["C"]
+    hidden_dim = spec.get("hidden")
+    torch.manual_seed(spec["seed"])
+    crf = UncertaintySemiMarkovCRFHead(num_classes=C, max_duration=K, hidden_dim=hidden_dim)
+    params = make_hidden(B, T, C, K, spec["seed"], "default", hidden_dim)
+    with torch.no_grad():
+        crf.transition.copy_(params["transition"])
+        crf.duration_dist.duration_bias.copy_(params["duration_bias"])
+        if hidden_dim is not None:
+            crf.projection.weight.copy_(params["proj_weight"])
+            crf.projection.bias.copy_(params["proj_bias"])
+    hidden = params["hidden"]
+    lengths = torch.tensor(spec["lengths"], dtype=torch.long)
+    labels = params["labels"]
+    out = {
+        "boundary": _np(crf.compute_boundary_marginals(hidden, lengths)),
+        "boundary_raw": _np(crf.compute_boundary_marginals(hidden, lengths, normalize=False)),
+        "position": _np(crf.compute_position_marginals(hidden, lengths)),
+        "entropy": _np(crf.compute_entropy_streaming(hidden, lengths)),
+        "loss_boundary": _np(crf.compute_loss_uncertainty_weighted(
+            hidden, lengths, labels, uncertainty_weight=0.5, focus_mode="boundary_regions",
+            reduction="none")),
+    }
+    loss = crf.compute_loss_uncertainty_weighted(hidden, lengths, labels, reduction="sum")
+    loss.backward()
+    out["loss_high_sum"] = float(loss.detach())
+    out["grad_transition"] = _np(crf.transition.grad)
+    out["grad_duration_bias"] = _np(crf.duration_dist.duration_bias.grad)
+    if hidden_dim is not None:
+        out["grad_proj_weight"] = _np(crf.projection.weight.grad)
+    save(name, B=B, T=T, K=K, C=C, seed=spec["seed"],
+         hidden_dim=-1 if hidden_dim is None else hidden_dim, lengths=lengths.numpy(),
+         labels=labels.numpy(), hidden=_np(hidden), transition=_np(params["transition"]),
+         duration_bias=_np(params["duration_bias"]), proj_weight=_np(params.get("proj_weight")),
+         proj_bias=_np(params.get("proj_bias")), **out)
+    print(f"  {name}: {time.time() - t0:.1f}s")
+
+
+# ---------------------------------------------------------------------------
 # Gold scoring cases (float64)
 # ---------------------------------------------------------------------------
 
@@ -269,6 +319,9 @@ def main(argv):
     for name, spec in GOLD_CASES.items():
         if not want or name in want:
             run_gold_case(name, spec)
+    for name, spec in UNCERT_CASES.items():
+        if not want or name in want:
+            run_uncert_case(name, spec)
 
 
 if __name__ == "__main__":

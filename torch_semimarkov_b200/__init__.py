@@ -20,6 +20,7 @@ from .streaming import (
     launch_streaming_triton_kernel,
     semi_crf_streaming_forward,
 )
+from .uncertainty import UncertaintyMixin, UncertaintySemiMarkovCRFHead
 
 __version__ = "0.2.0+b200"
 
@@ -38,4 +39,6 @@ __all__ = [
     "launch_streaming_triton_kernel",
     "launch_streaming_triton_backward",
     "NEG_INF",
+    "UncertaintyMixin",
+    "UncertaintySemiMarkovCRFHead",
 ]
