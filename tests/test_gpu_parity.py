@@ -275,8 +275,9 @@ def test_random_vs_oracle_recompute(case, oracle, monkeypatch):
 
 
 # (K, C, C) transitions (kcc.cu): both semirings, projections, K > T, C = 1,
-# C > 32 (several row tiles of the transition marginals) and C*C too large for
-# the shared-memory copies of the transition factors
+# C > 32 (several row tiles of the transition marginals), factors resident in
+# shared memory, streamed through it in chunks (K*C*C large), and read
+# directly from L2 (C = 130)
 KCC_CASES = [
     (3, 60, 6, 5, "default", None, "log"),
     (2, 80, 12, 24, "cfg2", "both", "log"),
@@ -287,6 +288,9 @@ KCC_CASES = [
     (2, 50, 2, 1, "default", None, "log"),
     (2, 300, 64, 16, "default", None, "log"),
     (2, 64, 33, 9, "default", "both", "max"),
+    (2, 30, 3, 130, "default", None, "log"),
+    (2, 150, 120, 20, "cfg2", None, "log"),
+    (2, 90, 70, 24, "default", None, "max"),
 ]
 
 

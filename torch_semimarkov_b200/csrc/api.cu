@@ -316,7 +316,8 @@ struct KccLayout {
 KccLayout carve_kcc(Carver& cv, const semicrf_problem* p, bool backward) {
   KccLayout w{};
   const int K = (int)p->K, C = (int)p->C;
-  w.pr = kcc_prep_carve(cv.take<double>(kcc_prep_doubles(K, C)), K, C);
+  w.pr = kcc_prep_carve(cv.take<double>(kcc_prep_doubles(K, C, p->semiring)), K, C,
+                        p->semiring);
   if (!backward) return w;
   const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
   w.st = cv.take<double>(n);

@@ -43,13 +43,25 @@ __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
   return l < 0 ? 0 : (l > T ? T : (int)l);
 }
 
-__device__ __forceinline__ void online_lse(double& m, double& s, double x) {
+// running sum of v * exp(x), kept as (m, s) with value s * exp(m); v in [0, C]
+__device__ __forceinline__ void online_add(double& m, double& s, double x, double v) {
   if (x > m) {
-    s = s * exp(m - x) + 1.0;
+    s = s * exp(m - x) + v;
     m = x;
   } else {
-    s += exp(x - m);
+    s += v * exp(x - m);
   }
+}
+
+__device__ __forceinline__ void cp_async8(double* dst, const double* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait1() {
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
 }
 
 __global__ void kcc_prep_kernel(const float* __restrict__ tr, const float* __restrict__ db, int K,
@@ -67,51 +79,77 @@ __global__ void kcc_prep_kernel(const float* __restrict__ tr, const float* __res
     pr.tb[i] = mb;
     pr.tdf[i] = mf + (double)db[i];
     for (int q = 0; q < C; ++q) {
-      pr.ef[((size_t)k * C + q) * C + c] = exp((double)m[q * C + c] - mf);
-      pr.eb[((size_t)k * C + q) * C + c] = exp((double)m[c * C + q] - mb);
+      const size_t j = ((size_t)k * C + q) * C + c;
+      pr.ef[j] = exp((double)m[q * C + c] - mf);
+      pr.eb[j] = exp((double)m[c * C + q] - mb);
+      if (pr.rf) {
+        pr.rf[j] = (double)m[q * C + c];
+        pr.rb[j] = (double)m[c * C + q];
+      }
     }
   }
 }
 
-// shared memory of the chain kernel, offsets in doubles
-struct ChainSmem {
-  size_t ring, rn, xs, xm, dt, vals, redm, reds, efs, total;
+// Shared memory of the chain kernel (offsets in doubles).  The per-duration
+// C x C factors E[k] are resident when all K of them fit; otherwise they are
+// streamed from L2 in chunks of kc durations through two cp.async buffers, or,
+// when not even two single-duration buffers fit (C > ~110), read from L2.
+struct ChainPlan {
+  int kc, resident, direct;
+  size_t ring, rn, xs, xm, dt, vals, redm, reds, eb, total;
 };
-__host__ __device__ inline ChainSmem chain_smem(int C, int K, bool ef_smem) {
-  ChainSmem s{};
+__host__ __device__ inline ChainPlan chain_plan(int C, int K) {
+  ChainPlan p{};
+  const size_t cc = (size_t)C * C;
+  const int kcap = K - 1;
   size_t o = 0;
-  s.ring = o;
+  p.ring = o;
   o += (size_t)K * C;
-  s.rn = o;
+  p.rn = o;
   o += K;
-  s.xs = o;
+  p.xs = o;
   o += (size_t)kKC * C;
-  s.xm = o;
+  p.xm = o;
   o += kKC;
-  s.dt = o;
+  p.dt = o;
   o += C;
-  s.vals = o;
+  p.vals = o;
   o += C;
-  s.redm = o;
+  p.redm = o;
   o += kKT;
-  s.reds = o;
+  p.reds = o;
   o += kKT;
-  s.efs = o;
-  if (ef_smem) o += (size_t)K * C * C;
-  s.total = o;
-  return s;
+  p.eb = o;
+  const size_t cap = kSmemMax / 8;
+  if (o + (size_t)K * cc <= cap) {
+    p.resident = 1;
+    p.kc = kKC < kcap ? kKC : kcap;
+    o += (size_t)K * cc;
+  } else if (o + 2 * cc <= cap) {
+    size_t kc = (cap - o) / (2 * cc);
+    if (kc > (size_t)kKC) kc = kKC;
+    if (kc > (size_t)kcap) kc = kcap;
+    p.kc = (int)kc;
+    o += 2 * kc * cc;
+  } else {
+    p.direct = 1;
+    p.kc = kKC < kcap ? kKC : kcap;
+  }
+  p.total = o;
+  return p;
 }
 
 // One CTA per (sequence, direction).  Writes log alpha and its row maxima
 // (dir 0) or log beta (dir 1) for positions 0 .. len when the tables are given.
 template <int SEMI>
-__global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_smem) {
+__global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
   extern __shared__ __align__(16) double ksm[];
   const int C = a.C, K = a.K, T = a.T, kcap = a.kcap, R = K;
   const int b = blockIdx.x, dir = blockIdx.y, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int Lb = seq_len(a.lengths, b, T);
-  const ChainSmem sp = chain_smem(C, K, ef_smem != 0);
+  const ChainPlan sp = chain_plan(C, K);
+  const size_t cc = (size_t)C * C;
   double* ring = ksm + sp.ring;  // dir 0: alpha rows (linear for log); dir 1: log source rows
   double* rn = ksm + sp.rn;      // dir 0: row maxima of alpha
   double* xs = ksm + sp.xs;      // dir 1: one chunk of duration source rows
@@ -120,6 +158,7 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
   double* vals = ksm + sp.vals;
   double* redm = ksm + sp.redm;
   double* reds = ksm + sp.reds;
+  double* ebuf = ksm + sp.eb;
   __shared__ double s_m;
   const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
   const float* ps_b = a.ps ? a.ps + (size_t)b * T * C : nullptr;
@@ -131,12 +170,13 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
   auto pev = [&](int t, int c) {
     return (pe_b && t >= 1) ? (double)pe_b[(size_t)(t - 1) * C + c] : 0.0;
   };
-  const double* E = dir == 0 ? a.pr.ef : a.pr.eb;
-  if (SEMI == 0 && ef_smem) {
-    double* efs = ksm + sp.efs;
-    for (size_t i = tid; i < (size_t)K * C * C; i += kKT) efs[i] = E[i];
-    E = efs;
-  }
+  // E[k][q][c]: log semiring exp(tr - max) factors, max semiring raw tr, in the
+  // orientation of this direction
+  const double* Eg = SEMI == 0 ? (dir == 0 ? a.pr.ef : a.pr.eb) : (dir == 0 ? a.pr.rf : a.pr.rb);
+  const bool resident = sp.resident != 0 || sp.direct != 0;  // no staging either way
+  const double* Eall = sp.direct ? Eg : ebuf;
+  if (sp.resident)
+    for (size_t i = tid; i < (size_t)K * cc; i += kKT) ebuf[i] = Eg[i];
   if (dir == 0 && a.ref_ckpt) {
     float* rc = a.ref_ckpt + (size_t)b * a.nref * K * C;
     for (size_t i = tid; i < (size_t)a.nref * K * C; i += kKT)
@@ -145,6 +185,32 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
   const int nks = kKT / C;  // threads per label
   const int c = tid % C, ks = tid / C;
   const bool act = ks < nks;
+  // durations per chunk: all at once (forward, resident), else the x-row / staging chunk
+  const int cs = (sp.resident && dir == 0) ? kcap : sp.kc;
+  int par = 0;  // staging buffer holding the current chunk
+  auto issue = [&](int k0, int nk, int q) {
+    double* dst = ebuf + (size_t)q * sp.kc * cc;
+    const double* src = Eg + (size_t)k0 * cc;
+    const int n = nk * (int)cc;
+    for (int i = tid; i < n; i += kKT) cp_async8(dst + i, src + i);
+    cp_async_commit();
+  };
+  // E rows of duration k inside the current chunk starting at k0
+  auto erow = [&](int k, int k0) -> const double* {
+    return resident ? Eall + (size_t)k * cc
+                    : ebuf + (size_t)par * sp.kc * cc + (size_t)(k - k0) * cc;
+  };
+  // before a chunk: queue the next one (of this or the next position), wait for this one
+  auto stage = [&](int k0, int kmax, int tnext, int kmax_next) {
+    if (resident) return;
+    if (k0 + cs <= kmax)
+      issue(k0 + cs, min(cs, kmax - (k0 + cs) + 1), par ^ 1);
+    else if (tnext >= 0)
+      issue(1, min(cs, kmax_next), par ^ 1);
+    else
+      cp_async_commit();
+    cp_async_wait1();
+  };
 
   // vals[] holds position t's log values: store them in the ring and tables
   auto finish = [&](int t) {
@@ -206,41 +272,65 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
     }
     __syncthreads();
   };
+  // dot product of a source row with column c of E[k] (stride C)
+  auto dot = [&](const double* x, const double* e) {
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    int q = 0;
+    for (; q + 3 < C; q += 4) {
+      a0 = fma(x[q], e[(size_t)q * C], a0);
+      a1 = fma(x[q + 1], e[(size_t)(q + 1) * C], a1);
+      a2 = fma(x[q + 2], e[(size_t)(q + 2) * C], a2);
+      a3 = fma(x[q + 3], e[(size_t)(q + 3) * C], a3);
+    }
+    for (; q < C; ++q) a0 = fma(x[q], e[(size_t)q * C], a0);
+    return (a0 + a1) + (a2 + a3);
+  };
+  auto vmax = [&](const double* x, const double* e) {
+    double mp = -INFINITY;
+    for (int q = 0; q < C; ++q) mp = fmax(mp, x[q] + e[(size_t)q * C]);
+    return mp;
+  };
+  // a dot product too small to scale by exp(x - m) alone moves into x
+  auto add_dot = [&](double& m, double& S, double x, double acc) {
+    if (!(acc > 0.0)) return;
+    if (acc < 1e-280)
+      online_add(m, S, x + log(acc), 1.0);
+    else
+      online_add(m, S, x, acc);
+  };
 
   for (int q = tid; q < C; q += kKT) vals[q] = 0.0;  // alpha[0] = 0, beta[len] = 0
   __syncthreads();
   if (dir == 0) {
     finish(0);
+    if (!resident && Lb >= 1) issue(1, 1, par);
     for (int t = 1; t <= Lb; ++t) {
       const int kmax = t < kcap ? t : kcap;
-      double m = -INFINITY, ssum = 0.0;
-      if (act)
-        for (int k = 1 + ks; k <= kmax; k += nks) {
-          const int s = t - k, slot = s % R;
-          const double* src = ring + (size_t)slot * C;
-          if (SEMI == 0) {
-            const double* e = E + (size_t)k * C * C + c;
-            double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-            int q = 0;
-            for (; q + 3 < C; q += 4) {
-              a0 = fma(src[q], e[(size_t)q * C], a0);
-              a1 = fma(src[q + 1], e[(size_t)(q + 1) * C], a1);
-              a2 = fma(src[q + 2], e[(size_t)(q + 2) * C], a2);
-              a3 = fma(src[q + 3], e[(size_t)(q + 3) * C], a3);
+      const int tn = t + 1 <= Lb ? t + 1 : -1;
+      const int kmax_n = tn > 0 ? (tn < kcap ? tn : kcap) : 0;
+      double m = -INFINITY, S = 0.0;
+      for (int k0 = 1; k0 <= kmax; k0 += cs) {
+        const int nk = min(cs, kmax - k0 + 1);
+        stage(k0, kmax, tn, kmax_n);
+        if (!resident) __syncthreads();
+        if (act)
+          for (int kk = ks; kk < nk; kk += nks) {
+            const int k = k0 + kk, s = t - k, slot = s % R;
+            const double* src = ring + (size_t)slot * C;
+            const double* e = erow(k, k0) + c;
+            if (SEMI == 0) {
+              add_dot(m, S, rn[slot] + a.pr.tdf[k * C + c] + psv(s, c) - cu(s, c), dot(src, e));
+            } else {
+              const double mp = vmax(src, e);
+              if (mp > -INFINITY) m = fmax(m, mp + (double)a.db[k * C + c] + psv(s, c) - cu(s, c));
             }
-            for (; q < C; ++q) a0 = fma(src[q], e[(size_t)q * C], a0);
-            const double acc = (a0 + a1) + (a2 + a3);
-            if (!(acc > 0.0)) continue;
-            online_lse(m, ssum, rn[slot] + a.pr.tdf[k * C + c] + log(acc) + psv(s, c) - cu(s, c));
-          } else {
-            const float* tk = a.tr + (size_t)k * C * C + c;
-            double mp = -INFINITY;
-            for (int q = 0; q < C; ++q) mp = fmax(mp, src[q] + (double)tk[(size_t)q * C]);
-            if (!(mp > -INFINITY)) continue;
-            m = fmax(m, mp + (double)a.db[k * C + c] + psv(s, c) - cu(s, c));
           }
+        if (!resident) {
+          __syncthreads();
+          par ^= 1;
         }
-      combine(m, ssum, t);
+      }
+      combine(m, S, t);
       finish(t);
     }
     if (tid == 0) {
@@ -251,9 +341,9 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
         if (M > -INFINITY) {
           lz = M;
           if (SEMI == 0) {
-            double S = 0.0;
-            for (int q = 0; q < C; ++q) S += exp(vals[q] - M);
-            lz = M + log(S);
+            double Sz = 0.0;
+            for (int q = 0; q < C; ++q) Sz += exp(vals[q] - M);
+            lz = M + log(Sz);
           }
         }
       }
@@ -262,13 +352,17 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
     }
   } else {
     finish(Lb);
+    if (!resident && Lb >= 1) issue(1, 1, par);
     for (int t = Lb - 1; t >= 0; --t) {
       const int kmax = (Lb - t) < kcap ? (Lb - t) : kcap;
+      const int tn = t - 1;
+      const int kmax_n = tn >= 0 ? ((Lb - tn) < kcap ? (Lb - tn) : kcap) : 0;
       for (int q = tid; q < C; q += kKT) dt[q] = psv(t, q) - cu(t, q);
       __syncthreads();
-      double m = -INFINITY, ssum = 0.0;
-      for (int k0 = 1; k0 <= kmax; k0 += kKC) {
-        const int nkc = (kmax - k0 + 1) < kKC ? (kmax - k0 + 1) : kKC;
+      double m = -INFINITY, S = 0.0;
+      for (int k0 = 1; k0 <= kmax; k0 += cs) {
+        const int nkc = min(cs, kmax - k0 + 1);
+        stage(k0, kmax, tn, kmax_n);
         // the source rows of this chunk of durations, one warp per row
         for (int kk = warp; kk < nkc; kk += kKT / 32) {
           const int k = k0 + kk;
@@ -292,31 +386,17 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a, int ef_
           for (int kk = ks; kk < nkc; kk += nks) {
             const int k = k0 + kk;
             const double* x = xs + kk * C;
+            const double* e = erow(k, k0) + c;
             if (SEMI == 0) {
-              if (!(xm[kk] > -INFINITY)) continue;
-              const double* e = E + (size_t)k * C * C + c;
-              double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-              int q = 0;
-              for (; q + 3 < C; q += 4) {
-                a0 = fma(x[q], e[(size_t)q * C], a0);
-                a1 = fma(x[q + 1], e[(size_t)(q + 1) * C], a1);
-                a2 = fma(x[q + 2], e[(size_t)(q + 2) * C], a2);
-                a3 = fma(x[q + 3], e[(size_t)(q + 3) * C], a3);
-              }
-              for (; q < C; ++q) a0 = fma(x[q], e[(size_t)q * C], a0);
-              const double acc = (a0 + a1) + (a2 + a3);
-              if (!(acc > 0.0)) continue;
-              online_lse(m, ssum, xm[kk] + a.pr.tb[k * C + c] + log(acc));
+              if (xm[kk] > -INFINITY) add_dot(m, S, xm[kk] + a.pr.tb[k * C + c], dot(x, e));
             } else {
-              const float* tk = a.tr + ((size_t)k * C + c) * C;
-              double mp = -INFINITY;
-              for (int q = 0; q < C; ++q) mp = fmax(mp, x[q] + (double)tk[q]);
-              m = fmax(m, mp);
+              m = fmax(m, vmax(x, e));
             }
           }
         __syncthreads();
+        if (!resident) par ^= 1;
       }
-      combine(m, ssum, t);
+      combine(m, S, t);
       finish(t);
     }
   }
@@ -606,13 +686,17 @@ int grid_for(size_t n, int threads) {
 
 bool kcc_supported(int C, int K) {
   if (K < 2 || C < 1 || C > kKT) return false;  // transition[k] is used for k = 1 .. K-1
-  if (chain_smem(C, K, false).total * 8 > kSmemMax) return false;
+  const ChainPlan cp = chain_plan(C, K);
+  if (cp.kc < 1 || cp.total * 8 > kSmemMax) return false;
   return pos_plan(C, K - 1).total * 8 <= kSmemMax;
 }
 
-size_t kcc_prep_doubles(int K, int C) { return 2 * (size_t)K * C * C + 3 * (size_t)K * C; }
+size_t kcc_prep_doubles(int K, int C, int semiring) {
+  const size_t kcc = (size_t)K * C * C;
+  return (semiring == SEMICRF_MAX ? 4 : 2) * kcc + 3 * (size_t)K * C;
+}
 
-KccPrep kcc_prep_carve(double* base, int K, int C) {
+KccPrep kcc_prep_carve(double* base, int K, int C, int semiring) {
   KccPrep p{};
   if (!base) return p;
   const size_t kcc = (size_t)K * C * C, kc = (size_t)K * C;
@@ -621,6 +705,10 @@ KccPrep kcc_prep_carve(double* base, int K, int C) {
   p.tf = p.eb + kcc;
   p.tb = p.tf + kc;
   p.tdf = p.tb + kc;
+  if (semiring == SEMICRF_MAX) {
+    p.rf = p.tdf + kc;
+    p.rb = p.rf + kcc;
+  }
   return p;
 }
 
@@ -642,14 +730,12 @@ cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, int 
 
 cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s) {
   if (a.B <= 0) return cudaSuccess;
-  const int ef_smem =
-      a.semiring == SEMICRF_LOG && chain_smem(a.C, a.K, true).total * 8 <= kSmemMax;
-  const size_t bytes = chain_smem(a.C, a.K, ef_smem != 0).total * 8;
+  const size_t bytes = chain_plan(a.C, a.K).total * 8;
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
-    kern<<<dim3(a.B, ndir), kKT, bytes, s>>>(a, ef_smem);
+    kern<<<dim3(a.B, ndir), kKT, bytes, s>>>(a);
     return cudaGetLastError();
   };
   return a.semiring == SEMICRF_LOG ? go(kcc_chain_kernel<0>) : go(kcc_chain_kernel<1>);

@@ -286,7 +286,9 @@ struct KccPrep {
   double* eb;   // (K, C, C) [k][c2][c] = exp(tr[k][c,c2] - tb[k][c])   (beta chain)
   double* tf;   // (K, C) max over c' of tr[k][c',c]
   double* tb;   // (K, C) max over c2 of tr[k][c,c2]
-  double* tdf;  // (K, C) log semiring: tf + db; max semiring: db
+  double* tdf;  // (K, C) tf + db
+  double* rf;   // max semiring: (K, C, C) [k][c'][c] = tr[k][c',c]
+  double* rb;   // max semiring: (K, C, C) [k][c2][c] = tr[k][c,c2]
 };
 struct KccArgs {
   int B, T, K, C, kcap, semiring;
@@ -317,8 +319,8 @@ struct KccArgs {
   int nslice;
 };
 bool kcc_supported(int C, int K);
-size_t kcc_prep_doubles(int K, int C);
-KccPrep kcc_prep_carve(double* base, int K, int C);
+size_t kcc_prep_doubles(int K, int C, int semiring);
+KccPrep kcc_prep_carve(double* base, int K, int C, int semiring);
 int kcc_tr_slices(int B, int K, int C);
 cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, int semiring,
                             const KccPrep& pr, cudaStream_t s);
