@@ -43,16 +43,6 @@ __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
   return l < 0 ? 0 : (l > T ? T : (int)l);
 }
 
-// running sum of v * exp(x), kept as (m, s) with value s * exp(m); v in [0, C]
-__device__ __forceinline__ void online_add(double& m, double& s, double x, double v) {
-  if (x > m) {
-    s = s * exp(m - x) + v;
-    m = x;
-  } else {
-    s += v * exp(x - m);
-  }
-}
-
 __device__ __forceinline__ void cp_async8(double* dst, const double* src) {
   const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(d), "l"(src) : "memory");
@@ -93,25 +83,35 @@ __global__ void kcc_prep_kernel(const float* __restrict__ tr, const float* __res
 // Shared memory of the chain kernel (offsets in doubles).  The per-duration
 // C x C factors E[k] are resident when all K of them fit; otherwise they are
 // streamed from L2 in chunks of kc durations through two cp.async buffers, or,
-// when not even two single-duration buffers fit (C > ~110), read from L2.
+// when not even two single-duration buffers fit (C > ~110), read from L2.  The
+// (K, C) tables (tf or tb, and db) are kept as float32, which holds them
+// exactly (they are float32 inputs or maxima of them).  The forward chain also
+// keeps each source position's start term rn + ps - cum (rso) when room is left.
 struct ChainPlan {
-  int kc, resident, direct;
-  size_t ring, rn, xs, xm, dt, vals, redm, reds, eb, total;
+  int kc, resident, direct, rso;
+  size_t ring, rn, t1, dbs, xs, xm, dt, ct, vals, redm, reds, eb, rso_o, total;
 };
 __host__ __device__ inline ChainPlan chain_plan(int C, int K) {
   ChainPlan p{};
-  const size_t cc = (size_t)C * C;
+  const size_t cc = (size_t)C * C, kcs = (size_t)K * C;
   const int kcap = K - 1;
+  const int kc_max = kKC < kcap ? kKC : kcap;
   size_t o = 0;
   p.ring = o;
-  o += (size_t)K * C;
+  o += kcs;
   p.rn = o;
   o += K;
+  p.t1 = o;
+  o += (kcs + 1) / 2;
+  p.dbs = o;
+  o += (kcs + 1) / 2;
   p.xs = o;
   o += (size_t)kKC * C;
   p.xm = o;
   o += kKC;
   p.dt = o;
+  o += C;
+  p.ct = o;
   o += C;
   p.vals = o;
   o += C;
@@ -123,17 +123,26 @@ __host__ __device__ inline ChainPlan chain_plan(int C, int K) {
   const size_t cap = kSmemMax / 8;
   if (o + (size_t)K * cc <= cap) {
     p.resident = 1;
-    p.kc = kKC < kcap ? kKC : kcap;
+    p.kc = kc_max;
     o += (size_t)K * cc;
-  } else if (o + 2 * cc <= cap) {
-    size_t kc = (cap - o) / (2 * cc);
-    if (kc > (size_t)kKC) kc = kKC;
-    if (kc > (size_t)kcap) kc = kcap;
-    p.kc = (int)kc;
-    o += 2 * kc * cc;
   } else {
-    p.direct = 1;
-    p.kc = kKC < kcap ? kKC : kcap;
+    const size_t with_rso = cap > o + kcs ? (cap - o - kcs) / (2 * cc) : 0;
+    const size_t without = cap > o ? (cap - o) / (2 * cc) : 0;
+    const size_t want = kc_max < 8 ? kc_max : 8;
+    size_t kc = with_rso >= want ? with_rso : without;
+    if (kc > (size_t)kc_max) kc = kc_max;
+    if (kc >= 1) {
+      p.kc = (int)kc;
+      o += 2 * kc * cc;
+    } else {
+      p.direct = 1;
+      p.kc = kc_max;
+    }
+  }
+  if (o + kcs <= cap) {
+    p.rso = 1;
+    p.rso_o = o;
+    o += kcs;
   }
   p.total = o;
   return p;
@@ -141,6 +150,10 @@ __host__ __device__ inline ChainPlan chain_plan(int C, int K) {
 
 // One CTA per (sequence, direction).  Writes log alpha and its row maxima
 // (dir 0) or log beta (dir 1) for positions 0 .. len when the tables are given.
+// Thread (label c, slot j) = (tid % C, tid / C) handles the durations j, j + G,
+// ... of label c (G = 256 / C slots), so the lanes of a warp read one source
+// row and adjacent columns of E[k] (no bank conflicts); a position's G
+// partial sums per label are combined by one warp per label with shuffles.
 template <int SEMI>
 __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
   extern __shared__ __align__(16) double ksm[];
@@ -152,13 +165,18 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
   const size_t cc = (size_t)C * C;
   double* ring = ksm + sp.ring;  // dir 0: alpha rows (linear for log); dir 1: log source rows
   double* rn = ksm + sp.rn;      // dir 0: row maxima of alpha
+  float* t1f = reinterpret_cast<float*>(ksm + sp.t1);   // dir 0: tf, dir 1: tb
+  float* dbf = reinterpret_cast<float*>(ksm + sp.dbs);  // duration bias
   double* xs = ksm + sp.xs;      // dir 1: one chunk of duration source rows
   double* xm = ksm + sp.xm;
   double* dt = ksm + sp.dt;
+  double* ct = ksm + sp.ct;  // cum[t] + pe[t-1] of the position being computed
   double* vals = ksm + sp.vals;
   double* redm = ksm + sp.redm;
   double* reds = ksm + sp.reds;
   double* ebuf = ksm + sp.eb;
+  double* rso = ksm + sp.rso_o;  // dir 0 with sp.rso: start term of each ring position
+  const bool use_rso = sp.rso && dir == 0;
   __shared__ double s_m;
   const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
   const float* ps_b = a.ps ? a.ps + (size_t)b * T * C : nullptr;
@@ -177,14 +195,21 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
   const double* Eall = sp.direct ? Eg : ebuf;
   if (sp.resident)
     for (size_t i = tid; i < (size_t)K * cc; i += kKT) ebuf[i] = Eg[i];
+  {
+    const double* t1g = dir == 0 ? a.pr.tf : a.pr.tb;
+    for (int i = tid; i < K * C; i += kKT) {
+      t1f[i] = (float)t1g[i];
+      dbf[i] = a.db[i];
+    }
+  }
   if (dir == 0 && a.ref_ckpt) {
     float* rc = a.ref_ckpt + (size_t)b * a.nref * K * C;
     for (size_t i = tid; i < (size_t)a.nref * K * C; i += kKT)
       rc[i] = (i < (size_t)C) ? 0.f : kRefNegInf;
   }
-  const int nks = kKT / C;  // threads per label
+  const int G = kKT / C;  // duration slots per label
   const int c = tid % C, ks = tid / C;
-  const bool act = ks < nks;
+  const bool act = ks < G;
   // durations per chunk: all at once (forward, resident), else the x-row / staging chunk
   const int cs = (sp.resident && dir == 0) ? kcap : sp.kc;
   int par = 0;  // staging buffer holding the current chunk
@@ -228,6 +253,7 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
         const double v = vals[q];
         ring[(size_t)slot * C + q] =
             SEMI == 0 ? ((m > -INFINITY && v > -INFINITY) ? exp(v - m) : 0.0) : v;
+        if (use_rso) rso[(size_t)slot * C + q] = (SEMI == 0 ? m : 0.0) + dt[q];
         if (a.alpha) a.alpha[((size_t)b * (T + 1) + t) * C + q] = v;
         if (a.ref_ckpt) {
           const int S = a.sref;
@@ -244,33 +270,58 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
     } else {
       for (int q = tid; q < C; q += kKT) {
         const double v = vals[q];
-        ring[(size_t)slot * C + q] = v > -INFINITY ? v + cu(t, q) + pev(t, q) : -INFINITY;
+        ring[(size_t)slot * C + q] = v > -INFINITY ? v + ct[q] : -INFINITY;
         if (a.beta) a.beta[((size_t)b * (T + 1) + t) * C + q] = v;
       }
     }
     __syncthreads();
   };
-  // per-thread partial results of a position -> one value per label in vals[]
-  auto combine = [&](double m, double s, int t) {
+  // the G partial results of each label -> vals[label]: one warp per label,
+  // a shuffle max, one exp per slot and a shuffle sum
+  auto combine = [&](double m, double S) {
     redm[tid] = m;
-    reds[tid] = s;
+    reds[tid] = S;
     __syncthreads();
-    if (tid < C) {
-      double M = -INFINITY;
-      for (int j = 0; j < nks; ++j) M = fmax(M, redm[j * C + tid]);
-      double r = M;
-      if (SEMI == 0 && M > -INFINITY) {
-        double S = 0.0;
-        for (int j = 0; j < nks; ++j) {
-          const double mj = redm[j * C + tid];
-          if (mj > -INFINITY) S += reds[j * C + tid] * exp(mj - M);
+    for (int lc = warp; lc < C; lc += kKT / 32) {
+      double mm = -INFINITY;
+      for (int j = lane; j < G; j += 32) mm = fmax(mm, redm[j * C + lc]);
+      for (int o = 16; o > 0; o >>= 1) mm = fmax(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+      double r = mm;
+      if (SEMI == 0 && mm > -INFINITY) {
+        double ss = 0.0;
+        for (int j = lane; j < G; j += 32) {
+          const double mj = redm[j * C + lc];
+          if (mj > -INFINITY) ss += reds[j * C + lc] * exp(mj - mm);
         }
-        r = M + log(S);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        r = mm + log(ss);
       }
-      if (dir == 0 && r > -INFINITY) r += cu(t, tid) + pev(t, tid);
-      vals[tid] = r;
+      if (lane == 0) {
+        if (dir == 0 && r > -INFINITY) r += ct[lc];
+        vals[lc] = r;
+      }
     }
     __syncthreads();
+  };
+  // a batch of up to four items: fold sum_u v_u exp(x_u) into (m, S) with one rescale
+  auto add_batch = [&](double& m, double& S, double* xv, double* av) {
+    double bm = m;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (av[u] > 0.0) {
+        if (av[u] < 1e-280) {  // too small to scale by exp(x - m) alone: move into x
+          xv[u] += log(av[u]);
+          av[u] = 1.0;
+        }
+        bm = fmax(bm, xv[u]);
+      }
+    if (!(bm > -INFINITY)) return;
+    double ns = (m > -INFINITY) ? S * exp(m - bm) : 0.0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (av[u] > 0.0) ns += av[u] * exp(xv[u] - bm);
+    S = ns;
+    m = bm;
   };
   // dot product of a source row with column c of E[k] (stride C)
   auto dot = [&](const double* x, const double* e) {
@@ -290,16 +341,18 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
     for (int q = 0; q < C; ++q) mp = fmax(mp, x[q] + e[(size_t)q * C]);
     return mp;
   };
-  // a dot product too small to scale by exp(x - m) alone moves into x
-  auto add_dot = [&](double& m, double& S, double x, double acc) {
-    if (!(acc > 0.0)) return;
-    if (acc < 1e-280)
-      online_add(m, S, x + log(acc), 1.0);
-    else
-      online_add(m, S, x, acc);
+  // the per-position input terms, loaded before the position's items so their
+  // latency hides behind them: dt = ps[t] - cum[t], ct = cum[t] + pe[t-1]
+  auto load_terms = [&](int t) {
+    for (int q = tid; q < C; q += kKT) {
+      const double cv = cu(t, q);
+      dt[q] = psv(t, q) - cv;
+      ct[q] = cv + pev(t, q);
+    }
   };
 
   for (int q = tid; q < C; q += kKT) vals[q] = 0.0;  // alpha[0] = 0, beta[len] = 0
+  load_terms(dir == 0 ? 0 : Lb);
   __syncthreads();
   if (dir == 0) {
     finish(0);
@@ -308,29 +361,42 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
       const int kmax = t < kcap ? t : kcap;
       const int tn = t + 1 <= Lb ? t + 1 : -1;
       const int kmax_n = tn > 0 ? (tn < kcap ? tn : kcap) : 0;
+      load_terms(t);
       double m = -INFINITY, S = 0.0;
       for (int k0 = 1; k0 <= kmax; k0 += cs) {
         const int nk = min(cs, kmax - k0 + 1);
         stage(k0, kmax, tn, kmax_n);
         if (!resident) __syncthreads();
         if (act)
-          for (int kk = ks; kk < nk; kk += nks) {
-            const int k = k0 + kk, s = t - k, slot = s % R;
-            const double* src = ring + (size_t)slot * C;
-            const double* e = erow(k, k0) + c;
-            if (SEMI == 0) {
-              add_dot(m, S, rn[slot] + a.pr.tdf[k * C + c] + psv(s, c) - cu(s, c), dot(src, e));
-            } else {
-              const double mp = vmax(src, e);
-              if (mp > -INFINITY) m = fmax(m, mp + (double)a.db[k * C + c] + psv(s, c) - cu(s, c));
+          for (int kb = ks; kb < nk; kb += 4 * G) {
+            double xv[4], av[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int kk = kb + u * G;
+              xv[u] = -INFINITY;
+              av[u] = 0.0;
+              if (kk >= nk) continue;
+              const int k = k0 + kk, s = t - k, slot = s % R;
+              const double* src = ring + (size_t)slot * C;
+              const double* e = erow(k, k0) + c;
+              const double so = use_rso ? rso[(size_t)slot * C + c]
+                                        : (SEMI == 0 ? rn[slot] : 0.0) + psv(s, c) - cu(s, c);
+              if (SEMI == 0) {
+                av[u] = dot(src, e);
+                xv[u] = so + (double)t1f[k * C + c] + (double)dbf[k * C + c];
+              } else {
+                const double mp = vmax(src, e);
+                if (mp > -INFINITY) m = fmax(m, mp + (double)dbf[k * C + c] + so);
+              }
             }
+            if (SEMI == 0) add_batch(m, S, xv, av);
           }
         if (!resident) {
           __syncthreads();
           par ^= 1;
         }
       }
-      combine(m, S, t);
+      combine(m, S);
       finish(t);
     }
     if (tid == 0) {
@@ -357,46 +423,60 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
       const int kmax = (Lb - t) < kcap ? (Lb - t) : kcap;
       const int tn = t - 1;
       const int kmax_n = tn >= 0 ? ((Lb - tn) < kcap ? (Lb - tn) : kcap) : 0;
-      for (int q = tid; q < C; q += kKT) dt[q] = psv(t, q) - cu(t, q);
+      load_terms(t);
       __syncthreads();
       double m = -INFINITY, S = 0.0;
       for (int k0 = 1; k0 <= kmax; k0 += cs) {
         const int nkc = min(cs, kmax - k0 + 1);
         stage(k0, kmax, tn, kmax_n);
-        // the source rows of this chunk of durations, one warp per row
-        for (int kk = warp; kk < nkc; kk += kKT / 32) {
-          const int k = k0 + kk;
-          const double* srow = ring + (size_t)((t + k) % R) * C;
-          double mx = -INFINITY;
-          for (int q = lane; q < C; q += 32) {
-            const double x = srow[q] + (double)a.db[k * C + q] + dt[q];
-            xs[kk * C + q] = x;
-            mx = fmax(mx, x);
-          }
-          for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          if (SEMI == 0)
-            for (int q = lane; q < C; q += 32) {
-              const double x = xs[kk * C + q];
-              xs[kk * C + q] = (mx > -INFINITY && x > -INFINITY) ? exp(x - mx) : 0.0;
-            }
-          if (lane == 0) xm[kk] = mx;
+        // the source rows x[k][q] of this chunk of durations, all threads
+        for (int i = tid; i < nkc * C; i += kKT) {
+          const int kk = i / C, q = i % C, k = k0 + kk;
+          xs[i] = ring[(size_t)((t + k) % R) * C + q] + (double)dbf[k * C + q] + dt[q];
         }
         __syncthreads();
+        if (SEMI == 0) {
+          // row maxima (one warp per row), then the rows in linear form
+          for (int kk = warp; kk < nkc; kk += kKT / 32) {
+            double mx = -INFINITY;
+            for (int q = lane; q < C; q += 32) mx = fmax(mx, xs[kk * C + q]);
+            for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) xm[kk] = mx;
+          }
+          __syncthreads();
+          for (int i = tid; i < nkc * C; i += kKT) {
+            const double mx = xm[i / C], x = xs[i];
+            xs[i] = (mx > -INFINITY && x > -INFINITY) ? exp(x - mx) : 0.0;
+          }
+          __syncthreads();
+        }
         if (act)
-          for (int kk = ks; kk < nkc; kk += nks) {
-            const int k = k0 + kk;
-            const double* x = xs + kk * C;
-            const double* e = erow(k, k0) + c;
-            if (SEMI == 0) {
-              if (xm[kk] > -INFINITY) add_dot(m, S, xm[kk] + a.pr.tb[k * C + c], dot(x, e));
-            } else {
-              m = fmax(m, vmax(x, e));
+          for (int kb = ks; kb < nkc; kb += 4 * G) {
+            double xv[4], av[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int kk = kb + u * G;
+              xv[u] = -INFINITY;
+              av[u] = 0.0;
+              if (kk >= nkc) continue;
+              const int k = k0 + kk;
+              const double* x = xs + kk * C;
+              const double* e = erow(k, k0) + c;
+              if (SEMI == 0) {
+                if (xm[kk] > -INFINITY) {
+                  av[u] = dot(x, e);
+                  xv[u] = xm[kk] + (double)t1f[k * C + c];
+                }
+              } else {
+                m = fmax(m, vmax(x, e));
+              }
             }
+            if (SEMI == 0) add_batch(m, S, xv, av);
           }
         __syncthreads();
         if (!resident) par ^= 1;
       }
-      combine(m, S, t);
+      combine(m, S);
       finish(t);
     }
   }
