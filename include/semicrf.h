@@ -151,9 +151,12 @@ size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_
  * must not call cudaMalloc on its request path).  Results equal
  * semicrf_forward's partition for the same problem.
  *  - Scratch: a fixed 2 MiB device array inside the library, one per
- *    device; every accepted shape fits (the largest, at C=256, need about
- *    1.3 MiB).  A problem whose semicrf_forward_workspace_size exceeds
- *    2 MiB is rejected with SEMICRF_ERR_WORKSPACE (before any CUDA call).
+ *    device; every shape with (C, C) transitions fits (the largest, at
+ *    C=256, need about 1.3 MiB).  (K, C, C) transitions need
+ *    16*K*C*C + 24*K*C bytes (twice the K*C*C part for max), so only those
+ *    up to about K*C*C = 130k fit.  A problem whose
+ *    semicrf_forward_workspace_size exceeds 2 MiB is rejected with
+ *    SEMICRF_ERR_WORKSPACE (before any CUDA call).
  *  - Nothing in the scratch needs to start at zero (each call writes what it
  *    reads, in stream order).
  *  - Calls on one device share that scratch: overlapping calls (different

@@ -13,10 +13,12 @@
 // Limits and rules:
 //  - The scratch holds the forward's prepared constants (the exponentiated
 //    transition and duration tables, about 16*C*C + 8*(K+16)*C bytes in the
-//    log semiring).  It is kNoallocScratchBytes (2 MiB) large.  Every shape the
-//    scan accepts fits (the largest, at C=256, need about 1.3 MiB); a problem
-//    whose forward workspace (semicrf_forward_workspace_size) exceeds 2 MiB is
-//    rejected with SEMICRF_ERR_WORKSPACE before any CUDA call.
+//    log semiring).  It is kNoallocScratchBytes (2 MiB) large.  Every shape
+//    with (C, C) transitions fits (the largest, at C=256, need about 1.3 MiB);
+//    (K, C, C) transitions need per-duration factor tables, 16*K*C*C + 24*K*C
+//    bytes, so only the smaller ones fit.  A problem whose forward workspace
+//    (semicrf_forward_workspace_size) exceeds 2 MiB is rejected with
+//    SEMICRF_ERR_WORKSPACE before any CUDA call.
 //  - Nothing in the scratch has to start at zero: every byte the scan reads
 //    is first written by the preparation kernel of the same call, earlier on
 //    the same stream.
