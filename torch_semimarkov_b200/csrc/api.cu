@@ -495,6 +495,8 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     }
     if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_ws_supported((int)p->C, (int)p->K))
       return cuda_status(launch_lchain_ws(L, grid, s));
+    if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_cl_supported((int)p->C, (int)p->K))
+      return cuda_status(launch_lchain_cl(L, grid, s));
     return cuda_status(launch_lchain(L, grid, s));
   }
   ChainLaunch L = base_launch(p, pr);

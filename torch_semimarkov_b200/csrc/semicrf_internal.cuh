@@ -158,6 +158,10 @@ struct LChainLaunch {
 cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s);
 // warp-specialised variant for C <= 64, whole-sequence chains (mode 0) only
 cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s);
+// cluster variant for 64 < C <= 256 (lchain_cl.cu): one chain per cluster of
+// four CTAs, whole-sequence chains (mode 0) without ring checkpoints
+bool lchain_cl_supported(int C, int K);
+cudaError_t launch_lchain_cl(const LChainLaunch& L, int nchains, cudaStream_t s);
 
 // time chunking of the float64 chains (lchunk.cu)
 struct ChunkPlan {
