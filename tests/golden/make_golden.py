@@ -271,6 +271,74 @@ def run_uncert_case(name, spec):
 
 
 # ---------------------------------------------------------------------------
+# Duration distributions (reference duration.py) and heads that use them
+# ---------------------------------------------------------------------------
+
+
+def run_duration_dists(name="duration_dists"):
+    from torch_semimarkov.duration import (
+        GeometricDuration,
+        NegativeBinomialDuration,
+        PoissonDuration,
+    )
+
+    K, C = 12, 4
+    g = torch.Generator().manual_seed(61)
+    w = torch.randn(K, C, generator=g)
+    out = {"K": K, "C": C, "weights": _np(w)}
+    specs = {
+        "geometric": (GeometricDuration, {"logit_p": torch.randn(C, generator=g)}),
+        "negbin": (NegativeBinomialDuration, {"logit_p": torch.randn(C, generator=g),
+                                               "log_r": torch.randn(C, generator=g)}),
+        "poisson": (PoissonDuration, {"log_lambda": torch.randn(C, generator=g) + 1.0}),
+    }
+    for kind, (cls, params) in specs.items():
+        d = cls(K, C)
+        with torch.no_grad():
+            for pname, v in params.items():
+                getattr(d, pname).copy_(v)
+        bias = d()
+        (bias * w).sum().backward()
+        out[kind + "_bias"] = _np(bias)
+        for pname, v in params.items():
+            out[kind + "_" + pname] = _np(v)
+            out[kind + "_grad_" + pname] = _np(getattr(d, pname).grad)
+    save(name, **out)
+
+
+HEAD_DIST_CASES = {
+    "dhead_geometric": dict(B=2, T=50, K=8, C=4, lengths=[50, 31], seed=71, dist="geometric",
+                           params={"logit_p": [-0.5, 0.2, 1.0, -1.5]}),
+    "dhead_negbin": dict(B=2, T=50, K=8, C=4, lengths=[50, 40], seed=72, dist="negbin",
+                        params={"logit_p": [0.3, -0.4, 0.1, 0.8],
+                                "log_r": [0.5, -0.2, 1.1, 0.0]}),
+}
+
+
+def run_head_dist_case(name, spec):
+    B, T, K, C = spec["B"], spec["T"], spec["K"], spec["C"]
+    torch.manual_seed(spec["seed"])
+    crf = SemiMarkovCRFHead(num_classes=C, max_duration=K, duration_distribution=spec["dist"])
+    p = make_hidden(B, T, C, K, spec["seed"], "default", None)
+    with torch.no_grad():
+        crf.transition.copy_(p["transition"])
+        for pname, v in spec["params"].items():
+            getattr(crf.duration_dist, pname).copy_(torch.tensor(v))
+    lengths = torch.tensor(spec["lengths"], dtype=torch.long)
+    res = crf(p["hidden"], lengths, use_triton=False)
+    loss = crf.compute_loss(p["hidden"], lengths, p["labels"], use_triton=False, reduction="sum")
+    loss.backward()
+    out = {"partition": _np(res["partition"]), "loss_sum": float(loss.detach()),
+           "grad_transition": _np(crf.transition.grad)}
+    for pname in spec["params"]:
+        out["param_" + pname] = _np(getattr(crf.duration_dist, pname).detach())
+        out["grad_" + pname] = _np(getattr(crf.duration_dist, pname).grad)
+    save(name, B=B, T=T, K=K, C=C, seed=spec["seed"], dist=np.array(spec["dist"]),
+         lengths=lengths.numpy(), labels=p["labels"].numpy(), hidden=_np(p["hidden"]),
+         transition=_np(p["transition"]), **out)
+
+
+# ---------------------------------------------------------------------------
 # Gold scoring cases (float64)
 # ---------------------------------------------------------------------------
 
@@ -322,6 +390,11 @@ def main(argv):
     for name, spec in UNCERT_CASES.items():
         if not want or name in want:
             run_uncert_case(name, spec)
+    if not want or "duration_dists" in want:
+        run_duration_dists()
+    for name, spec in HEAD_DIST_CASES.items():
+        if not want or name in want:
+            run_head_dist_case(name, spec)
 
 
 if __name__ == "__main__":

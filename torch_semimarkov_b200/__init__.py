@@ -8,7 +8,16 @@ include/semicrf.h).  There is no Triton, no backend dispatch and no CPU
 fallback.
 """
 
-from .duration import DurationDistribution, LearnedDuration, create_duration_distribution
+from .duration import (
+    CallableDuration,
+    DurationDistribution,
+    GeometricDuration,
+    LearnedDuration,
+    NegativeBinomialDuration,
+    PoissonDuration,
+    UniformDuration,
+    create_duration_distribution,
+)
 from .helpers import Segment, ViterbiResult, score_gold_vectorized
 from .nn import SemiMarkovCRFHead
 from .streaming import (
@@ -31,6 +40,11 @@ __all__ = [
     "score_gold_vectorized",
     "DurationDistribution",
     "LearnedDuration",
+    "GeometricDuration",
+    "NegativeBinomialDuration",
+    "PoissonDuration",
+    "UniformDuration",
+    "CallableDuration",
     "create_duration_distribution",
     "semi_crf_streaming_forward",
     "SemiCRFStreaming",
