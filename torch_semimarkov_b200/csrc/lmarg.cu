@@ -183,9 +183,12 @@ __global__ void __launch_bounds__(kMT) lmarg_blk_kernel(const LMargArgs a) {
 // for sources s = t0+1+j, so X[i] Y[i+k-1] = P(t0+i -> t0+i+k) / exp(db);
 // X <= 1 and Y is bounded by a segment marginal, so both stay in range, and a
 // source that underflows in Ylin is negligible beside its block's maximum.
-// An item is a (label, 8 consecutive k) pair: MI items per thread.
+// An item is a (label, kLG consecutive k) pair: MI items per thread.  A thread
+// forms 8 targets x kLG lags per step from 8 + (8 + kLG - 1) staged values, so
+// each shared-memory load serves four FMAs.
+constexpr int kLG = 16;
 template <int MI>
-__global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LMargArgs a) {
+__global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LMargArgs a) {
   extern __shared__ __align__(16) unsigned char smraw[];
   const int C = a.C, T = a.T, kcap = a.kcap, CG = a.cg;
   const int g0 = blockIdx.x * CG;
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LM
   double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
   double* Y = X + (size_t)kTT * CG;               // [ny][CG]
   double* G = Y + (size_t)ny * CG;                // [nq][CG]
-  const int nkg = (kcap + 7) / 8;
+  const int nkg = (kcap + kLG - 1) / kLG;
   const int nitems = cgn * nkg;
   const int Lb = seq_len(a.lengths, b, T);
   const int ntile = (Lb + kTT - 1) / kTT;  // target blocks (targets t < Lb)
@@ -209,11 +212,11 @@ __global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LM
   const size_t rowb = (size_t)b * (T + 1);
   const double* mx_b = a.maX + (size_t)b * nblk * C + g0;
   const double* my_b = a.mbY + (size_t)b * nblk * C + g0;
-  double acc[MI][8];
+  double acc[MI][kLG];
 #pragma unroll
   for (int j = 0; j < MI; ++j)
 #pragma unroll
-    for (int q = 0; q < 8; ++q) acc[j][q] = 0.0;
+    for (int q = 0; q < kLG; ++q) acc[j][q] = 0.0;
 
   for (int tau = tau_lo; tau < tau_hi; ++tau) {
     const int t0 = tau * kTT;
@@ -229,18 +232,41 @@ __global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LM
       }
       G[q * CG + cc] = gv;
     }
-    for (int e = tid; e < kTT * cgn; e += kMT) {
-      const int i = e / cgn, cc = e % cgn;
-      X[i * CG + cc] = (i < n) ? a.la[(rowb + t0 + i) * C + g0 + cc] : 0.0;
+    // staging: four loads in flight per thread before any is used
+    for (int e0 = tid; e0 < kTT * cgn; e0 += 4 * kMT) {
+      double v[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int e = e0 + r * kMT;
+        const int i = e / cgn, cc = e % cgn;
+        v[r] = (e < kTT * cgn && i < n) ? a.la[(rowb + t0 + i) * C + g0 + cc] : 0.0;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int e = e0 + r * kMT;
+        if (e < kTT * cgn) X[(e / cgn) * CG + e % cgn] = v[r];
+      }
     }
     __syncthreads();
-    for (int e = tid; e < ny * cgn; e += kMT) {
-      const int j = e / cgn, cc = e % cgn;
-      const int s = t0 + 1 + j;
-      double y = 0.0;
-      if (s <= Lb && j < n - 1 + kcap)
-        y = a.lb[(rowb + s) * C + g0 + cc] * G[(s / kTT - tau) * CG + cc];
-      Y[j * CG + cc] = y;
+    for (int e0 = tid; e0 < ny * cgn; e0 += 4 * kMT) {
+      double v[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int e = e0 + r * kMT;
+        const int j = e / cgn, cc = e % cgn;
+        const int s = t0 + 1 + j;
+        v[r] = (e < ny * cgn && s <= Lb && j < n - 1 + kcap) ? a.lb[(rowb + s) * C + g0 + cc]
+                                                             : 0.0;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int e = e0 + r * kMT;
+        if (e < ny * cgn) {
+          const int j = e / cgn, cc = e % cgn;
+          const int s = t0 + 1 + j;
+          Y[j * CG + cc] = v[r] != 0.0 ? v[r] * G[(s / kTT - tau) * CG + cc] : 0.0;
+        }
+      }
     }
     __syncthreads();
 #pragma unroll
@@ -248,20 +274,20 @@ __global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LM
       const int it = tid + jt * kMT;
       if (it < nitems) {
         const int cc = it % cgn, kg = it / cgn;
-        const int k_lo = 1 + 8 * kg;
+        const int k_lo = 1 + kLG * kg;
         // target i pairs with Y[i + k - 1]: for targets i0 .. i0+7 the window
-        // y[m] = Y[i0 + k_lo - 1 + m], m < 16, covers all 8 lags (X is zero
-        // beyond the last target, so whole groups of 8 are safe)
+        // y[m] = Y[i0 + k_lo - 1 + m], m < kLG + 7, covers all kLG lags (X is
+        // zero beyond the last target, so whole groups of 8 are safe)
         for (int i0 = 0; i0 < n; i0 += 8) {
-          double y[16], x[8];
+          double y[kLG + 7], x[8];
 #pragma unroll
-          for (int m = 0; m < 16; ++m) y[m] = Y[(i0 + k_lo - 1 + m) * CG + cc];
+          for (int m = 0; m < kLG + 7; ++m) y[m] = Y[(i0 + k_lo - 1 + m) * CG + cc];
 #pragma unroll
           for (int d = 0; d < 8; ++d) x[d] = X[(i0 + d) * CG + cc];
 #pragma unroll
           for (int d = 0; d < 8; ++d)
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc[jt][q] = fma(x[d], y[d + q], acc[jt][q]);
+            for (int q = 0; q < kLG; ++q) acc[jt][q] = fma(x[d], y[d + q], acc[jt][q]);
         }
       }
     }
@@ -273,8 +299,8 @@ __global__ void __launch_bounds__(kMT, MI == 4 ? 2 : 1) lmarg_db_kernel(const LM
     if (it < nitems) {
       const int cc = it % cgn, kg = it / cgn;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int k = 1 + 8 * kg + q;
+      for (int q = 0; q < kLG; ++q) {
+        const int k = 1 + kLG * kg + q;
         if (k <= kcap) out[(size_t)(k - 1) * C + g0 + cc] = acc[jt][q];
       }
     }
@@ -351,11 +377,11 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
   if (nch < 1) nch = 1;
   p.nchunk = nch;
   // duration partials: label group sized so that the staging fits two CTAs
-  // per SM with 4 items per thread where possible, else one CTA with 8
+  // per SM with one item per thread where possible, else one CTA with two
   const int ny = kTT + kcap + 16;
   const int nq = ny / kTT + 2;
   const size_t per_label = 8 * (size_t)(kTT + ny + nq);
-  const int nkg = (kcap + 7) / 8;
+  const int nkg = (kcap + kLG - 1) / kLG;
   auto fit = [&](size_t smem, int items) {
     long cg = (long)(smem / per_label);
     const long ci = (long)items * kMT / nkg;
@@ -363,16 +389,16 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
     if (cg > C) cg = C;
     return (int)cg;
   };
-  int cg = fit(110 * 1024, 4);
-  p.mi = 4;
-  if (cg < 1 || (cg < C && fit(200 * 1024, 8) >= 2 * cg)) {
-    cg = fit(200 * 1024, 8);
-    p.mi = 8;
+  int cg = fit(110 * 1024, 1);
+  p.mi = 1;
+  if (cg < 1 || (cg < C && fit(200 * 1024, 2) >= 2 * cg)) {
+    cg = fit(200 * 1024, 2);
+    p.mi = 2;
   }
   if (cg < 1) cg = 1;
   p.cg = cg;
   p.ncg = (C + cg - 1) / cg;
-  const int target = (p.mi == 4 ? 4 : 2) * sms;
+  const int target = (p.mi == 1 ? 4 : 2) * sms;
   int nsp = (target + B * p.ncg - 1) / (B * p.ncg);
   const int maxsp = (T + kTT - 1) / kTT;
   if (nsp > maxsp) nsp = maxsp;
@@ -412,16 +438,16 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const dim3 gdb(p.ncg, a.nsplit, a.B);
-  if (p.mi == 4) {
-    e = cudaFuncSetAttribute(lmarg_db_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (p.mi == 1) {
+    e = cudaFuncSetAttribute(lmarg_db_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)p.db_smem);
     if (e != cudaSuccess) return e;
-    lmarg_db_kernel<4><<<gdb, kMT, p.db_smem, s>>>(a);
+    lmarg_db_kernel<1><<<gdb, kMT, p.db_smem, s>>>(a);
   } else {
-    e = cudaFuncSetAttribute(lmarg_db_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(lmarg_db_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)p.db_smem);
     if (e != cudaSuccess) return e;
-    lmarg_db_kernel<8><<<gdb, kMT, p.db_smem, s>>>(a);
+    lmarg_db_kernel<2><<<gdb, kMT, p.db_smem, s>>>(a);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
