@@ -392,9 +392,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           const int u = u0 + i;
           const double d = csign * (pre[r] - cA[bf * CP + cc]);
           if (noproj) {
+            // |dc| <= 650 keeps exp(dc) and its reciprocal normal
             const double dc = fmin(fmax(d, -650.0), 650.0);
-            gb[(bf * LP + i) * CP + cc] = edb[cc] * exp(dc);
-            hb[(bf * LP + i) * CP + cc] = ecm[cc] * exp(-dc);
+            const double ed = exp(dc);
+            gb[(bf * LP + i) * CP + cc] = edb[cc] * ed;
+            hb[(bf * LP + i) * CP + cc] = ecm[cc] * __drcp_rn(ed);
           } else {
             gb[(bf * LP + i) * CP + cc] = exp(fmin(toff_at(u, cc) + dbmax[cc] + d, 700.0));
             hb[(bf * LP + i) * CP + cc] = exp(fmin(colmax[cc] + soff_at(u, cc) - d, 700.0));
