@@ -20,6 +20,11 @@
  *   semicrf_score_gold_backward  autograd of score_gold_vectorized
  *   semicrf_checkpoint_interval  _compute_checkpoint_interval
  *                              (streaming/pytorch_reference.py:25-45)
+ *   semicrf_edge_scan_forward  the edge-tensor scan: launch_triton_kernel
+ *                              (triton_scan.py:594-656) and the forward of
+ *                              SemiCRFTritonForward (triton_scan.py:738-752)
+ *   semicrf_edge_scan_backward the backward of SemiCRFTritonForward
+ *                              (triton_scan.py:754-770)
  *
  * Conventions
  *  - All tensors are device pointers to contiguous row-major float32 (int64
@@ -144,6 +149,29 @@ int semicrf_score_gold_backward(int64_t B, int64_t T, int64_t K, int64_t C,
                                 float* grad_duration_bias, void* workspace,
                                 size_t workspace_bytes, void* stream);
 size_t semicrf_score_gold_workspace_size(int64_t B, int64_t T, int64_t K, int64_t C);
+
+/* Edge-tensor scan (triton_scan.py:163-273, semi_crf_triton_forward at
+ * :773-860): log potentials edge (B, N-1, K, C, C), indexed [b][start]
+ * [duration index][new label][previous label], for sequences of N
+ * positions.  partition (B) = (+)_c beta[L-1, c] with beta[0] = 0 and
+ * beta[n, c] = (+)_{k, c'} (beta[n-k, c'] + edge[n-k, min(k, K-1), c, c']),
+ * k = 1 .. max(1, min(K-1, n)); (+) = logsumexp (SEMICRF_LOG) or max.
+ * Lengths 0 or above N give -1e9, length 1 gives (+) over zeros.  `saved`
+ * (may be NULL when no backward follows) keeps what the backward needs;
+ * edge may be NULL when N == 1. */
+size_t semicrf_edge_scan_saved_size(int64_t B, int64_t N, int64_t K, int64_t C, int semiring);
+int semicrf_edge_scan_forward(int64_t B, int64_t N, int64_t K, int64_t C, const float* edge,
+                              const int64_t* lengths, int semiring, float* partition, void* saved,
+                              void* stream);
+/* grad_edge (B, N-1, K, C, C) is overwritten with grad_out[b] * d partition[b]
+ * / d edge: the segment marginals (log), or 1 on the first-maximum path
+ * (max, as torch.max routes its gradient). */
+size_t semicrf_edge_scan_backward_workspace_size(int64_t B, int64_t N, int64_t K, int64_t C,
+                                                 int semiring);
+int semicrf_edge_scan_backward(int64_t B, int64_t N, int64_t K, int64_t C, const float* edge,
+                               const int64_t* lengths, int semiring, const void* saved,
+                               const float* grad_out, float* grad_edge, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* Partition-only forward scan that allocates nothing and takes no workspace.
  * It has no counterpart in the reference: it is for hosts that cannot supply

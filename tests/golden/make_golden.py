@@ -339,6 +339,37 @@ def run_head_dist_case(name, spec):
 
 
 # ---------------------------------------------------------------------------
+# Edge-tensor scan (reference triton_scan.py, float64 PyTorch scan)
+# ---------------------------------------------------------------------------
+
+ESCAN_CASES = {
+    "escan_basic": dict(B=4, N=30, K=5, C=4, lengths=[30, 17, 1, 2], seed=81),
+    "escan_k1": dict(B=2, N=12, K=1, C=3, lengths=[12, 7], seed=82),
+    "escan_wide": dict(B=2, N=24, K=8, C=6, lengths=[24, 15], seed=83),
+    "escan_oob": dict(B=3, N=10, K=4, C=3, lengths=[0, 10, 11], seed=84),
+}
+
+
+def run_escan_case(name, spec):
+    from torch_semimarkov.triton_scan import semi_crf_forward_pytorch
+
+    B, N, K, C = spec["B"], spec["N"], spec["K"], spec["C"]
+    g = torch.Generator().manual_seed(spec["seed"])
+    edge = torch.randn(B, N - 1, K, C, C, generator=g).float()
+    lengths = torch.tensor(spec["lengths"], dtype=torch.long)
+    gout = torch.rand(B, generator=g, dtype=torch.float64) + 0.5
+    out = {}
+    for semi in ("log", "max"):
+        e = edge.double().requires_grad_(True)
+        part = semi_crf_forward_pytorch(e, lengths, semiring=semi)
+        part.backward(gout)
+        out[semi + "_partition"] = _np(part)
+        out[semi + "_grad_edge"] = _np(e.grad).astype(np.float32)
+    save(name, B=B, N=N, K=K, C=C, edge=_np(edge), lengths=lengths.numpy(),
+         grad_output=_np(gout), **out)
+
+
+# ---------------------------------------------------------------------------
 # Gold scoring cases (float64)
 # ---------------------------------------------------------------------------
 
@@ -390,6 +421,9 @@ def main(argv):
     for name, spec in UNCERT_CASES.items():
         if not want or name in want:
             run_uncert_case(name, spec)
+    for name, spec in ESCAN_CASES.items():
+        if not want or name in want:
+            run_escan_case(name, spec)
     if not want or "duration_dists" in want:
         run_duration_dists()
     for name, spec in HEAD_DIST_CASES.items():

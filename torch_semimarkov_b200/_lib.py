@@ -73,6 +73,10 @@ EXPORTED_SYMBOLS = (
     "semicrf_strerror",
     "semicrf_abi_version",
     "semicrf_forward_noalloc",
+    "semicrf_edge_scan_saved_size",
+    "semicrf_edge_scan_forward",
+    "semicrf_edge_scan_backward_workspace_size",
+    "semicrf_edge_scan_backward",
 )
 
 
@@ -138,6 +142,15 @@ def load():
     lib.semicrf_abi_version.restype = ci
     lib.semicrf_forward_noalloc.restype = ci
     lib.semicrf_forward_noalloc.argtypes = [P, vp, vp]
+    for name in ("semicrf_edge_scan_saved_size", "semicrf_edge_scan_backward_workspace_size"):
+        f = getattr(lib, name)
+        f.restype = sz
+        f.argtypes = [i64, i64, i64, i64, ci]
+    lib.semicrf_edge_scan_forward.restype = ci
+    lib.semicrf_edge_scan_forward.argtypes = [i64, i64, i64, i64, vp, vp, ci, vp, vp, vp]
+    lib.semicrf_edge_scan_backward.restype = ci
+    lib.semicrf_edge_scan_backward.argtypes = [i64, i64, i64, i64, vp, vp, ci, vp, vp, vp, vp,
+                                               sz, vp]
     _lib = lib
     return lib
 
@@ -348,3 +361,57 @@ def score_gold_backward(labels, lengths, grad_out, B, T, K, C, device):
                                              _stream(device))
         check(st, "semicrf_score_gold_backward")
     return gc, gt, gd
+
+
+def _edge_inputs(edge, lengths):
+    if not isinstance(edge, torch.Tensor) or edge.dim() != 5 or edge.shape[3] != edge.shape[4]:
+        raise ValueError("edge must be a (batch, N-1, K, C, C) tensor")
+    if not edge.is_cuda:
+        raise RuntimeError("torch_semimarkov_b200 runs on CUDA devices only "
+                           "(edge is on the CPU; there is no CPU fallback)")
+    B, N1, K, C, _ = edge.shape
+    if not isinstance(lengths, torch.Tensor):
+        lengths = torch.as_tensor(lengths)
+    if lengths.shape != (B,):
+        raise ValueError(f"lengths must have shape ({B},)")
+    e = edge.detach().to(torch.float32).contiguous()
+    ln = lengths.to(device=edge.device, dtype=torch.int64).contiguous()
+    return e, ln, B, N1 + 1, K, C
+
+
+def edge_scan_forward(edge, lengths, semiring="log", want_saved=False):
+    """semicrf_edge_scan_forward.  Returns (partition float32 (B,), saved or None)."""
+    if semiring not in SEMIRINGS:
+        raise ValueError(f"semiring must be 'log' or 'max', got {semiring!r}")
+    lib = load()
+    e, ln, B, N, K, C = _edge_inputs(edge, lengths)
+    sr = SEMIRINGS[semiring]
+    dev = e.device
+    with torch.cuda.device(dev):
+        part = torch.empty(B, dtype=torch.float32, device=dev)
+        saved = None
+        if want_saved:
+            n = lib.semicrf_edge_scan_saved_size(B, N, K, C, sr)
+            if n == 0 and B > 0:
+                check(SEMICRF_ERR_UNSUPPORTED, "semicrf_edge_scan_saved_size")
+            saved = _scratch(n, dev)
+        st = lib.semicrf_edge_scan_forward(B, N, K, C, _ptr(e), _ptr(ln), sr, _ptr(part),
+                                           _ptr(saved), _stream(dev))
+        check(st, "semicrf_edge_scan_forward")
+    return part, saved
+
+
+def edge_scan_backward(edge, lengths, semiring, saved, grad_output):
+    """semicrf_edge_scan_backward.  Returns grad_edge shaped like edge (float32)."""
+    lib = load()
+    e, ln, B, N, K, C = _edge_inputs(edge, lengths)
+    sr = SEMIRINGS[semiring]
+    dev = e.device
+    with torch.cuda.device(dev):
+        g = grad_output.detach().to(device=dev, dtype=torch.float32).contiguous()
+        ge = torch.zeros_like(e)
+        ws = _scratch(lib.semicrf_edge_scan_backward_workspace_size(B, N, K, C, sr), dev)
+        st = lib.semicrf_edge_scan_backward(B, N, K, C, _ptr(e), _ptr(ln), sr, _ptr(saved),
+                                            _ptr(g), _ptr(ge), _ptr(ws), ws.numel(), _stream(dev))
+        check(st, "semicrf_edge_scan_backward")
+    return ge

@@ -849,3 +849,85 @@ int semicrf_score_gold_backward(int64_t B, int64_t T, int64_t K, int64_t C,
 }
 
 }  // extern "C"
+
+// ---- edge-tensor scan --------------------------------------------------------
+
+namespace {
+
+int es_validate(int64_t B, int64_t N, int64_t K, int64_t C, int semiring) {
+  if (B < 0 || N < 1 || K < 1 || C < 1) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (semiring != SEMICRF_LOG && semiring != SEMICRF_MAX) return SEMICRF_ERR_SEMIRING;
+  if (N > (int64_t)1 << 30 || K > 32767 || C > 32767 || !escan_supported((int)K, (int)C))
+    return SEMICRF_ERR_UNSUPPORTED;
+  return SEMICRF_OK;
+}
+
+struct EsSaved {
+  double *logz, *beta;
+  int32_t* bp;
+};
+
+EsSaved es_carve(Carver& cv, int64_t B, int64_t N, int64_t C, int semiring) {
+  EsSaved e{};
+  e.logz = cv.take<double>(B);
+  e.beta = cv.take<double>((size_t)B * N * C);
+  e.bp = semiring == SEMICRF_MAX ? cv.take<int32_t>((size_t)B * N * C) : nullptr;
+  return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t semicrf_edge_scan_saved_size(int64_t B, int64_t N, int64_t K, int64_t C, int semiring) {
+  if (es_validate(B, N, K, C, semiring) != SEMICRF_OK) return 0;
+  Carver cv(nullptr);
+  es_carve(cv, B, N, C, semiring);
+  return cv.bytes();
+}
+
+int semicrf_edge_scan_forward(int64_t B, int64_t N, int64_t K, int64_t C, const float* edge,
+                              const int64_t* lengths, int semiring, float* partition, void* saved,
+                              void* stream) {
+  int st = es_validate(B, N, K, C, semiring);
+  if (st != SEMICRF_OK) return st;
+  if (B == 0) return SEMICRF_OK;
+  if (!lengths || !partition || (N > 1 && !edge)) return SEMICRF_ERR_INVALID_ARGUMENT;
+  EsSaved e{};
+  if (saved) {
+    Carver cv(saved);
+    e = es_carve(cv, B, N, C, semiring);
+  }
+  return cuda_status(launch_escan_forward((int)B, (int)N, (int)K, (int)C, edge, lengths, semiring,
+                                          partition, e.logz, e.beta, e.bp,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+size_t semicrf_edge_scan_backward_workspace_size(int64_t B, int64_t N, int64_t K, int64_t C,
+                                                 int semiring) {
+  if (es_validate(B, N, K, C, semiring) != SEMICRF_OK) return 0;
+  Carver cv(nullptr);
+  if (semiring == SEMICRF_LOG) cv.take<double>((size_t)B * N * C);
+  return cv.bytes() > 0 ? cv.bytes() : 256;
+}
+
+int semicrf_edge_scan_backward(int64_t B, int64_t N, int64_t K, int64_t C, const float* edge,
+                               const int64_t* lengths, int semiring, const void* saved,
+                               const float* grad_out, float* grad_edge, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  int st = es_validate(B, N, K, C, semiring);
+  if (st != SEMICRF_OK) return st;
+  if (B == 0 || N == 1) return SEMICRF_OK;  // no edges
+  if (!edge || !lengths || !saved || !grad_out || !grad_edge) return SEMICRF_ERR_INVALID_ARGUMENT;
+  if (!workspace || workspace_bytes < semicrf_edge_scan_backward_workspace_size(B, N, K, C, semiring))
+    return SEMICRF_ERR_WORKSPACE;
+  Carver sc(const_cast<void*>(saved));
+  const EsSaved e = es_carve(sc, B, N, C, semiring);
+  Carver cv(workspace);
+  double* gamma = semiring == SEMICRF_LOG ? cv.take<double>((size_t)B * N * C) : nullptr;
+  return cuda_status(launch_escan_backward((int)B, (int)N, (int)K, (int)C, edge, lengths,
+                                           semiring, e.beta, e.logz, e.bp, grad_out, grad_edge,
+                                           gamma, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

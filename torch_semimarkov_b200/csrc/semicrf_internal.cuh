@@ -331,6 +331,16 @@ cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, int 
 cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s);
 cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, cudaStream_t s);
 
+// escan.cu -- the edge-tensor scan
+bool escan_supported(int K, int C);
+cudaError_t launch_escan_forward(int B, int N, int K, int C, const float* edge,
+                                 const int64_t* lengths, int semiring, float* partition,
+                                 double* logz, double* beta_tab, int32_t* bp, cudaStream_t s);
+cudaError_t launch_escan_backward(int B, int N, int K, int C, const float* edge,
+                                  const int64_t* lengths, int semiring, const double* beta,
+                                  const double* logz, const int32_t* bp, const float* grad_output,
+                                  float* grad_edge, double* gamma, cudaStream_t s);
+
 // viterbi.cu
 // backtrace over the packed backpointers of vchain.cu
 size_t backtrace_packed_smem(int T, int C);
