@@ -255,11 +255,15 @@ ORACLE_CASES = [
     (2, 97, 13, 33, "default", "start", "log"),
     (2, 150, 10, 64, "default", None, "log"),
     (2, 60, 9, 130, "default", "end", "log"),
-    (2, 100, 20, 200, "default", "both", "log"),
-    (3, 70, 5, 65, "cfg2", None, "log"),
     (3, 180, 25, 16, "cfg5", None, "max"),
     (2, 120, 1, 6, "default", None, "log"),
     (2, 90, 2, 7, "default", None, "max"),
+    # large label sets (the cluster chain), odd batches, and enough chains for
+    # two per cluster
+    (2, 100, 20, 200, "default", "both", "log"),
+    (3, 70, 5, 65, "cfg2", None, "log"),
+    (20, 48, 6, 70, "default", "both", "log"),
+    (21, 40, 9, 96, "cfg2", None, "log"),
 ]
 
 
