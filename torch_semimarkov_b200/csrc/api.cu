@@ -418,7 +418,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     Carver cv(workspace);
     KccLayout w = carve_kcc(cv, p, false);
     cudaError_t e = launch_kcc_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
-                                    p->semiring, w.pr, s);
+                                    w.pr, s);
     if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
     KccArgs a = kcc_args(p, w.pr);
     a.partition = partition;
@@ -557,7 +557,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     Carver sc(const_cast<void*>(saved));
     SavedLayout sl = carve_saved(sc, p);
     cudaError_t e = launch_kcc_prep(p->transition, p->duration_bias, (int)p->K, (int)p->C,
-                                    p->semiring, w.pr, s);
+                                    w.pr, s);
     if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
     KccArgs a = kcc_args(p, w.pr);
     a.logz = sl.logz;

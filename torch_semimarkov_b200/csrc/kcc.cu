@@ -801,9 +801,9 @@ int kcc_tr_slices(int B, int K, int C) {
   return ns < 1 ? 1 : ns;
 }
 
-cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, int semiring,
-                            const KccPrep& pr, cudaStream_t s) {
-  (void)semiring;
+// the raw factors rf / rb are written when the carve gave them (max semiring)
+cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, const KccPrep& pr,
+                            cudaStream_t s) {
   kcc_prep_kernel<<<grid_for((size_t)K * C, 128), 128, 0, s>>>(tr, db, K, C, pr);
   return cudaGetLastError();
 }

@@ -326,8 +326,8 @@ bool kcc_supported(int C, int K);
 size_t kcc_prep_doubles(int K, int C, int semiring);
 KccPrep kcc_prep_carve(double* base, int K, int C, int semiring);
 int kcc_tr_slices(int B, int K, int C);
-cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, int semiring,
-                            const KccPrep& pr, cudaStream_t s);
+cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, const KccPrep& pr,
+                            cudaStream_t s);
 cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s);
 cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, cudaStream_t s);
 
