@@ -349,6 +349,10 @@ def main():
                                              "cfg3: B=1 T=1e6 K=1000 C=8, one GPU")
         others["large_C"] = bench_fwd_bwd(dev, flush, "cfg4", 32, 4096, 64, 256,
                                           "cfg4: B=32 T=4096 K=64 C=256")
+        others["duration_transitions"] = bench_fwd_bwd(
+            dev, flush, "cfg2", 64, 10000, 300, 24,
+            "cfg2 shape with (K, C, C) duration-dependent transitions ~N(0, 0.1^2): "
+            "B=64 T=10000 K=300 C=24", kcc=True)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -409,6 +413,12 @@ def main():
                              "ns_per_position_step": t_fwd / T * 1e9,
                              "ctas": 2 * B, "sms": torch.cuda.get_device_properties(dev)
                              .multi_processor_count},
+        # the reference's O(T K C^2) formulation does (K-1) C^2 semiring edge
+        # terms per position and pass, four passes per fwd+bwd (forward, alpha
+        # recompute, beta, marginals); this is the rate at which the same
+        # result is produced in those units (not work this build executes)
+        "reference_equivalent": {"edge_terms_per_position_pass": kcap * C * C, "passes": 4,
+                                 "edge_terms_per_s": 4 * kcap * C * C * B * T / t_step},
         # per step: forward = prep (2) + chains (1); backward = pos, blk, tr, db, reduce
         "gpu_launches": 8 * args.steps,
         "clocks": clocks,
@@ -421,14 +431,14 @@ def main():
     print(json.dumps(line), flush=True)
 
 
-def bench_fwd_bwd(dev, flush, gen, Bc, Tc, Kc, Cc, label):
+def bench_fwd_bwd(dev, flush, gen, Bc, Tc, Kc, Cc, label, kcc=False):
     """fwd+bwd positions/s of another configuration (inputs resident)."""
     import torch
 
     from inputs import config_lengths, make_streaming_inputs
     from torch_semimarkov_b200 import semi_crf_streaming_forward
 
-    inp = make_streaming_inputs(Bc, Tc, Kc, Cc, seed=3, gen=gen)
+    inp = make_streaming_inputs(Bc, Tc, Kc, Cc, seed=3, gen=gen, kcc=kcc)
     cum = inp["cum_scores"].to(dev)
     tr = inp["transition"].to(dev)
     db = inp["duration_bias"].to(dev)

@@ -297,6 +297,11 @@ KCC_CASES = [
     (2, 30, 3, 130, "default", None, "log"),
     (2, 150, 120, 20, "cfg2", None, "log"),
     (2, 90, 70, 24, "default", None, "max"),
+    # many 16-position blocks with ragged lengths, and N(0,1) emissions that
+    # move the per-label frames between blocks
+    (3, 400, 40, 6, "cfg2", "both", "log"),
+    (2, 500, 50, 8, "cfg5", None, "log"),
+    (2, 200, 17, 33, "cfg5", "end", "log"),
 ]
 
 

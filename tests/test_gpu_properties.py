@@ -140,3 +140,26 @@ def test_traceback_invariants(B, T, K, C):
         total = sum(s.score for s in segs)
         score = float(res.scores[b])
         assert abs(total - score) <= 1e-5 * abs(score) + 1e-4, f"{b}: {total} vs {score}"
+
+
+@pytest.mark.parametrize("kcc", [False, True])
+def test_float64_inputs(kcc):
+    """float64 inputs (the dtype of the reference's gradcheck tests) give the
+    float32 results up to input rounding, with gradients in the inputs' dtype."""
+    from torch_semimarkov_b200 import semi_crf_streaming_forward
+
+    dev = _dev()
+    B, T, K, C = 3, 50, 6, 4
+    inp = _inputs(B, T, K, C, seed=305, kcc=kcc)
+    lengths = torch.tensor([50, 37, 21], device=dev)
+    p32, g32 = _grads(inp, lengths, K, torch.ones(B, device=dev))
+    leaves = {k: v.detach().double().requires_grad_(True) for k, v in inp.items() if v is not None}
+    p64 = semi_crf_streaming_forward(leaves["cum_scores"], leaves["transition"],
+                                     leaves["duration_bias"], lengths, K)
+    assert p64.dtype == torch.float64
+    p64.sum().backward()
+    torch.testing.assert_close(p64, p32.double(), rtol=1e-6, atol=1e-5)
+    for key in ("cum_scores", "transition", "duration_bias"):
+        g = leaves[key].grad
+        assert g.dtype == torch.float64, key
+        torch.testing.assert_close(g, g32[key], rtol=1e-5, atol=1e-6)

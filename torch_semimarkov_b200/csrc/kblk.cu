@@ -1,0 +1,492 @@
+// kblk.cu -- (K, C, C) transitions, log semiring: the blocked chain.
+//
+// The recurrences are those of kcc.cu (pytorch_reference.py:87-111 with
+// transition[k] per duration, :213 and :437-446):
+//   alpha[t,c] = ct[t,c] + (+)_{k,c'} ( alpha[t-k,c'] + tr[k][c',c] + db[k,c] + dt[t-k,c] )
+//   beta[s,c'] = (+)_{k,c} ( tr[k][c',c] + db[k,c] + dt[s,c] + ct[s+k,c] + beta[s+k,c] )
+// with ct[t,c] = cum[t,c] + pe[t-1,c], dt[s,c] = ps[s,c] - cum[s,c], alpha[0] = 0,
+// beta[len] = 0, durations k = 1 .. K-1.  Both directions are written in the
+// chain's own position index rho (rho = t forward, rho = len - s backward), in
+// which the source of duration k is rho - k.
+//
+// Positions are processed in blocks of P.  With the per-label constant
+// fk[c] = max_{k,c'} (tr[k][c',c] + db[k,c]) the weights
+//   xf[k][m][l] = exp(tr[k][m][l] + db[k][l] - fk[l])   (forward, m = source label)
+//   xb[k][m][l] = exp(tr[k][l][m] + db[k][m] - fk[m])   (backward, m = next label)
+// are at most 1, and every source enters in float64 linear form relative to a
+// per-label frame fixed at the start of its block:
+//   forward   a[s,m] = exp(alpha[s,m] - n_s),  y[s,l] = exp(n_s + dt[s,l] + fk[l] - F[l])
+//             exp(alpha[t,l] - ct[t,l] - F[l]) = sum_{s,m} xf[t-s][m][l] a[s,m] y[s,l] w[l]
+//   backward  g[u,m] = exp(beta[u,m] + ct[u,m] + fk[m] - H[m]),  v[s,m] = exp(dt[s,m] + H[m] - Rb)
+//             exp(beta[s,l] - Rb) = sum_m v[s,m] sum_u xb[u-s][m][l] g[u,m] w[m]
+// where n_s is the row maximum of alpha, F (H) the frame of the target block
+// and w = exp(frame of the source's block - frame of the target block).  A
+// frame is taken from the last row of the previous block, so within a block
+// the factors only drift by the emissions of P positions; values that fall
+// below the float64 range are dropped (their weight relative to the row's
+// maximum is below e^-700).
+//
+// Per block, with all threads of the CTA:
+//  1. far sums: every source in an earlier block.  The work of output label l
+//     is (contracted label m) x (source block q) units; one unit is the P x P
+//     Toeplitz tile out[j] += sum_r x[D + j - r][m][l] z[r] (D = block
+//     distance), evaluated from a register window of 2P-1 weights that slides
+//     by P between consecutive source blocks, so each weight is loaded once
+//     per block and used P times.  Units are split evenly over the threads of
+//     each label; a fixed-order sum over the threads gives the block's
+//     pending values.
+//  2. the P rows in order: a row's source factors are its pending values
+//     times a per-block factor, and its contributions to the later rows of
+//     the block (durations 1 .. P-1) are one C-term dot product per (target,
+//     label) with weights held in registers; one barrier per row.
+//  3. the block's log tables and row maxima, in parallel.
+// The tables written are those of kcc_chain_kernel: log alpha and its row
+// maxima (forward), log beta (backward), log Z and the ring checkpoints.
+
+#include "semicrf_internal.cuh"
+
+namespace semicrf {
+
+namespace {
+
+constexpr int kBT = 256;  // threads per CTA
+constexpr int kBP = 16;   // positions per block
+constexpr size_t kBSmemMax = 220 * 1024;
+
+__device__ __forceinline__ int bseq_len(const int64_t* lengths, int b, int T) {
+  const long long l = lengths[b];
+  return l < 0 ? 0 : (l > T ? T : (int)l);
+}
+
+__device__ __forceinline__ int floor_div(int a, int b) {
+  return a >= 0 ? a / b : -((-a + b - 1) / b);
+}
+
+// Shared memory of the blocked chain (offsets in doubles, each even).
+struct BlkPlan {
+  int nbr, R;
+  size_t ra, ry, fn, fd, wq, pend, part, ctb, dtb, kap, vb, lv, fk, vals, red, total;
+};
+__host__ __device__ inline BlkPlan blk_plan(int C, int K, int P) {
+  BlkPlan p{};
+  p.nbr = (K - 1 + P - 1) / P + 2;  // far source blocks + the current one + 1
+  p.R = p.nbr * P;
+  size_t o = 0;
+  auto take = [&](size_t n) {
+    const size_t r = o;
+    o += (n + 1) & ~size_t(1);
+    return r;
+  };
+  p.ra = take((size_t)p.R * C);    // forward a rows / backward g rows
+  p.ry = take((size_t)p.R * C);    // forward y rows
+  p.fn = take(p.nbr);              // frame of each block in the ring: scalar part N
+  p.fd = take((size_t)p.nbr * C);  // and per-label part (dt or ct of its reference row)
+  p.wq = take((size_t)p.nbr * C);  // rebase factor per far source block
+  p.pend = take((size_t)P * C);    // pending values of the block's positions
+  p.part = take((size_t)P * kBT);  // per-thread far sums
+  p.ctb = take((size_t)P * C);
+  p.dtb = take((size_t)P * C);
+  p.kap = take((size_t)P * C);     // factor from pending value to source factor
+  p.vb = take((size_t)P * C);      // forward y / backward target factors v
+  p.lv = take((size_t)P * C);      // the block's log values
+  p.fk = take(C);
+  p.vals = take(C);
+  p.red = take(64);
+  p.total = o;
+  return p;
+}
+
+constexpr int kRegC = 32;  // largest C whose near weights are kept in registers
+
+// Frames.  Block tau has a scalar N and per-label offsets fd[l], taken from
+// the row before the block (its reference row; position 0 or len for the
+// first block): forward N = max_l alpha, fd = dt of that row, and
+//   F[l] = N + fd[l] + fk[l]    a[s,m] = pend[s,m] exp(ct[s,m] + fd[m] + fk[m])
+//                               y[s,l] = exp(dt[s,l] - fd[l])
+// backward N = max_l beta, fd = ct of that row, rb = max_m (dt[first,m] + fd[m] + fk[m]),
+//   H[m] = N + fd[m] + fk[m]    g[u,m] = pend[u,m] exp(rb + ct[u,m] - fd[m])
+//                               v[s,m] = exp(dt[s,m] + fd[m] + fk[m] - rb)
+// where pend is the row's sum relative to its frame, so alpha = N + log a and
+// beta = N + fd - ct + log g.  The kernel accumulates the factors a (g)
+// directly: every contribution to a row is multiplied by the row's
+// exp(ct + fd + fk) (exp(rb + ct - fd)), so no log or exp lies between the
+// rows of a block.  The log tables are written per block, after its rows.
+template <int P, int CR>
+__global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
+  extern __shared__ __align__(16) double bsm[];
+  const int C = a.C, K = a.K, T = a.T, kcap = a.kcap;
+  const int b = blockIdx.x, dir = blockIdx.y, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int Lb = bseq_len(a.lengths, b, T);
+  const BlkPlan pl = blk_plan(C, K, P);
+  const int NBR = pl.nbr;
+  double* ra = bsm + pl.ra;
+  double* ry = bsm + pl.ry;
+  double* fN = bsm + pl.fn;
+  double* fd = bsm + pl.fd;
+  double* wq = bsm + pl.wq;
+  double* pend = bsm + pl.pend;
+  double* part = bsm + pl.part;
+  double* ctb = bsm + pl.ctb;
+  double* dtb = bsm + pl.dtb;
+  double* kap = bsm + pl.kap;
+  double* vb = bsm + pl.vb;
+  double* lv = bsm + pl.lv;
+  double* fk = bsm + pl.fk;
+  double* vals = bsm + pl.vals;
+  double* red = bsm + pl.red;  // [32]: maximum of the last row of the previous block; [33]: rb
+  const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
+  const float* ps_b = a.ps ? a.ps + (size_t)b * T * C : nullptr;
+  const float* pe_b = a.pe ? a.pe + (size_t)b * T * C : nullptr;
+  const double* X = dir == 0 ? a.pr.xf : a.pr.xb;
+  const size_t CC = (size_t)C * C;
+
+  for (int i = tid; i < C; i += kBT) fk[i] = a.pr.fk[i];
+  if (dir == 0 && a.ref_ckpt) {
+    float* rc = a.ref_ckpt + (size_t)b * a.nref * K * C;
+    for (size_t i = tid; i < (size_t)a.nref * K * C; i += kBT)
+      rc[i] = (i < (size_t)C) ? 0.f : kRefNegInf;
+  }
+  if (tid == 0) red[32] = 0.0;
+  __syncthreads();
+
+  const int G = kBT / C, ell = tid % C, sig = tid / C;
+  const bool act = sig < G;
+  const int nblk = Lb / P + 1;
+  const int nnear = (P - 1) * C;  // (duration 1..P-1, label) items of the in-block contributions
+  for (int tau = 0; tau < nblk; ++tau) {
+    const int s0 = tau * P, fs = tau % NBR;
+    // this block's frame from its reference row (the previous block's last row,
+    // still in ctb / dtb); a row of -inf keeps the previous frame
+    {
+      const double nr = red[32];
+      const bool fresh = tau == 0 || nr > -INFINITY;
+      for (int l = tid; l < C; l += kBT) {
+        double d;
+        if (tau == 0) {
+          const double cu = cum_b[(size_t)(dir == 0 ? 0 : Lb) * C + l];
+          d = dir == 0 ? ((ps_b && T > 0) ? (double)ps_b[l] : 0.0) - cu
+                       : cu + ((pe_b && Lb >= 1) ? (double)pe_b[(size_t)(Lb - 1) * C + l] : 0.0);
+        } else {
+          d = fresh ? (dir == 0 ? dtb : ctb)[(P - 1) * C + l] : fd[((tau - 1) % NBR) * C + l];
+        }
+        fd[fs * C + l] = d;
+      }
+      if (tid == 0) fN[fs] = tau == 0 ? 0.0 : (fresh ? nr : fN[(tau - 1) % NBR]);
+    }
+    __syncthreads();
+    const double N = fN[fs];
+    // the block's input terms; pending values start at zero
+    for (int i = tid; i < P * C; i += kBT) {
+      const int j = i / C, l = i % C, rho = s0 + j;
+      double cv = 0.0, dv = 0.0;
+      if (rho <= Lb) {
+        const int t = dir == 0 ? rho : Lb - rho;
+        const double cu = cum_b[(size_t)t * C + l];
+        cv = cu + ((pe_b && t >= 1) ? (double)pe_b[(size_t)(t - 1) * C + l] : 0.0);
+        dv = ((ps_b && t < T) ? (double)ps_b[(size_t)t * C + l] : 0.0) - cu;
+      }
+      ctb[i] = cv;
+      dtb[i] = dv;
+      pend[i] = rho == 0 ? 1.0 : 0.0;  // position 0: alpha = 0 (beta = 0), factor 1
+    }
+    const int bmin = max(0, floor_div(s0 - kcap, P));
+    const int nq = tau - bmin;  // far source blocks bmin .. tau-1
+    for (int i = tid; i < nq * C; i += kBT) {
+      const int q = (bmin + i / C) % NBR, l = i % C;
+      wq[q * C + l] = exp(fmin(fN[q] - N + fd[q * C + l] - fd[fs * C + l], 700.0));
+    }
+    __syncthreads();
+    double rb = 0.0;
+    if (dir == 1) {
+      if (warp == 0) {
+        const int jf = tau == 0 ? 1 : 0;
+        double mx = -INFINITY;
+        if (s0 + jf <= Lb)
+          for (int m = lane; m < C; m += 32) mx = fmax(mx, dtb[jf * C + m] + fd[fs * C + m] + fk[m]);
+        for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red[33] = mx;
+      }
+      __syncthreads();
+      rb = red[33];
+    }
+    // per-row factors of the block
+    for (int i = tid; i < P * C; i += kBT) {
+      const int j = i / C, l = i % C;
+      const double dd = fd[fs * C + l];
+      if (dir == 0) {
+        kap[i] = exp(fmin(ctb[i] + dd + fk[l], 700.0));
+        const double y = exp(fmin(dtb[i] - dd, 700.0));
+        vb[i] = y;
+        ry[(size_t)(fs * P + j) * C + l] = y;
+      } else {
+        const bool ok = rb > -INFINITY;
+        vb[i] = ok ? exp(fmin(dtb[i] + dd + fk[l] - rb, 700.0)) : 0.0;
+        kap[i] = ok ? exp(fmin(rb + ctb[i] - dd, 700.0)) : 0.0;
+      }
+    }
+    __syncthreads();
+
+    // 1. far sums
+    if (nq > 0) {
+      double out[P];
+#pragma unroll
+      for (int j = 0; j < P; ++j) out[j] = 0.0;
+      if (act) {
+        const int U = C * nq;
+        const int u0 = (int)((long long)sig * U / G), u1 = (int)((long long)(sig + 1) * U / G);
+        double d[2 * P - 1], nx[P];
+        for (int u = u0; u < u1; ++u) {
+          const int m = u / nq, q = bmin + u % nq;
+          const int D = (tau - q) * P;
+          const double* xc = X + (size_t)m * C + ell;
+          if (u > u0 && u % nq != 0) {  // same label as the previous unit, next source block
+#pragma unroll
+            for (int i = 2 * P - 2; i >= P; --i) d[i] = d[i - P];
+#pragma unroll
+            for (int i = 0; i < P; ++i) d[i] = nx[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 2 * P - 1; ++i) {
+              const int k = D - P + 1 + i;
+              d[i] = k <= kcap ? __ldcg(xc + (size_t)k * CC) : 0.0;
+            }
+          }
+          // the next unit's new weights, in flight during this unit's tile
+          if (u + 1 < u1 && (u + 1) % nq != 0) {
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+              const int k = D - 2 * P + 1 + i;
+              nx[i] = (k >= 1 && k <= kcap) ? __ldcg(xc + (size_t)k * CC) : 0.0;
+            }
+          }
+          const int base = (q % NBR) * P;
+          double z[P];
+          if (dir == 0) {
+            const double w = wq[(q % NBR) * C + ell];
+#pragma unroll
+            for (int r = 0; r < P; ++r)
+              z[r] = ra[(size_t)(base + r) * C + m] * ry[(size_t)(base + r) * C + ell] * w;
+#pragma unroll
+            for (int r = 0; r < P; ++r)
+#pragma unroll
+              for (int j = 0; j < P; ++j) out[j] = fma(d[P - 1 + j - r], z[r], out[j]);
+          } else {
+            const double w = wq[(q % NBR) * C + m];
+#pragma unroll
+            for (int r = 0; r < P; ++r) z[r] = ra[(size_t)(base + r) * C + m] * w;
+            double acc[P];
+#pragma unroll
+            for (int j = 0; j < P; ++j) acc[j] = 0.0;
+#pragma unroll
+            for (int r = 0; r < P; ++r)
+#pragma unroll
+              for (int j = 0; j < P; ++j) acc[j] = fma(d[P - 1 + j - r], z[r], acc[j]);
+#pragma unroll
+            for (int j = 0; j < P; ++j) out[j] = fma(vb[j * C + m], acc[j], out[j]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < P; ++j) part[j * kBT + tid] = out[j];
+      __syncthreads();
+      for (int i = tid; i < P * C; i += kBT) {
+        const int j = i / C, l = i % C;
+        double s = 0.0;
+        for (int g = 0; g < G; ++g) s += part[j * kBT + g * C + l];
+        pend[i] = s * kap[i];
+      }
+      __syncthreads();
+    }
+
+    // 2. the block's rows in order.  pend holds a row's source factors (a or
+    // g) once the row is complete.  Item i = tid + r * kBT of row j is the
+    // contribution of row j to row j + k (k = 1 + i / C) at label i % C; its
+    // C weights do not depend on j and stay in registers for the block (CR >
+    // 0: C <= CR).  One barrier per row.
+    const int last = min(P - 1, Lb - s0);
+    if constexpr (CR > 0) {
+      constexpr int NREP = ((P - 1) * CR + kBT - 1) / kBT;
+      double w[NREP][CR];
+      int kr[NREP], lr[NREP];
+      bool vr[NREP];
+#pragma unroll
+      for (int rep = 0; rep < NREP; ++rep) {
+        const int i = tid + rep * kBT;
+        kr[rep] = 1 + i / C;
+        lr[rep] = i % C;
+        vr[rep] = i < nnear && kr[rep] <= kcap;
+#pragma unroll
+        for (int m = 0; m < CR; ++m)
+          w[rep][m] = (vr[rep] && m < C) ? __ldg(X + ((size_t)kr[rep] * C + m) * C + lr[rep]) : 0.0;
+      }
+      for (int j = 0; j <= last; ++j) {
+        const double* pj = pend + j * C;
+#pragma unroll
+        for (int rep = 0; rep < NREP; ++rep) {
+          const int jj = j + kr[rep], l = lr[rep];
+          if (vr[rep] && jj <= last) {
+            double s4[4] = {0.0, 0.0, 0.0, 0.0};
+            if (dir == 0) {
+#pragma unroll
+              for (int m = 0; m < CR; ++m)
+                if (m < C) s4[m & 3] = fma(pj[m], w[rep][m], s4[m & 3]);
+              pend[jj * C + l] +=
+                  kap[jj * C + l] * vb[j * C + l] * ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+            } else {
+              const double* vj = vb + jj * C;
+#pragma unroll
+              for (int m = 0; m < CR; ++m)
+                if (m < C) s4[m & 3] = fma(pj[m] * vj[m], w[rep][m], s4[m & 3]);
+              pend[jj * C + l] += kap[jj * C + l] * ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+            }
+          }
+        }
+        __syncthreads();
+      }
+    } else {
+      for (int j = 0; j <= last; ++j) {
+        const double* pj = pend + j * C;
+        for (int i = tid; i < nnear; i += kBT) {
+          const int k = 1 + i / C, l = i % C, jj = j + k;
+          if (k > kcap || jj > last) continue;
+          const double* xk = X + (size_t)k * CC + l;
+          const double* vj = vb + jj * C;
+          auto am = [&](int m) { return dir == 0 ? pj[m] : pj[m] * vj[m]; };
+          double s0a = 0.0, s1a = 0.0, s2a = 0.0, s3a = 0.0;
+          int m = 0;
+          for (; m + 3 < C; m += 4) {
+            s0a = fma(am(m), __ldg(xk + (size_t)m * C), s0a);
+            s1a = fma(am(m + 1), __ldg(xk + (size_t)(m + 1) * C), s1a);
+            s2a = fma(am(m + 2), __ldg(xk + (size_t)(m + 2) * C), s2a);
+            s3a = fma(am(m + 3), __ldg(xk + (size_t)(m + 3) * C), s3a);
+          }
+          for (; m < C; ++m) s0a = fma(am(m), __ldg(xk + (size_t)m * C), s0a);
+          pend[jj * C + l] += kap[jj * C + l] * (dir == 0 ? vb[j * C + l] : 1.0) *
+                              ((s0a + s1a) + (s2a + s3a));
+        }
+        __syncthreads();
+      }
+    }
+
+    // 3. the block's log tables and row maxima
+    const int nrow = last + 1;
+    for (int i = tid; i < nrow * C; i += kBT) {
+      const int j = i / C, l = i % C, rho = s0 + j;
+      const int t = dir == 0 ? rho : Lb - rho;
+      const double pv = pend[i];
+      ra[(size_t)(fs * P + j) * C + l] = pv;
+      double v = 0.0;
+      if (rho > 0)
+        v = pv > 0.0 ? (dir == 0 ? N : N + fd[fs * C + l] - ctb[i]) + log(pv) : -INFINITY;
+      lv[i] = v;
+      if (dir == 0) {
+        if (a.alpha) a.alpha[((size_t)b * (T + 1) + t) * C + l] = v;
+        if (a.ref_ckpt) {
+          const int S = a.sref;
+          const int ic = (t + S - 1) / S;
+          if (ic < a.nref && (long long)ic * S <= Lb && (long long)ic * S - t < K)
+            a.ref_ckpt[(((size_t)b * a.nref + ic) * K + (t % K)) * C + l] =
+                v > -INFINITY ? (float)v : kRefNegInf;
+        }
+      } else if (a.beta) {
+        a.beta[((size_t)b * (T + 1) + t) * C + l] = v;
+      }
+    }
+    __syncthreads();
+    for (int j = warp; j < nrow; j += kBT / 32) {
+      double mx = -INFINITY;
+      for (int l = lane; l < C; l += 32) mx = fmax(mx, lv[j * C + l]);
+      for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) {
+        const int t = dir == 0 ? s0 + j : Lb - (s0 + j);
+        if (dir == 0 && a.amax) a.amax[(size_t)b * (T + 1) + t] = mx;
+        if (j == P - 1) red[32] = mx;
+      }
+    }
+    if (s0 + last == Lb)
+      for (int l = tid; l < C; l += kBT) vals[l] = lv[last * C + l];
+    __syncthreads();
+  }
+  if (dir == 0 && tid == 0) {
+    double lz = (double)kRefNegInf;
+    if (Lb > 0) {
+      double M = -INFINITY;
+      for (int q = 0; q < C; ++q) M = fmax(M, vals[q]);
+      if (M > -INFINITY) {
+        double Sz = 0.0;
+        for (int q = 0; q < C; ++q) Sz += exp(vals[q] - M);
+        lz = M + log(Sz);
+      }
+    }
+    if (a.logz) a.logz[b] = lz;
+    if (a.partition) a.partition[b] = (float)lz;
+  }
+}
+
+// fk[c] = max over durations 1 .. K-1 and source labels of tr + db (the
+// prepared tdf), 0 when that is -inf so the weights of the label become 0
+__global__ void kblk_fk_kernel(int K, int C, KccPrep pr) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double m = -INFINITY;
+  for (int k = 1; k < K; ++k) m = fmax(m, pr.tdf[(size_t)k * C + c]);
+  pr.fk[c] = m > -INFINITY ? m : 0.0;
+}
+
+__global__ void kblk_weights_kernel(const float* __restrict__ tr, const float* __restrict__ db,
+                                    int K, int C, KccPrep pr) {
+  const size_t CC = (size_t)C * C, n = (size_t)K * CC;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i / CC), m = (int)((i / C) % C), l = (int)(i % C);
+    double f = 0.0, g = 0.0;
+    if (k >= 1) {
+      const float* tk = tr + (size_t)k * CC;
+      f = exp((double)tk[(size_t)m * C + l] + (double)db[(size_t)k * C + l] - pr.fk[l]);
+      g = exp((double)tk[(size_t)l * C + m] + (double)db[(size_t)k * C + m] - pr.fk[m]);
+    }
+    pr.xf[i] = f;
+    pr.xb[i] = g;
+  }
+}
+
+}  // namespace
+
+bool kblk_supported(int C, int K) {
+  if (K < 2 || C < 1 || C > 128) return false;
+  return blk_plan(C, K, kBP).total * 8 <= kBSmemMax;
+}
+
+cudaError_t launch_kblk_prep(const float* tr, const float* db, int K, int C, const KccPrep& pr,
+                             cudaStream_t s) {
+  if (!pr.xf) return cudaSuccess;
+  kblk_fk_kernel<<<(C + 127) / 128, 128, 0, s>>>(K, C, pr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t n = (size_t)K * C * C;
+  size_t g = (n + 255) / 256;
+  if (g > 148 * 8) g = 148 * 8;
+  kblk_weights_kernel<<<(int)(g < 1 ? 1 : g), 256, 0, s>>>(tr, db, K, C, pr);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s) {
+  if (a.B <= 0) return cudaSuccess;
+  const size_t bytes = blk_plan(a.C, a.K, kBP).total * 8;
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return e;
+    kern<<<dim3(a.B, ndir), kBT, bytes, s>>>(a);
+    return cudaGetLastError();
+  };
+  // register-held in-block weights for C <= kRegC, sized to the next multiple of 8
+  if (a.C <= 8) return go(kblk_chain_kernel<kBP, 8>);
+  if (a.C <= 16) return go(kblk_chain_kernel<kBP, 16>);
+  if (a.C <= 24) return go(kblk_chain_kernel<kBP, 24>);
+  if (a.C <= kRegC) return go(kblk_chain_kernel<kBP, kRegC>);
+  return go(kblk_chain_kernel<kBP, 0>);
+}
+
+}  // namespace semicrf

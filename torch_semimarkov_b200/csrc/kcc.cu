@@ -771,9 +771,11 @@ bool kcc_supported(int C, int K) {
   return pos_plan(C, K - 1).total * 8 <= kSmemMax;
 }
 
+// log semiring: ef, eb, tf, tb, tdf and the blocked chain's xf, xb, fk;
+// max semiring: ef, eb, tf, tb, tdf, rf, rb
 size_t kcc_prep_doubles(int K, int C, int semiring) {
   const size_t kcc = (size_t)K * C * C;
-  return (semiring == SEMICRF_MAX ? 4 : 2) * kcc + 3 * (size_t)K * C;
+  return 4 * kcc + 3 * (size_t)K * C + (semiring == SEMICRF_MAX ? 0 : (size_t)C);
 }
 
 KccPrep kcc_prep_carve(double* base, int K, int C, int semiring) {
@@ -788,6 +790,10 @@ KccPrep kcc_prep_carve(double* base, int K, int C, int semiring) {
   if (semiring == SEMICRF_MAX) {
     p.rf = p.tdf + kc;
     p.rb = p.rf + kcc;
+  } else {
+    p.xf = p.tdf + kc;
+    p.xb = p.xf + kcc;
+    p.fk = p.xb + kcc;
   }
   return p;
 }
@@ -805,11 +811,15 @@ int kcc_tr_slices(int B, int K, int C) {
 cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, const KccPrep& pr,
                             cudaStream_t s) {
   kcc_prep_kernel<<<grid_for((size_t)K * C, 128), 128, 0, s>>>(tr, db, K, C, pr);
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_kblk_prep(tr, db, K, C, pr, s);  // the blocked chain's weights (log semiring)
 }
 
 cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s) {
   if (a.B <= 0) return cudaSuccess;
+  if (a.semiring == SEMICRF_LOG && a.pr.xf && kblk_supported(a.C, a.K))
+    return launch_kblk_chains(a, ndir, s);
   const size_t bytes = chain_plan(a.C, a.K).total * 8;
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e =

@@ -293,6 +293,11 @@ struct KccPrep {
   double* tdf;  // (K, C) tf + db
   double* rf;   // max semiring: (K, C, C) [k][c'][c] = tr[k][c',c]
   double* rb;   // max semiring: (K, C, C) [k][c2][c] = tr[k][c,c2]
+  // log semiring, blocked chain (kblk.cu): fk[c] = max_{k>=1,c'} tr[k][c',c] + db[k,c],
+  // xf[k][m][l] = exp(tr[k][m][l] + db[k,l] - fk[l]), xb[k][m][l] = exp(tr[k][l][m] + db[k,m] - fk[m])
+  double* xf;
+  double* xb;
+  double* fk;
 };
 struct KccArgs {
   int B, T, K, C, kcap, semiring;
@@ -330,6 +335,11 @@ cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, cons
                             cudaStream_t s);
 cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s);
 cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, cudaStream_t s);
+// kblk.cu -- the blocked (K, C, C) chain of the log semiring
+bool kblk_supported(int C, int K);
+cudaError_t launch_kblk_prep(const float* tr, const float* db, int K, int C, const KccPrep& pr,
+                             cudaStream_t s);
+cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s);
 
 // escan.cu -- the edge-tensor scan
 bool escan_supported(int K, int C);
