@@ -309,7 +309,7 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SEMICRF_OK : SEMICRF_
 // (K, C, C) transitions: prepared factors, then (backward) the marginal terms
 struct KccLayout {
   KccPrep pr;
-  double *st, *et, *pend, *part_tr;
+  double *st, *et, *pend, *part_tr, *al, *anc, *ep1;
   int nslice;
 };
 
@@ -323,7 +323,13 @@ KccLayout carve_kcc(Carver& cv, const semicrf_problem* p, bool backward) {
   w.st = cv.take<double>(n);
   w.et = cv.take<double>(n);
   w.pend = p->semiring == SEMICRF_MAX ? cv.take<double>(n) : nullptr;
-  w.nslice = kcc_tr_slices((int)p->batch, K, C);
+  const bool blk = p->semiring == SEMICRF_LOG && kblk_supported(C, K);
+  if (blk) {
+    w.al = cv.take<double>(n);
+    w.ep1 = cv.take<double>(n);
+    w.anc = cv.take<double>((size_t)p->batch * kblk_anchor_rows((int)p->T) * C);
+  }
+  w.nslice = blk ? kblk_tr_slices((int)p->batch, K, C) : kcc_tr_slices((int)p->batch, K, C);
   w.part_tr = cv.take<double>((size_t)w.nslice * C * (size_t)(K - 1) * C);
   return w;
 }
@@ -573,6 +579,9 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     a.pend = w.pend;
     a.part_tr = w.part_tr;
     a.nslice = w.nslice;
+    a.al = w.al;
+    a.anc = w.anc;
+    a.ep1 = w.ep1;
     return cuda_status(launch_kcc_grads(a, grad_transition, grad_duration_bias, s));
   }
   if (p->semiring == SEMICRF_LOG) {

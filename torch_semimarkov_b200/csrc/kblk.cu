@@ -451,6 +451,282 @@ __global__ void kblk_weights_kernel(const float* __restrict__ tr, const float* _
   }
 }
 
+// ---------------------------------------------------------------------------
+// Gradients (log semiring).  The segment marginal
+//   P(s -> e, m -> l) = exp(alpha[s,m] + tr[e-s][m][l] + db[e-s,l] + dt[s,l] + ct[e,l]
+//                           + beta[e,l] - logZ)   (pytorch_reference.py:458-499)
+// is written with per-position float64 factors and the weights xf:
+//   P = al[s,m] xf[e-s][m][l] Sp[s,l] Ep[e,l] Z(q(s), q(e), l)
+//   al = exp(alpha - amax), Sp = exp(st - A[q(s)]), Ep = exp(et + A[q(e)] + fk),
+//   Z(q, q') = exp(A[q] - A[q'])
+// with st = amax + dt - logZ and et = beta + ct (kcc_terms_kernel) and A[q,l]
+// the maximum of st over block q's rows, so Sp <= 1 and the products stay in
+// range.  grad_transition[k][m][l] = xf[k][m][l] sum_b g_b sum_s al[s,m] Sp[s,l]
+// Ep[s+k,l] Z is a lag correlation per label pair; the start marginal
+// Pstart[s,l] = Sp[s,l] sum_{k,m} al[s,m] xf[k][m][l] Ep[s+k,l] Z is a Toeplitz
+// product per (source block, label).  Both evaluate P x P register tiles from a
+// window of 2P-1 end factors.
+
+// A[b][q][l]: maximum of st over the rows s < len of block q; a block without a
+// finite one takes -max(et + fk) of its rows (0 when none), which keeps its end
+// factors at most 1
+__global__ void kblk_anchor_kernel(const KccArgs a) {
+  const int C = a.C, T = a.T, nb = T / kBP + 1;
+  const size_t n = (size_t)a.B * nb * C;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const size_t bq = i / C;
+    const int q = (int)(bq % nb), b = (int)(bq / nb);
+    const int Lb = bseq_len(a.lengths, b, T);
+    const size_t row0 = (size_t)b * (T + 1);
+    double m = -INFINITY, me = -INFINITY;
+    for (int r = 0; r < kBP; ++r) {
+      const int s = q * kBP + r;
+      if (s < Lb) m = fmax(m, a.st[(row0 + s) * C + c]);
+      if (s >= 1 && s <= Lb) me = fmax(me, a.et[(row0 + s) * C + c]);
+    }
+    a.anc[i] = m > -INFINITY ? m : (me > -INFINITY ? -(me + a.pr.fk[c]) : 0.0);
+  }
+}
+
+// al, and st / et replaced by Sp / Ep in place
+__global__ void kblk_factor_kernel(const KccArgs a) {
+  const int C = a.C, T = a.T, nb = T / kBP + 1;
+  const size_t n = (size_t)a.B * (T + 1) * C;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const size_t bt = i / C;
+    const int t = (int)(bt % (T + 1)), b = (int)(bt / (T + 1));
+    const int Lb = bseq_len(a.lengths, b, T);
+    const double A = a.anc[((size_t)b * nb + t / kBP) * C + c];
+    const double A1 = t >= kBP ? a.anc[((size_t)b * nb + t / kBP - 1) * C + c] : 0.0;
+    double av = 0.0, sv = 0.0, ev = 0.0, ev1 = 0.0;
+    if (t < Lb) {
+      const double nm = a.amax[bt], x = a.alpha[i];
+      if (nm > -INFINITY && x > -INFINITY) av = exp(x - nm);
+      const double st = a.st[i];
+      if (st > -INFINITY) sv = exp(st - A);
+    }
+    if (t >= 1 && t <= Lb) {
+      const double et = a.et[i];
+      if (et > -INFINITY) {
+        ev = exp(fmin(et + A + a.pr.fk[c], 700.0));
+        if (t >= kBP) ev1 = exp(fmin(et + A1 + a.pr.fk[c], 700.0));
+      }
+    }
+    a.al[i] = av;
+    a.st[i] = sv;
+    a.et[i] = ev;
+    a.ep1[i] = ev1;
+  }
+}
+
+// the window of end factors for source block q and lag chunk lam: rows
+// (q + lam) * P + x, x < 2P-1, relative to block q's anchor
+template <int P>
+__device__ __forceinline__ void end_window(const KccArgs& a, const double* anc, size_t row0,
+                                           int Lb, int nb, int q, int lam, int l, double* w) {
+  const int C = a.C, q1 = q + lam;
+  const double Aq = anc[(size_t)q * C + l];
+  const double z1 = q1 < nb ? exp(fmin(Aq - anc[(size_t)q1 * C + l], 700.0)) : 0.0;
+  const double z2 = q1 + 1 < nb ? exp(fmin(Aq - anc[(size_t)(q1 + 1) * C + l], 700.0)) : 0.0;
+#pragma unroll
+  for (int x = 0; x < 2 * P - 1; ++x) {
+    const int e = q1 * P + x;
+    w[x] = e <= Lb ? a.et[(row0 + e) * C + l] * (x < P ? z1 : z2) : 0.0;
+  }
+}
+
+__device__ __forceinline__ void cp_async8z(double* dst, const double* src, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  const int n = valid ? 8 : 0;  // 0: the destination is zero-filled
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(src), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_g() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_1() {
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+}
+
+// part[slice][m][(k-1)*C + l] = sum over the slice's sequences and sources of
+// g_b al[s,m] Sp[s,l] Ep[s+k,l] Z.  A CTA takes one lag chunk lam (k = lam*P + i),
+// one slice and up to blockDim label pairs; its items are the (sequence, source
+// block q) of the slice.  An item's rows -- al and Sp of the block's sources,
+// the end factors of rows (q+lam)*P .. +2P-2 (block q+lam relative to its own
+// anchor, block q+lam+1 relative to block q+lam's) and the two anchors -- are
+// staged in shared memory by cp.async, one item ahead, so the item's factor
+// exp(A[q] - A[q+lam]) is a single scale of the source values.
+template <int P>
+__global__ void __launch_bounds__(kBT, 2) kblk_tr_kernel(const KccArgs a, int nch, int npg) {
+  extern __shared__ __align__(16) double tsm[];
+  const int C = a.C, T = a.T, kcap = a.kcap, nb = T / P + 1;
+  const int npair = C * C, tid = threadIdx.x, nt = blockDim.x;
+  const int pg = blockIdx.x % npg, rest = blockIdx.x / npg;
+  const int lam = rest % nch, slice = rest / nch;
+  const int pair = pg * nt + tid;
+  const bool act = pair < npair;
+  const int m = act ? pair / C : 0, l = act ? pair % C : 0;
+  constexpr int RW = 4 * P - 1;  // staged rows: al (P), Sp (P), end factors (2P-1)
+  const int SZ = (RW + 2) * C;   // and the two anchor rows
+  double* buf0 = tsm;
+  double* buf1 = tsm + SZ;
+  auto nq_of = [&](int b) -> int {
+    const int Lb = bseq_len(a.lengths, b, T);
+    if (Lb <= 0 || a.grad_output[b] == 0.0f) return 0;
+    const int n = min((Lb - 1) / P + 1, Lb / P - lam + 1);
+    return n > 0 ? n : 0;
+  };
+  auto first_from = [&](int b0, int& b, int& q) -> bool {
+    for (b = b0; b < a.B; b += a.nslice)
+      if (nq_of(b) > 0) {
+        q = 0;
+        return true;
+      }
+    return false;
+  };
+  auto stage = [&](int b, int q, double* d) {
+    const int Lb = bseq_len(a.lengths, b, T);
+    const size_t row0 = (size_t)b * (T + 1);
+    for (int i = tid; i < RW * C; i += nt) {
+      const int x = i / C, c = i % C;
+      const double* src = a.al;
+      bool ok = false;
+      if (x < P) {
+        const int s = q * P + x;
+        ok = s < Lb;
+        if (ok) src = a.al + (row0 + s) * C + c;
+      } else if (x < 2 * P) {
+        const int s = q * P + x - P;
+        ok = s < Lb;
+        if (ok) src = a.st + (row0 + s) * C + c;
+      } else {
+        const int xx = x - 2 * P, e = (q + lam) * P + xx;
+        ok = e <= Lb;
+        if (ok) src = (xx < P ? a.et : a.ep1) + (row0 + e) * C + c;
+      }
+      cp_async8z(d + i, src, ok);
+    }
+    for (int i = tid; i < 2 * C; i += nt) {
+      const int qq = i < C ? q : q + lam;
+      cp_async8z(d + RW * C + i, a.anc + ((size_t)b * nb + qq) * C + (i % C), true);
+    }
+  };
+  double acc[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) acc[i] = 0.0;
+  int b = 0, q = 0, n = 0;
+  bool have = first_from(slice, b, q);
+  if (have) stage(b, q, buf0);
+  cp_async_commit_g();
+  while (have) {
+    int bn = b, qn = q;
+    bool more;
+    if (q + 1 < nq_of(b)) {
+      qn = q + 1;
+      more = true;
+    } else {
+      more = first_from(b + a.nslice, bn, qn);
+    }
+    if (more) stage(bn, qn, (n & 1) ? buf0 : buf1);
+    cp_async_commit_g();
+    cp_async_wait_1();
+    __syncthreads();
+    const double* d = (n & 1) ? buf1 : buf0;
+    if (act) {
+      const double z = (double)a.grad_output[b] *
+                       exp(fmin(d[RW * C + l] - d[(RW + 1) * C + l], 700.0));
+      double w[2 * P - 1];
+#pragma unroll
+      for (int x = 0; x < 2 * P - 1; ++x) w[x] = d[(2 * P + x) * C + l];
+#pragma unroll
+      for (int r = 0; r < P; ++r) {
+        const double u = z * d[r * C + m] * d[(P + r) * C + l];
+#pragma unroll
+        for (int i = 0; i < P; ++i) acc[i] = fma(u, w[r + i], acc[i]);
+      }
+    }
+    __syncthreads();  // this buffer is staged again two items later
+    b = bn;
+    q = qn;
+    have = more;
+    ++n;
+  }
+  if (!act) return;
+  const int ncol = kcap * C;
+  double* out = a.part_tr + (size_t)slice * C * ncol + (size_t)m * ncol;
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const int k = lam * P + i;
+    if (k >= 1 && k <= kcap) out[(size_t)(k - 1) * C + l] = acc[i];
+  }
+}
+
+// start marginals and the position gradients; thread (sequence, source block,
+// label) for every row 0 .. T
+template <int P>
+__global__ void __launch_bounds__(kBT, 1) kblk_pos_kernel(const KccArgs a, int nch) {
+  const int C = a.C, T = a.T, kcap = a.kcap, nb = T / P + 1;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int l = (int)(gid % C);
+  const long long rest = gid / C;
+  const int q = (int)(rest % nb), b = (int)(rest / nb);
+  if (b >= a.B) return;
+  const int Lb = bseq_len(a.lengths, b, T);
+  const size_t row0 = (size_t)b * (T + 1);
+  const double* anc = a.anc + (size_t)b * nb * C;
+  const size_t CC = (size_t)C * C;
+  const int s0 = q * P;
+  double out[P];
+#pragma unroll
+  for (int r = 0; r < P; ++r) out[r] = 0.0;
+  if (s0 < Lb) {
+    for (int lam = 0; lam < nch && (q + lam) * P <= Lb; ++lam) {
+      double w[2 * P - 1];
+      end_window<P>(a, anc, row0, Lb, nb, q, lam, l, w);
+      for (int m = 0; m < C; ++m) {
+        double xk[P], V[P];
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          const int k = lam * P + i;
+          xk[i] = (k >= 1 && k <= kcap) ? __ldg(a.pr.xf + (size_t)k * CC + (size_t)m * C + l) : 0.0;
+          V[i] = 0.0;
+        }
+#pragma unroll
+        for (int i = 0; i < P; ++i)
+#pragma unroll
+          for (int r = 0; r < P; ++r) V[r] = fma(xk[i], w[r + i], V[r]);
+#pragma unroll
+        for (int r = 0; r < P; ++r) {
+          const int s = s0 + r;
+          const double av = s < Lb ? a.al[(row0 + s) * C + m] : 0.0;
+          out[r] = fma(av, V[r], out[r]);
+        }
+      }
+    }
+  }
+  const double g = (double)a.grad_output[b];
+  const double lz = a.logz[b];
+#pragma unroll
+  for (int r = 0; r < P; ++r) {
+    const int s = s0 + r;
+    if (s > T) break;
+    const size_t i = (row0 + s) * C + l;
+    double pend = 0.0;
+    if (s >= 1 && s <= Lb) {
+      const double v = a.alpha[i] + a.beta[i] - lz;
+      pend = v > -INFINITY ? exp(v) : 0.0;
+    }
+    const double pst = s < Lb ? a.st[i] * out[r] : 0.0;
+    a.grad_cum[i] = (float)(g * (pend - pst));
+    if (a.grad_ps && s < T) a.grad_ps[((size_t)b * T + s) * C + l] = (float)(g * pst);
+    if (a.grad_pe && s >= 1) a.grad_pe[((size_t)b * T + s - 1) * C + l] = (float)(g * pend);
+  }
+}
+
 }  // namespace
 
 bool kblk_supported(int C, int K) {
@@ -487,6 +763,53 @@ cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s) {
   if (a.C <= 24) return go(kblk_chain_kernel<kBP, 24>);
   if (a.C <= kRegC) return go(kblk_chain_kernel<kBP, kRegC>);
   return go(kblk_chain_kernel<kBP, 0>);
+}
+
+size_t kblk_anchor_rows(int T) { return (size_t)(T / kBP + 1); }
+
+// label pairs per CTA of the transition-gradient kernel: npg CTAs of tpb threads
+static void tr_shape(int C, int& npg, int& tpb) {
+  const int npair = C * C;
+  npg = (npair + kBT - 1) / kBT;
+  tpb = ((npair + npg - 1) / npg + 31) / 32 * 32;
+}
+
+int kblk_tr_slices(int B, int K, int C) {
+  int npg, tpb;
+  tr_shape(C, npg, tpb);
+  const long long per = (long long)npg * ((K + kBP - 1) / kBP);  // CTAs per slice
+  const long long want = 148LL * 2 * 4;                          // four waves of two CTAs per SM
+  long long ns = (want + per - 1) / per;
+  if (ns > B) ns = B;
+  return ns < 1 ? 1 : (int)ns;
+}
+
+cudaError_t launch_kblk_grads(const KccArgs& a, cudaStream_t s) {
+  const int nb = a.T / kBP + 1;
+  auto grid = [](size_t n, int t) {
+    size_t g = (n + t - 1) / t;
+    if (g > 148 * 16) g = 148 * 16;
+    return (int)(g < 1 ? 1 : g);
+  };
+  kblk_anchor_kernel<<<grid((size_t)a.B * nb * a.C, 256), 256, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  kblk_factor_kernel<<<grid((size_t)a.B * (a.T + 1) * a.C, 256), 256, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int nch = (a.K + kBP - 1) / kBP;  // lag chunks covering k = 0 .. K-1
+  const long long npos = (long long)a.B * nb * a.C;
+  kblk_pos_kernel<kBP><<<(unsigned)((npos + kBT - 1) / kBT), kBT, 0, s>>>(a, nch);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  int npg, tpb;
+  tr_shape(a.C, npg, tpb);
+  const size_t tbytes = (size_t)2 * (4 * kBP - 1 + 2) * a.C * 8;
+  e = cudaFuncSetAttribute(kblk_tr_kernel<kBP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)tbytes);
+  if (e != cudaSuccess) return e;
+  kblk_tr_kernel<kBP><<<npg * nch * a.nslice, tpb, tbytes, s>>>(a, nch, npg);
+  return cudaGetLastError();
 }
 
 }  // namespace semicrf

@@ -747,7 +747,8 @@ __global__ void kcc_reduce_kernel(const KccArgs a, float* grad_tr, float* grad_d
       if (k >= 1 && k <= kcap) {
         const size_t j = (size_t)q * ncol + (size_t)(k - 1) * C + c;
         for (int sl = 0; sl < a.nslice; ++sl) v += a.part_tr[(size_t)sl * C * ncol + j];
-        v *= a.pr.ef[((size_t)k * C + q) * C + c];
+        // the blocked kernels' partial sums carry the weights xf, the others ef
+        v *= (a.al ? a.pr.xf : a.pr.ef)[((size_t)k * C + q) * C + c];
       }
       grad_tr[((size_t)k * C + q) * C + c] = (float)v;
       dsum += v;
@@ -837,6 +838,12 @@ cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, c
   kcc_terms_kernel<<<grid_for(n, 256), 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (a.al) {  // log semiring, blocked kernels (kblk.cu)
+    e = launch_kblk_grads(a, s);
+    if (e != cudaSuccess) return e;
+    kcc_reduce_kernel<<<grid_for((size_t)a.K * a.C, 128), 128, 0, s>>>(a, grad_tr, grad_db);
+    return cudaGetLastError();
+  }
   if (a.semiring == SEMICRF_MAX) {
     kcc_pend_max_kernel<<<grid_for(n, 128), 128, 0, s>>>(a);
     e = cudaGetLastError();

@@ -326,6 +326,12 @@ struct KccArgs {
   double* pend;     // max semiring: end marginals (B, T+1, C)
   double* part_tr;  // (nslice, C, kcap*C) partial sums of the transition marginals
   int nslice;
+  // log semiring with the blocked kernels (kblk.cu): source factors al (B, T+1, C)
+  // and per-block anchors anc (B, T/16+1, C); st / et then hold the linear start
+  // and end factors
+  double* al;
+  double* anc;
+  double* ep1;  // end factors relative to the previous block's anchor
 };
 bool kcc_supported(int C, int K);
 size_t kcc_prep_doubles(int K, int C, int semiring);
@@ -340,6 +346,9 @@ bool kblk_supported(int C, int K);
 cudaError_t launch_kblk_prep(const float* tr, const float* db, int K, int C, const KccPrep& pr,
                              cudaStream_t s);
 cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s);
+int kblk_tr_slices(int B, int K, int C);
+size_t kblk_anchor_rows(int T);  // anchors per sequence and label
+cudaError_t launch_kblk_grads(const KccArgs& a, cudaStream_t s);
 
 // escan.cu -- the edge-tensor scan
 bool escan_supported(int K, int C);
