@@ -50,6 +50,8 @@ def parse():
     # kernel; the benchmark line is only the configuration-2 number at the defaults
     # only the configuration-5 Viterbi sub-benchmark (e.g. for a profiler)
     ap.add_argument("--viterbi-only", action="store_true")
+    # only the (K, C, C)-transition fwd+bwd sub-benchmark, at --batch / --seq-len
+    ap.add_argument("--kcc-only", action="store_true")
     ap.add_argument("--batch", type=int, default=B)
     ap.add_argument("--seq-len", type=int, default=T)
     return ap.parse_args()
@@ -214,6 +216,14 @@ def main():
         if rank == 0:
             flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
             print(json.dumps(bench_viterbi(dev, flush)), flush=True)
+        return
+    if args.kcc_only:
+        if rank == 0:
+            flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+            print(json.dumps(bench_fwd_bwd(
+                dev, flush, "cfg2", B, T, K, C,
+                f"cfg2 shape with (K, C, C) transitions: B={B} T={T} K={K} C={C}", kcc=True)),
+                flush=True)
         return
     if world > 1:
         import datetime

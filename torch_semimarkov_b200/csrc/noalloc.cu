@@ -15,8 +15,9 @@
 //    transition and duration tables, about 16*C*C + 8*(K+16)*C bytes in the
 //    log semiring).  It is kNoallocScratchBytes (2 MiB) large.  Every shape
 //    with (C, C) transitions fits (the largest, at C=256, need about 1.3 MiB);
-//    (K, C, C) transitions need per-duration factor tables, 16*K*C*C + 24*K*C
-//    bytes, so only the smaller ones fit.  A problem whose forward workspace
+//    (K, C, C) transitions need per-duration factor tables, 32*K*C*C + 24*K*C
+//    bytes (plus 8*C in the log semiring), so only those up to about
+//    K*C*C = 65k fit.  A problem whose forward workspace
 //    (semicrf_forward_workspace_size) exceeds 2 MiB is rejected with
 //    SEMICRF_ERR_WORKSPACE before any CUDA call.
 //  - Nothing in the scratch has to start at zero: every byte the scan reads
