@@ -236,11 +236,17 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
         const int U = C * nq;
         const int u0 = (int)((long long)sig * U / G), u1 = (int)((long long)(sig + 1) * U / G);
         double d[2 * P - 1], nx[P];
+        // unit u = m * nq + (q - bmin), advanced without divisions
+        int m = u0 / nq, qi = u0 % nq;
         for (int u = u0; u < u1; ++u) {
-          const int m = u / nq, q = bmin + u % nq;
+          if (u > u0 && ++qi == nq) {
+            qi = 0;
+            ++m;
+          }
+          const int q = bmin + qi, qs = q % NBR;
           const int D = (tau - q) * P;
           const double* xc = X + (size_t)m * C + ell;
-          if (u > u0 && u % nq != 0) {  // same label as the previous unit, next source block
+          if (u > u0 && qi != 0) {  // same label as the previous unit, next source block
 #pragma unroll
             for (int i = 2 * P - 2; i >= P; --i) d[i] = d[i - P];
 #pragma unroll
@@ -253,17 +259,17 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
             }
           }
           // the next unit's new weights, in flight during this unit's tile
-          if (u + 1 < u1 && (u + 1) % nq != 0) {
+          if (u + 1 < u1 && qi + 1 < nq) {
 #pragma unroll
             for (int i = 0; i < P; ++i) {
               const int k = D - 2 * P + 1 + i;
               nx[i] = (k >= 1 && k <= kcap) ? __ldcg(xc + (size_t)k * CC) : 0.0;
             }
           }
-          const int base = (q % NBR) * P;
+          const int base = qs * P;
           double z[P];
           if (dir == 0) {
-            const double w = wq[(q % NBR) * C + ell];
+            const double w = wq[qs * C + ell];
 #pragma unroll
             for (int r = 0; r < P; ++r)
               z[r] = ra[(size_t)(base + r) * C + m] * ry[(size_t)(base + r) * C + ell] * w;
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
 #pragma unroll
               for (int j = 0; j < P; ++j) out[j] = fma(d[P - 1 + j - r], z[r], out[j]);
           } else {
-            const double w = wq[(q % NBR) * C + m];
+            const double w = wq[qs * C + m];
 #pragma unroll
             for (int r = 0; r < P; ++r) z[r] = ra[(size_t)(base + r) * C + m] * w;
             double acc[P];
@@ -588,11 +594,14 @@ __global__ void __launch_bounds__(kBT, 2) kblk_tr_kernel(const KccArgs a, int nc
       }
     return false;
   };
+  // this thread's staged elements i = tid + j * nt as (row x, label c), advanced
+  // without divisions
+  const int x0 = tid / C, c0 = tid % C, dx = nt / C, dc = nt % C;
   auto stage = [&](int b, int q, double* d) {
     const int Lb = bseq_len(a.lengths, b, T);
     const size_t row0 = (size_t)b * (T + 1);
+    int x = x0, c = c0;
     for (int i = tid; i < RW * C; i += nt) {
-      const int x = i / C, c = i % C;
       const double* src = a.al;
       bool ok = false;
       if (x < P) {
@@ -609,6 +618,12 @@ __global__ void __launch_bounds__(kBT, 2) kblk_tr_kernel(const KccArgs a, int nc
         if (ok) src = (xx < P ? a.et : a.ep1) + (row0 + e) * C + c;
       }
       cp_async8z(d + i, src, ok);
+      x += dx;
+      c += dc;
+      if (c >= C) {
+        c -= C;
+        ++x;
+      }
     }
     for (int i = tid; i < 2 * C; i += nt) {
       const int qq = i < C ? q : q + lam;
