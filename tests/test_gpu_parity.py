@@ -303,6 +303,11 @@ KCC_CASES = [
     (3, 400, 40, 6, "cfg2", "both", "log"),
     (2, 500, 50, 8, "cfg5", None, "log"),
     (2, 200, 17, 33, "cfg5", "end", "log"),
+    # batches whose forward (two chains per sequence) runs the blocked chain on
+    # clusters of 4, 2 and 1 CTAs per chain (small batches use 8)
+    (12, 120, 30, 6, "cfg2", None, "log"),
+    (20, 80, 20, 4, "default", "both", "log"),
+    (40, 50, 6, 5, "default", None, "log"),
 ]
 
 

@@ -43,9 +43,13 @@
 // The tables written are those of kcc_chain_kernel: log alpha and its row
 // maxima (forward), log beta (backward), log Z and the ring checkpoints.
 
+#include <cooperative_groups.h>
+
 #include "semicrf_internal.cuh"
 
 namespace semicrf {
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -97,6 +101,7 @@ __host__ __device__ inline BlkPlan blk_plan(int C, int K, int P) {
 }
 
 constexpr int kRegC = 32;  // largest C whose near weights are kept in registers
+constexpr int kBMaxQ = 8;  // largest cluster per chain (the portable cluster size)
 
 // Frames.  Block tau has a scalar N and per-label offsets fd[l], taken from
 // the row before the block (its reference row; position 0 or len for the
@@ -112,10 +117,14 @@ constexpr int kRegC = 32;  // largest C whose near weights are kept in registers
 // exp(ct + fd + fk) (exp(rb + ct - fd)), so no log or exp lies between the
 // rows of a block.  The log tables are written per block, after its rows.
 template <int P, int CR>
-__global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
+__global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a, int Q) {
   extern __shared__ __align__(16) double bsm[];
   const int C = a.C, K = a.K, T = a.T, kcap = a.kcap;
-  const int b = blockIdx.x, dir = blockIdx.y, tid = threadIdx.x;
+  // Q CTAs (one cluster when Q > 1) per sequence and direction: they split the
+  // far sums and repeat the rest, so every rank holds the same state; rank 0
+  // writes the outputs
+  const int b = blockIdx.x / Q, rank = blockIdx.x % Q, dir = blockIdx.y, tid = threadIdx.x;
+  const bool out0 = rank == 0;
   const int lane = tid & 31, warp = tid >> 5;
   const int Lb = bseq_len(a.lengths, b, T);
   const BlkPlan pl = blk_plan(C, K, P);
@@ -142,7 +151,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
   const size_t CC = (size_t)C * C;
 
   for (int i = tid; i < C; i += kBT) fk[i] = a.pr.fk[i];
-  if (dir == 0 && a.ref_ckpt) {
+  if (dir == 0 && a.ref_ckpt && out0) {
     float* rc = a.ref_ckpt + (size_t)b * a.nref * K * C;
     for (size_t i = tid; i < (size_t)a.nref * K * C; i += kBT)
       rc[i] = (i < (size_t)C) ? 0.f : kRefNegInf;
@@ -234,7 +243,8 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
       for (int j = 0; j < P; ++j) out[j] = 0.0;
       if (act) {
         const int U = C * nq;
-        const int u0 = (int)((long long)sig * U / G), u1 = (int)((long long)(sig + 1) * U / G);
+        const int QG = Q * G, slot = rank * G + sig;  // this thread's share of the cluster's
+        const int u0 = (int)((long long)slot * U / QG), u1 = (int)((long long)(slot + 1) * U / QG);
         double d[2 * P - 1], nx[P];
         // unit u = m * nq + (q - bmin), advanced without divisions
         int m = u0 / nq, qi = u0 % nq;
@@ -300,9 +310,23 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
         const int j = i / C, l = i % C;
         double s = 0.0;
         for (int g = 0; g < G; ++g) s += part[j * kBT + g * C + l];
-        pend[i] = s * kap[i];
+        if (Q == 1)
+          pend[i] = s * kap[i];
+        else
+          lv[i] = s;  // this rank's share, summed over the ranks in rank order below
       }
-      __syncthreads();
+      if (Q > 1) {
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        for (int i = tid; i < P * C; i += kBT) {
+          double s = 0.0;
+          for (int r = 0; r < Q; ++r) s += cl.map_shared_rank(lv, r)[i];
+          pend[i] = s * kap[i];
+        }
+        cl.sync();  // every rank has read lv before its tables overwrite it
+      } else {
+        __syncthreads();
+      }
     }
 
     // 2. the block's rows in order.  pend holds a row's source factors (a or
@@ -386,6 +410,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
       if (rho > 0)
         v = pv > 0.0 ? (dir == 0 ? N : N + fd[fs * C + l] - ctb[i]) + log(pv) : -INFINITY;
       lv[i] = v;
+      if (!out0) continue;
       if (dir == 0) {
         if (a.alpha) a.alpha[((size_t)b * (T + 1) + t) * C + l] = v;
         if (a.ref_ckpt) {
@@ -406,7 +431,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
       for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       if (lane == 0) {
         const int t = dir == 0 ? s0 + j : Lb - (s0 + j);
-        if (dir == 0 && a.amax) a.amax[(size_t)b * (T + 1) + t] = mx;
+        if (dir == 0 && a.amax && out0) a.amax[(size_t)b * (T + 1) + t] = mx;
         if (j == P - 1) red[32] = mx;
       }
     }
@@ -414,7 +439,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a) {
       for (int l = tid; l < C; l += kBT) vals[l] = lv[last * C + l];
     __syncthreads();
   }
-  if (dir == 0 && tid == 0) {
+  if (dir == 0 && tid == 0 && out0) {
     double lz = (double)kRefNegInf;
     if (Lb > 0) {
       double M = -INFINITY;
@@ -769,7 +794,35 @@ cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
-    kern<<<dim3(a.B, ndir), kBT, bytes, s>>>(a);
+    // a cluster of Q CTAs per chain when the chains alone leave SMs idle and
+    // all the clusters fit at once
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int nchain = a.B * ndir;
+    for (int Q = kBMaxQ; Q >= 2; Q /= 2) {
+      if (nchain * Q > nsm) continue;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(a.B * Q, ndir);
+      cfg.blockDim = dim3(kBT);
+      cfg.dynamicSmemBytes = bytes;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = Q;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int ncl = 0;
+      if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        continue;
+      }
+      if (ncl < nchain) continue;
+      return cudaLaunchKernelEx(&cfg, kern, a, Q);
+    }
+    kern<<<dim3(a.B, ndir), kBT, bytes, s>>>(a, 1);
     return cudaGetLastError();
   };
   // register-held in-block weights for C <= kRegC, sized to the next multiple of 8
