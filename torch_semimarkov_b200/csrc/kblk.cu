@@ -586,7 +586,8 @@ __device__ __forceinline__ void cp_async_wait_1() {
 // part[slice][m][(k-1)*C + l] = sum over the slice's sequences and sources of
 // g_b al[s,m] Sp[s,l] Ep[s+k,l] Z.  A CTA takes one lag chunk lam (k = lam*P + i),
 // one slice and up to blockDim label pairs; its items are the (sequence, source
-// block q) of the slice.  An item's rows -- al and Sp of the block's sources,
+// block q) of the slice (a class of sequences, and a chunk of their source
+// blocks when there are more slices than sequences).  An item's rows -- al and Sp of the block's sources,
 // the end factors of rows (q+lam)*P .. +2P-2 (block q+lam relative to its own
 // anchor, block q+lam+1 relative to block q+lam's) and the two anchors -- are
 // staged in shared memory by cp.async, one item ahead, so the item's factor
@@ -611,12 +612,22 @@ __global__ void __launch_bounds__(kBT, 2) kblk_tr_kernel(const KccArgs a, int nc
     const int n = min((Lb - 1) / P + 1, Lb / P - lam + 1);
     return n > 0 ? n : 0;
   };
+  // slice = (sequence class bs, source-block chunk qc): sequences bs, bs + nbs, ...
+  // and, of each, the qc-th of nqc equal chunks of its source blocks
+  const int nbs = min(a.B, a.nslice), nqc = a.nslice / nbs;
+  const int bs = slice % nbs, qc = slice / nbs;
+  auto q_hi = [&](int b) -> int {
+    const int nq = nq_of(b), ql = (nq + nqc - 1) / nqc;
+    return min(nq, (qc + 1) * ql);
+  };
   auto first_from = [&](int b0, int& b, int& q) -> bool {
-    for (b = b0; b < a.B; b += a.nslice)
-      if (nq_of(b) > 0) {
-        q = 0;
+    for (b = b0; b < a.B; b += nbs) {
+      const int nq = nq_of(b), ql = (nq + nqc - 1) / nqc;
+      if (qc * ql < min(nq, (qc + 1) * ql)) {
+        q = qc * ql;
         return true;
       }
+    }
     return false;
   };
   // this thread's staged elements i = tid + j * nt as (row x, label c), advanced
@@ -659,17 +670,17 @@ __global__ void __launch_bounds__(kBT, 2) kblk_tr_kernel(const KccArgs a, int nc
 #pragma unroll
   for (int i = 0; i < P; ++i) acc[i] = 0.0;
   int b = 0, q = 0, n = 0;
-  bool have = first_from(slice, b, q);
+  bool have = first_from(bs, b, q);
   if (have) stage(b, q, buf0);
   cp_async_commit_g();
   while (have) {
     int bn = b, qn = q;
     bool more;
-    if (q + 1 < nq_of(b)) {
+    if (q + 1 < q_hi(b)) {
       qn = q + 1;
       more = true;
     } else {
-      more = first_from(b + a.nslice, bn, qn);
+      more = first_from(b + nbs, bn, qn);
     }
     if (more) stage(bn, qn, (n & 1) ? buf0 : buf1);
     cp_async_commit_g();
@@ -848,8 +859,10 @@ int kblk_tr_slices(int B, int K, int C) {
   const long long per = (long long)npg * ((K + kBP - 1) / kBP);  // CTAs per slice
   const long long want = 148LL * 2 * 4;                          // four waves of two CTAs per SM
   long long ns = (want + per - 1) / per;
-  if (ns > B) ns = B;
-  return ns < 1 ? 1 : (int)ns;
+  if (ns < 1) ns = 1;
+  // slices cover sequences first, then chunks of each sequence's source blocks
+  const long long nbs = ns < B ? ns : (B > 0 ? B : 1);
+  return (int)(nbs * (ns / nbs));
 }
 
 cudaError_t launch_kblk_grads(const KccArgs& a, cudaStream_t s) {
