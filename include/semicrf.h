@@ -181,8 +181,8 @@ int semicrf_edge_scan_backward(int64_t B, int64_t N, int64_t K, int64_t C, const
  *  - Scratch: a fixed 2 MiB device array inside the library, one per
  *    device; every shape with (C, C) transitions fits (the largest, at
  *    C=256, need about 1.3 MiB).  (K, C, C) transitions need
- *    32*K*C*C + 24*K*C bytes (plus 8*C in the log semiring), so only those
- *    up to about K*C*C = 65k fit.  A problem whose
+ *    32*K*C*C + 24*K*C + 8*C bytes (48*K*C*C + 24*K*C + 8*C for max), so
+ *    only those up to about K*C*C = 65k (43k for max) fit.  A problem whose
  *    semicrf_forward_workspace_size exceeds 2 MiB is rejected with
  *    SEMICRF_ERR_WORKSPACE (before any CUDA call).
  *  - Nothing in the scratch needs to start at zero (each call writes what it

@@ -323,7 +323,7 @@ KccLayout carve_kcc(Carver& cv, const semicrf_problem* p, bool backward) {
   w.st = cv.take<double>(n);
   w.et = cv.take<double>(n);
   w.pend = p->semiring == SEMICRF_MAX ? cv.take<double>(n) : nullptr;
-  const bool blk = p->semiring == SEMICRF_LOG && kblk_supported(C, K);
+  const bool blk = kblk_supported(C, K);  // blocked gradient kernels (both semirings)
   if (blk) {
     w.al = cv.take<double>(n);
     w.ep1 = cv.take<double>(n);

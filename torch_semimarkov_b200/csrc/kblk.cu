@@ -716,6 +716,66 @@ __global__ void __launch_bounds__(kBT, 2) kblk_tr_kernel(const KccArgs a, int nc
   }
 }
 
+// max semiring: the end marginal of every (position, label), summed over its
+// incoming segments, Pend[e,l] = Ep[e,l] sum_{s,m} al[s,m] xf[e-s][m][l] Sp[s,l] Z
+// (the log semiring has it as exp(alpha + beta - logZ)).  Thread (sequence,
+// target block tau, label l): for each source block q within reach and source
+// label m, the P x P Toeplitz tile out[j] += sum_r x[D + j - r][m][l] z[r] from a
+// window of 2P-1 weights, as in the chain's far sums.
+template <int P>
+__global__ void __launch_bounds__(kBT, 1) kblk_pend_kernel(const KccArgs a) {
+  const int C = a.C, T = a.T, kcap = a.kcap, nb = T / P + 1;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int l = (int)(gid % C);
+  const long long rest = gid / C;
+  const int tau = (int)(rest % nb), b = (int)(rest / nb);
+  if (b >= a.B) return;
+  const int Lb = bseq_len(a.lengths, b, T);
+  const size_t row0 = (size_t)b * (T + 1);
+  const double* anc = a.anc + (size_t)b * nb * C;
+  const size_t CC = (size_t)C * C;
+  const int e0 = tau * P;
+  double out[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) out[j] = 0.0;
+  if (e0 <= Lb) {
+    const double At = anc[(size_t)tau * C + l];
+    const int qlo = max(0, floor_div(e0 - kcap, P));
+    for (int q = qlo; q <= tau; ++q) {
+      const int D = (tau - q) * P;
+      const double Z = exp(fmin(anc[(size_t)q * C + l] - At, 700.0));
+      double zs[P];
+#pragma unroll
+      for (int r = 0; r < P; ++r) {
+        const int s = q * P + r;
+        zs[r] = s < Lb ? a.st[(row0 + s) * C + l] * Z : 0.0;
+      }
+      for (int m = 0; m < C; ++m) {
+        double d[2 * P - 1];
+#pragma unroll
+        for (int i = 0; i < 2 * P - 1; ++i) {
+          const int k = D - P + 1 + i;
+          d[i] = (k >= 1 && k <= kcap) ? __ldg(a.pr.xf + (size_t)k * CC + (size_t)m * C + l) : 0.0;
+        }
+#pragma unroll
+        for (int r = 0; r < P; ++r) {
+          const int s = q * P + r;
+          const double z = s < Lb ? a.al[(row0 + s) * C + m] * zs[r] : 0.0;
+#pragma unroll
+          for (int j = 0; j < P; ++j) out[j] = fma(d[P - 1 + j - r], z, out[j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int e = e0 + j;
+    if (e > T) break;
+    const size_t i = (row0 + e) * C + l;
+    a.pend[i] = (e >= 1 && e <= Lb) ? a.et[i] * out[j] : 0.0;
+  }
+}
+
 // start marginals and the position gradients; thread (sequence, source block,
 // label) for every row 0 .. T
 template <int P>
@@ -768,8 +828,12 @@ __global__ void __launch_bounds__(kBT, 1) kblk_pos_kernel(const KccArgs a, int n
     const size_t i = (row0 + s) * C + l;
     double pend = 0.0;
     if (s >= 1 && s <= Lb) {
-      const double v = a.alpha[i] + a.beta[i] - lz;
-      pend = v > -INFINITY ? exp(v) : 0.0;
+      if (a.semiring == SEMICRF_MAX) {
+        pend = a.pend[i];
+      } else {
+        const double v = a.alpha[i] + a.beta[i] - lz;
+        pend = v > -INFINITY ? exp(v) : 0.0;
+      }
     }
     const double pst = s < Lb ? a.st[i] * out[r] : 0.0;
     a.grad_cum[i] = (float)(g * (pend - pst));
@@ -880,6 +944,11 @@ cudaError_t launch_kblk_grads(const KccArgs& a, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const int nch = (a.K + kBP - 1) / kBP;  // lag chunks covering k = 0 .. K-1
   const long long npos = (long long)a.B * nb * a.C;
+  if (a.semiring == SEMICRF_MAX) {
+    kblk_pend_kernel<kBP><<<(unsigned)((npos + kBT - 1) / kBT), kBT, 0, s>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   kblk_pos_kernel<kBP><<<(unsigned)((npos + kBT - 1) / kBT), kBT, 0, s>>>(a, nch);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -772,11 +772,11 @@ bool kcc_supported(int C, int K) {
   return pos_plan(C, K - 1).total * 8 <= kSmemMax;
 }
 
-// log semiring: ef, eb, tf, tb, tdf and the blocked chain's xf, xb, fk;
-// max semiring: ef, eb, tf, tb, tdf, rf, rb
+// both semirings: ef, eb, tf, tb, tdf and the blocked kernels' xf, xb, fk;
+// the max semiring adds rf, rb
 size_t kcc_prep_doubles(int K, int C, int semiring) {
   const size_t kcc = (size_t)K * C * C;
-  return 4 * kcc + 3 * (size_t)K * C + (semiring == SEMICRF_MAX ? 0 : (size_t)C);
+  return (semiring == SEMICRF_MAX ? 6 : 4) * kcc + 3 * (size_t)K * C + (size_t)C;
 }
 
 KccPrep kcc_prep_carve(double* base, int K, int C, int semiring) {
@@ -788,13 +788,12 @@ KccPrep kcc_prep_carve(double* base, int K, int C, int semiring) {
   p.tf = p.eb + kcc;
   p.tb = p.tf + kc;
   p.tdf = p.tb + kc;
+  p.xf = p.tdf + kc;
+  p.xb = p.xf + kcc;
+  p.fk = p.xb + kcc;
   if (semiring == SEMICRF_MAX) {
-    p.rf = p.tdf + kc;
+    p.rf = p.fk + C;
     p.rb = p.rf + kcc;
-  } else {
-    p.xf = p.tdf + kc;
-    p.xb = p.xf + kcc;
-    p.fk = p.xb + kcc;
   }
   return p;
 }
@@ -838,7 +837,7 @@ cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, c
   kcc_terms_kernel<<<grid_for(n, 256), 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (a.al) {  // log semiring, blocked kernels (kblk.cu)
+  if (a.al) {  // blocked kernels (kblk.cu), both semirings
     e = launch_kblk_grads(a, s);
     if (e != cudaSuccess) return e;
     kcc_reduce_kernel<<<grid_for((size_t)a.K * a.C, 128), 128, 0, s>>>(a, grad_tr, grad_db);

@@ -16,8 +16,8 @@
 //    log semiring).  It is kNoallocScratchBytes (2 MiB) large.  Every shape
 //    with (C, C) transitions fits (the largest, at C=256, need about 1.3 MiB);
 //    (K, C, C) transitions need per-duration factor tables, 32*K*C*C + 24*K*C
-//    bytes (plus 8*C in the log semiring), so only those up to about
-//    K*C*C = 65k fit.  A problem whose forward workspace
+//    + 8*C bytes (48*K*C*C + 24*K*C + 8*C for max), so only those up to about
+//    K*C*C = 65k (43k for max) fit.  A problem whose forward workspace
 //    (semicrf_forward_workspace_size) exceeds 2 MiB is rejected with
 //    SEMICRF_ERR_WORKSPACE before any CUDA call.
 //  - Nothing in the scratch has to start at zero: every byte the scan reads
