@@ -483,6 +483,253 @@ __global__ void kblk_weights_kernel(const float* __restrict__ tr, const float* _
 }
 
 // ---------------------------------------------------------------------------
+// Max semiring chain: the same blocks and cluster split, in the log domain
+// with (max, +), so no frames are needed:
+//   alpha[t,l] = ct[t,l] + max_{s,m} (alpha[s,m] + tr[t-s][m][l] + db[t-s,l] + dt[s,l])
+//   beta[s,l]  = max_{u,m} (tr[u-s][l][m] + db[u-s,m] + dt[s,m] + ct[u,m] + beta[u,m])
+// pend[j][l] is ct plus the running maximum of row j; the ring holds alpha
+// (forward, with dt beside it) or G = ct + beta (backward) of the sources.
+template <int P, int CR>
+__global__ void __launch_bounds__(kBT, 1) kblkm_chain_kernel(const KccArgs a, int Q) {
+  extern __shared__ __align__(16) double bsm[];
+  const int C = a.C, K = a.K, T = a.T, kcap = a.kcap;
+  const int b = blockIdx.x / Q, rank = blockIdx.x % Q, dir = blockIdx.y, tid = threadIdx.x;
+  const bool out0 = rank == 0;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int Lb = bseq_len(a.lengths, b, T);
+  const BlkPlan pl = blk_plan(C, K, P);
+  const int NBR = pl.nbr;
+  double* ra = bsm + pl.ra;
+  double* ry = bsm + pl.ry;
+  double* pend = bsm + pl.pend;
+  double* part = bsm + pl.part;
+  double* ctb = bsm + pl.ctb;
+  double* dtb = bsm + pl.dtb;
+  double* lv = bsm + pl.lv;
+  double* vals = bsm + pl.vals;
+  const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
+  const float* ps_b = a.ps ? a.ps + (size_t)b * T * C : nullptr;
+  const float* pe_b = a.pe ? a.pe + (size_t)b * T * C : nullptr;
+  // log weights with the new segment's duration bias: forward rf[k][m][l] =
+  // tr[k][m][l] + db[k,l], backward rb[k][m][l] = tr[k][l][m] + db[k,m]
+  const double* Wr = dir == 0 ? a.pr.rf : a.pr.rb;
+  const size_t CC = (size_t)C * C;
+  auto wgt = [&](int k, int m, int l) -> double {
+    return (k >= 1 && k <= kcap) ? Wr[(size_t)k * CC + (size_t)m * C + l] : -INFINITY;
+  };
+  if (dir == 0 && a.ref_ckpt && out0) {
+    float* rc = a.ref_ckpt + (size_t)b * a.nref * K * C;
+    for (size_t i = tid; i < (size_t)a.nref * K * C; i += kBT)
+      rc[i] = (i < (size_t)C) ? 0.f : kRefNegInf;
+  }
+  __syncthreads();
+
+  const int G = kBT / C, ell = tid % C, sig = tid / C;
+  const bool act = sig < G;
+  const int nblk = Lb / P + 1;
+  const int nnear = (P - 1) * C;
+  for (int tau = 0; tau < nblk; ++tau) {
+    const int s0 = tau * P, fs = tau % NBR;
+    for (int i = tid; i < P * C; i += kBT) {
+      const int j = i / C, l = i % C, rho = s0 + j;
+      double cv = 0.0, dv = 0.0;
+      if (rho <= Lb) {
+        const int t = dir == 0 ? rho : Lb - rho;
+        const double cu = cum_b[(size_t)t * C + l];
+        cv = cu + ((pe_b && t >= 1) ? (double)pe_b[(size_t)(t - 1) * C + l] : 0.0);
+        dv = ((ps_b && t < T) ? (double)ps_b[(size_t)t * C + l] : 0.0) - cu;
+      }
+      ctb[i] = cv;
+      dtb[i] = dv;
+      // row 0 holds its source values already: alpha = 0, or G = ct + 0
+      pend[i] = rho == 0 ? (dir == 0 ? 0.0 : cv) : -INFINITY;
+      if (dir == 0) ry[(size_t)(fs * P + j) * C + l] = dv;
+    }
+    const int bmin = max(0, floor_div(s0 - kcap, P));
+    const int nq = tau - bmin;
+    __syncthreads();
+
+    // 1. far sums
+    if (nq > 0) {
+      double out[P];
+#pragma unroll
+      for (int j = 0; j < P; ++j) out[j] = -INFINITY;
+      if (act) {
+        const int U = C * nq;
+        const int QG = Q * G, slot = rank * G + sig;
+        const int u0 = (int)((long long)slot * U / QG), u1 = (int)((long long)(slot + 1) * U / QG);
+        double d[2 * P - 1], nx[P];
+        int m = u0 / nq, qi = u0 % nq;
+        for (int u = u0; u < u1; ++u) {
+          if (u > u0 && ++qi == nq) {
+            qi = 0;
+            ++m;
+          }
+          const int q = bmin + qi, qs = q % NBR;
+          const int D = (tau - q) * P;
+          if (u > u0 && qi != 0) {
+#pragma unroll
+            for (int i = 2 * P - 2; i >= P; --i) d[i] = d[i - P];
+#pragma unroll
+            for (int i = 0; i < P; ++i) d[i] = nx[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 2 * P - 1; ++i) d[i] = wgt(D - P + 1 + i, m, ell);
+          }
+          if (u + 1 < u1 && qi + 1 < nq) {
+#pragma unroll
+            for (int i = 0; i < P; ++i) nx[i] = wgt(D - 2 * P + 1 + i, m, ell);
+          }
+          const int base = qs * P;
+          if (dir == 0) {
+#pragma unroll
+            for (int r = 0; r < P; ++r) {
+              const double z = ra[(size_t)(base + r) * C + m] + ry[(size_t)(base + r) * C + ell];
+#pragma unroll
+              for (int j = 0; j < P; ++j) out[j] = fmax(out[j], d[P - 1 + j - r] + z);
+            }
+          } else {
+            double acc[P];
+#pragma unroll
+            for (int j = 0; j < P; ++j) acc[j] = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < P; ++r) {
+              const double z = ra[(size_t)(base + r) * C + m];
+#pragma unroll
+              for (int j = 0; j < P; ++j) acc[j] = fmax(acc[j], d[P - 1 + j - r] + z);
+            }
+#pragma unroll
+            for (int j = 0; j < P; ++j) out[j] = fmax(out[j], acc[j] + dtb[j * C + m]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < P; ++j) part[j * kBT + tid] = out[j];
+      __syncthreads();
+      for (int i = tid; i < P * C; i += kBT) {
+        const int j = i / C, l = i % C;
+        double v = -INFINITY;
+        for (int g = 0; g < G; ++g) v = fmax(v, part[j * kBT + g * C + l]);
+        if (Q == 1)
+          pend[i] = v + ctb[i];
+        else
+          lv[i] = v;
+      }
+      if (Q > 1) {
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        for (int i = tid; i < P * C; i += kBT) {
+          double v = -INFINITY;
+          for (int r = 0; r < Q; ++r) v = fmax(v, cl.map_shared_rank(lv, r)[i]);
+          pend[i] = v + ctb[i];
+        }
+        cl.sync();
+      } else {
+        __syncthreads();
+      }
+    }
+
+    // 2. the block's rows in order.  pend holds each row's running maximum
+    // plus its ct, which is the row's source value once the row is complete
+    // (alpha, or G = ct + beta); row j then adds its contributions to rows j + k
+    const int last = min(P - 1, Lb - s0);
+    auto src = [&](int j, int m) -> double { return pend[j * C + m]; };
+    if constexpr (CR > 0) {
+      constexpr int NREP = ((P - 1) * CR + kBT - 1) / kBT;
+      double w[NREP][CR];
+      int kr[NREP], lr[NREP];
+      bool vr[NREP];
+#pragma unroll
+      for (int rep = 0; rep < NREP; ++rep) {
+        const int i = tid + rep * kBT;
+        kr[rep] = 1 + i / C;
+        lr[rep] = i % C;
+        vr[rep] = i < nnear && kr[rep] <= kcap;
+#pragma unroll
+        for (int m = 0; m < CR; ++m)
+          w[rep][m] = (vr[rep] && m < C) ? wgt(kr[rep], m, lr[rep]) : -INFINITY;
+      }
+      for (int j = 0; j <= last; ++j) {
+#pragma unroll
+        for (int rep = 0; rep < NREP; ++rep) {
+          const int jj = j + kr[rep], l = lr[rep];
+          if (vr[rep] && jj <= last) {
+            double m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int m = 0; m < CR; ++m)
+              if (m < C) {
+                const double am = src(j, m) + (dir == 1 ? dtb[jj * C + m] : 0.0);
+                m4[m & 3] = fmax(m4[m & 3], am + w[rep][m]);
+              }
+            const double v = fmax(fmax(m4[0], m4[1]), fmax(m4[2], m4[3])) +
+                             (dir == 0 ? dtb[j * C + l] : 0.0) + ctb[jj * C + l];
+            pend[jj * C + l] = fmax(pend[jj * C + l], v);
+          }
+        }
+        __syncthreads();
+      }
+    } else {
+      for (int j = 0; j <= last; ++j) {
+        for (int i = tid; i < nnear; i += kBT) {
+          const int k = 1 + i / C, l = i % C, jj = j + k;
+          if (k > kcap || jj > last) continue;
+          double v = -INFINITY;
+          for (int m = 0; m < C; ++m)
+            v = fmax(v, src(j, m) + (dir == 1 ? dtb[jj * C + m] : 0.0) + wgt(k, m, l));
+          v += (dir == 0 ? dtb[j * C + l] : 0.0) + ctb[jj * C + l];
+          pend[jj * C + l] = fmax(pend[jj * C + l], v);
+        }
+        __syncthreads();
+      }
+    }
+
+    // 3. the block's tables, ring rows and row maxima
+    const int nrow = last + 1;
+    for (int i = tid; i < nrow * C; i += kBT) {
+      const int j = i / C, l = i % C, rho = s0 + j;
+      const int t = dir == 0 ? rho : Lb - rho;
+      ra[(size_t)(fs * P + j) * C + l] = pend[i];
+      const double v = rho == 0 ? 0.0 : (dir == 0 ? pend[i] : pend[i] - ctb[i]);
+      lv[i] = v;
+      if (!out0) continue;
+      if (dir == 0) {
+        if (a.alpha) a.alpha[((size_t)b * (T + 1) + t) * C + l] = v;
+        if (a.ref_ckpt) {
+          const int S = a.sref;
+          const int ic = (t + S - 1) / S;
+          if (ic < a.nref && (long long)ic * S <= Lb && (long long)ic * S - t < K)
+            a.ref_ckpt[(((size_t)b * a.nref + ic) * K + (t % K)) * C + l] =
+                v > -INFINITY ? (float)v : kRefNegInf;
+        }
+      } else if (a.beta) {
+        a.beta[((size_t)b * (T + 1) + t) * C + l] = v;
+      }
+    }
+    __syncthreads();
+    for (int j = warp; j < nrow; j += kBT / 32) {
+      double mx = -INFINITY;
+      for (int l = lane; l < C; l += 32) mx = fmax(mx, lv[j * C + l]);
+      for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0 && dir == 0 && a.amax && out0)
+        a.amax[(size_t)b * (T + 1) + (s0 + j)] = mx;
+    }
+    if (s0 + last == Lb)
+      for (int l = tid; l < C; l += kBT) vals[l] = lv[last * C + l];
+    __syncthreads();
+  }
+  if (dir == 0 && tid == 0 && out0) {
+    double lz = (double)kRefNegInf;
+    if (Lb > 0) {
+      double M = -INFINITY;
+      for (int q = 0; q < C; ++q) M = fmax(M, vals[q]);
+      if (M > -INFINITY) lz = M;
+    }
+    if (a.logz) a.logz[b] = lz;
+    if (a.partition) a.partition[b] = (float)lz;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Gradients (log semiring).  The segment marginal
 //   P(s -> e, m -> l) = exp(alpha[s,m] + tr[e-s][m][l] + db[e-s,l] + dt[s,l] + ct[e,l]
 //                           + beta[e,l] - logZ)   (pytorch_reference.py:458-499)
@@ -901,6 +1148,13 @@ cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s) {
     return cudaGetLastError();
   };
   // register-held in-block weights for C <= kRegC, sized to the next multiple of 8
+  if (a.semiring == SEMICRF_MAX) {
+    if (a.C <= 8) return go(kblkm_chain_kernel<kBP, 8>);
+    if (a.C <= 16) return go(kblkm_chain_kernel<kBP, 16>);
+    if (a.C <= 24) return go(kblkm_chain_kernel<kBP, 24>);
+    if (a.C <= kRegC) return go(kblkm_chain_kernel<kBP, kRegC>);
+    return go(kblkm_chain_kernel<kBP, 0>);
+  }
   if (a.C <= 8) return go(kblk_chain_kernel<kBP, 8>);
   if (a.C <= 16) return go(kblk_chain_kernel<kBP, 16>);
   if (a.C <= 24) return go(kblk_chain_kernel<kBP, 24>);

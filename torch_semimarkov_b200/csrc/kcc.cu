@@ -72,9 +72,9 @@ __global__ void kcc_prep_kernel(const float* __restrict__ tr, const float* __res
       const size_t j = ((size_t)k * C + q) * C + c;
       pr.ef[j] = exp((double)m[q * C + c] - mf);
       pr.eb[j] = exp((double)m[c * C + q] - mb);
-      if (pr.rf) {
-        pr.rf[j] = (double)m[q * C + c];
-        pr.rb[j] = (double)m[c * C + q];
+      if (pr.rf) {  // max semiring: the weights with the duration bias of the new segment
+        pr.rf[j] = (double)m[q * C + c] + (double)db[(size_t)k * C + c];
+        pr.rb[j] = (double)m[c * C + q] + (double)db[(size_t)k * C + q];
       }
     }
   }
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
                 xv[u] = so + (double)t1f[k * C + c] + (double)dbf[k * C + c];
               } else {
                 const double mp = vmax(src, e);
-                if (mp > -INFINITY) m = fmax(m, mp + (double)dbf[k * C + c] + so);
+                if (mp > -INFINITY) m = fmax(m, mp + so);  // rf holds tr + db
               }
             }
             if (SEMI == 0) add_batch(m, S, xv, av);
@@ -432,7 +432,9 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
         // the source rows x[k][q] of this chunk of durations, all threads
         for (int i = tid; i < nkc * C; i += kKT) {
           const int kk = i / C, q = i % C, k = k0 + kk;
-          xs[i] = ring[(size_t)((t + k) % R) * C + q] + (double)dbf[k * C + q] + dt[q];
+          // the max semiring's rb holds tr + db already
+          xs[i] = ring[(size_t)((t + k) % R) * C + q] + (SEMI == 0 ? (double)dbf[k * C + q] : 0.0) +
+                  dt[q];
         }
         __syncthreads();
         if (SEMI == 0) {
@@ -818,8 +820,8 @@ cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, cons
 
 cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s) {
   if (a.B <= 0) return cudaSuccess;
-  if (a.semiring == SEMICRF_LOG && a.pr.xf && kblk_supported(a.C, a.K))
-    return launch_kblk_chains(a, ndir, s);
+  const bool have = a.semiring == SEMICRF_MAX ? (a.pr.rf != nullptr) : (a.pr.xf != nullptr);
+  if (have && kblk_supported(a.C, a.K)) return launch_kblk_chains(a, ndir, s);
   const size_t bytes = chain_plan(a.C, a.K).total * 8;
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e =

@@ -291,8 +291,8 @@ struct KccPrep {
   double* tf;   // (K, C) max over c' of tr[k][c',c]
   double* tb;   // (K, C) max over c2 of tr[k][c,c2]
   double* tdf;  // (K, C) tf + db
-  double* rf;   // max semiring: (K, C, C) [k][c'][c] = tr[k][c',c]
-  double* rb;   // max semiring: (K, C, C) [k][c2][c] = tr[k][c,c2]
+  double* rf;   // max semiring: (K, C, C) [k][c'][c] = tr[k][c',c] + db[k,c]
+  double* rb;   // max semiring: (K, C, C) [k][c2][c] = tr[k][c,c2] + db[k,c2]
   // log semiring, blocked chain (kblk.cu): fk[c] = max_{k>=1,c'} tr[k][c',c] + db[k,c],
   // xf[k][m][l] = exp(tr[k][m][l] + db[k,l] - fk[l]), xb[k][m][l] = exp(tr[k][l][m] + db[k,m] - fk[m])
   double* xf;
