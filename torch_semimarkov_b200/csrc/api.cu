@@ -176,6 +176,7 @@ struct LBwdLayout {
   double *a_tab, *A_tab, *n_tab;  // SEMICRF_RECOMPUTE: alpha tables
   double *b_tab, *B_tab, *m_tab;  // SEMICRF_RECOMPUTE: beta tables
   double *la, *lb, *maX, *mbY, *part_tr, *part_db;
+  int* dbflag;
   LMargPlan mp;
 };
 
@@ -199,6 +200,7 @@ LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
   w.mbY = cv.take<double>((size_t)p->batch * w.mp.nblk * p->C);
   w.part_tr = cv.take<double>((size_t)p->batch * w.mp.nchunk * p->C * p->C);
   w.part_db = cv.take<double>((size_t)p->batch * w.mp.nsplit * kcap_of(p->K) * p->C);
+  w.dbflag = cv.take<int>((size_t)p->batch);
   return w;
 }
 
@@ -676,6 +678,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     m.part_db = w.part_db;
     m.nsplit = w.mp.nsplit;
     m.cg = w.mp.cg;
+    m.dbflag = w.dbflag;
     return cuda_status(launch_lmarg(m, grad_transition, grad_duration_bias, s));
   }
   Carver cv(workspace);

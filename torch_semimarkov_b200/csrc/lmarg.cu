@@ -29,6 +29,7 @@ namespace {
 
 constexpr int kMT = 256;
 constexpr int kTT = 64;  // positions per block (targets per correlation tile)
+constexpr double kDbFlag = 600.0;  // block-factor exponent beyond which a sequence is redone
 
 __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
   const long long l = lengths[b];
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(kMT) lmarg_blk_kernel(const LMargArgs a) {
     }
     a.maX[i] = ma;
     a.mbY[i] = mb;
+    if (blk == 0 && c == 0) a.dbflag[b] = 0;  // lmarg_db_kernel sets it
   }
 }
 
@@ -228,7 +230,13 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
       double gv = 0.0;
       if (beta < nblk) {
         const double rx = mx_b[(size_t)tau * C + cc], ry = my_b[(size_t)beta * C + cc];
-        if (rx > -INFINITY && ry > -INFINITY) gv = exp(fmin(ry + rx - lz, 700.0));
+        if (rx > -INFINITY && ry > -INFINITY) {
+          const double ex = ry + rx - lz;
+          // beyond this the factored tile loses terms (or clamps): the sequence
+          // is recomputed term by term by lmarg_db_fix_kernel
+          if (ex > kDbFlag) a.dbflag[b] = 1;
+          gv = exp(fmin(ex, 700.0));
+        }
       }
       G[q * CG + cc] = gv;
     }
@@ -305,6 +313,41 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
       }
     }
   }
+}
+
+// ---- duration partials of flagged sequences, term by term ---------------------
+// When the scores inside a 64-position block span more than the float64
+// exponent range (very large emission scores), the block-factored tiles above
+// lose or clamp terms; lmarg_db_kernel flags such a sequence.  Its partials are
+// recomputed here from the saved chain tables in the log domain,
+//   part_db[b][0][k-1][c] = sum_t exp(la[t,c] + lb[t+k,c] - logZ),
+//   la = log xA + xn + ps - cum (t < len),  lb = log yA + yn + cum + pe (t+k <= len),
+// and the other splits are zeroed.  Unflagged sequences return at once.
+__global__ void __launch_bounds__(kMT) lmarg_db_fix_kernel(const LMargArgs a) {
+  const int b = blockIdx.y;
+  if (a.dbflag[b] == 0) return;
+  const int C = a.C, T = a.T, kcap = a.kcap;
+  const int it = blockIdx.x * kMT + threadIdx.x;
+  if (it >= kcap * C) return;
+  const int k = 1 + it / C, c = it % C;
+  const int Lb = seq_len(a.lengths, b, T);
+  const double lz = a.logz[b];
+  const size_t row0 = (size_t)b * (T + 1);
+  const float* cum_b = a.cum + row0 * C;
+  double sum = 0.0;
+  for (int t = 0; t < Lb && t + k <= Lb; ++t) {
+    const int s = t + k;
+    const double x = a.xA[(row0 + t) * C + c], y = a.yA[(row0 + s) * C + c];
+    if (!(x > 0.0) || !(y > 0.0)) continue;
+    const double ps = a.ps ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
+    const double pe = a.pe ? (double)a.pe[((size_t)b * T + s - 1) * C + c] : 0.0;
+    const double la = log(x) + a.xn[row0 + t] + ps - (double)cum_b[(size_t)t * C + c];
+    const double lb = log(y) + a.yn[row0 + s] + (double)cum_b[(size_t)s * C + c] + pe;
+    sum += exp(la + lb - lz);
+  }
+  double* out = a.part_db + (size_t)b * a.nsplit * kcap * C;
+  out[(size_t)(k - 1) * C + c] = sum;
+  for (int sp = 1; sp < a.nsplit; ++sp) out[((size_t)sp * kcap + k - 1) * C + c] = 0.0;
 }
 
 // ---- fixed-order reduction over sequences and chunks -------------------------
@@ -449,6 +492,9 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
     if (e != cudaSuccess) return e;
     lmarg_db_kernel<2><<<gdb, kMT, p.db_smem, s>>>(a);
   }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  lmarg_db_fix_kernel<<<dim3((a.kcap * a.C + kMT - 1) / kMT, a.B), kMT, 0, s>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int nout = a.C * a.C + a.K * a.C;

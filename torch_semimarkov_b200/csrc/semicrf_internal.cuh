@@ -222,6 +222,7 @@ struct LMargArgs {
   double* part_db;  // (B, nsplit, kcap, C)
   int nsplit;
   int cg;           // labels per duration CTA
+  int* dbflag;      // (B) set when a duration tile's block factor nears the float64 range
 };
 struct LMargPlan {
   int nchunk, nsplit, cg, ncg, mi, nblk;
