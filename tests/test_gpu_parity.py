@@ -461,3 +461,21 @@ def test_chunked_chains_vs_oracle(case, oracle, monkeypatch):
     assert lib.semicrf_saved_size(prob.cref) > lib.semicrf_saved_size(ctypes.byref(prob_off))
     gout = np.random.default_rng(T).uniform(0.5, 1.5, size=B)
     _check_vs_oracle(inp, np.full(B, T), gout, K, "log", oracle)
+
+
+@pytest.mark.parametrize("scale,kcc", [(12.0, False), (20.0, False), (12.0, True)])
+def test_large_emission_scale_vs_oracle(scale, kcc, oracle):
+    """Emissions N(0, scale^2) per position: scores spread over hundreds of
+    log-units inside one block.  The duration gradient of the (C, C) path then
+    takes its term-by-term fallback; everything must still match the float64
+    oracle."""
+    B, T, K, C = 2, 160, 20, 6
+    g = torch.Generator().manual_seed(7)
+    em = torch.randn(B, T, C, generator=g, dtype=torch.float64) * scale
+    cum = torch.cat([torch.zeros(B, 1, C, dtype=torch.float64), em.cumsum(1)], 1).float()
+    shape = (K, C, C) if kcc else (C, C)
+    tr = (torch.randn(*shape, generator=g, dtype=torch.float64) * 0.1).float()
+    db = (torch.randn(K, C, generator=g, dtype=torch.float64) * 0.1).float()
+    inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
+           "proj_end": None}
+    _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, "log", oracle)
