@@ -463,12 +463,14 @@ def test_chunked_chains_vs_oracle(case, oracle, monkeypatch):
     _check_vs_oracle(inp, np.full(B, T), gout, K, "log", oracle)
 
 
-@pytest.mark.parametrize("scale,kcc", [(12.0, False), (20.0, False), (12.0, True)])
-def test_large_emission_scale_vs_oracle(scale, kcc, oracle):
+@pytest.mark.parametrize("scale,kcc,semiring", [(12.0, False, "log"), (20.0, False, "log"),
+                                                (12.0, True, "log"), (20.0, True, "log"),
+                                                (60.0, True, "max")])
+def test_large_emission_scale_vs_oracle(scale, kcc, semiring, oracle):
     """Emissions N(0, scale^2) per position: scores spread over hundreds of
-    log-units inside one block.  The duration gradient of the (C, C) path then
-    takes its term-by-term fallback; everything must still match the float64
-    oracle."""
+    log-units inside one block.  The (C, C) duration gradient then takes its
+    term-by-term fallback, and the (K, C, C) gradients their per-item log-domain
+    fallback; everything must still match the float64 oracle."""
     B, T, K, C = 2, 160, 20, 6
     g = torch.Generator().manual_seed(7)
     em = torch.randn(B, T, C, generator=g, dtype=torch.float64) * scale
@@ -478,4 +480,4 @@ def test_large_emission_scale_vs_oracle(scale, kcc, oracle):
     db = (torch.randn(K, C, generator=g, dtype=torch.float64) * 0.1).float()
     inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
            "proj_end": None}
-    _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, "log", oracle)
+    _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, semiring, oracle)

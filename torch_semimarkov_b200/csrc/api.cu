@@ -7,6 +7,8 @@
 #include <cmath>
 #include <cstring>
 
+#include <algorithm>
+
 #include "semicrf_internal.cuh"
 
 using namespace semicrf;
@@ -312,6 +314,7 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? SEMICRF_OK : SEMICRF_
 struct KccLayout {
   KccPrep pr;
   double *st, *et, *pend, *part_tr, *al, *anc, *ep1;
+  int* kflag;
   int nslice;
 };
 
@@ -320,6 +323,8 @@ KccLayout carve_kcc(Carver& cv, const semicrf_problem* p, bool backward) {
   const int K = (int)p->K, C = (int)p->C;
   w.pr = kcc_prep_carve(cv.take<double>(kcc_prep_doubles(K, C, p->semiring)), K, C,
                         p->semiring);
+  // the blocked kernels' overflow flag (forward: chain; backward: gradients)
+  if (kblk_supported(C, K)) w.kflag = cv.take<int>(1);
   if (!backward) return w;
   const size_t n = (size_t)p->batch * (p->T + 1) * p->C;
   w.st = cv.take<double>(n);
@@ -332,7 +337,9 @@ KccLayout carve_kcc(Carver& cv, const semicrf_problem* p, bool backward) {
     w.anc = cv.take<double>((size_t)p->batch * kblk_anchor_rows((int)p->T) * C);
   }
   w.nslice = blk ? kblk_tr_slices((int)p->batch, K, C) : kcc_tr_slices((int)p->batch, K, C);
-  w.part_tr = cv.take<double>((size_t)w.nslice * C * (size_t)(K - 1) * C);
+  // room for the per-item kernels' slices too: they are the blocked path's fallback
+  const int nsl_all = std::max(w.nslice, kcc_tr_slices((int)p->batch, K, C));
+  w.part_tr = cv.take<double>((size_t)nsl_all * C * (size_t)(K - 1) * C);
   return w;
 }
 
@@ -429,6 +436,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
                                     w.pr, s);
     if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
     KccArgs a = kcc_args(p, w.pr);
+    a.kflag = w.kflag;
     a.partition = partition;
     a.ref_ckpt = ring_checkpoints;
     a.nref = (int)num_ring_checkpoints;
@@ -584,6 +592,7 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
     a.al = w.al;
     a.anc = w.anc;
     a.ep1 = w.ep1;
+    a.kflag = w.kflag;
     return cuda_status(launch_kcc_grads(a, grad_transition, grad_duration_bias, s));
   }
   if (p->semiring == SEMICRF_LOG) {

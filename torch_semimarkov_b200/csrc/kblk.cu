@@ -149,6 +149,12 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a, int
   const float* pe_b = a.pe ? a.pe + (size_t)b * T * C : nullptr;
   const double* X = dir == 0 ? a.pr.xf : a.pr.xb;
   const size_t CC = (size_t)C * C;
+  // exp of a frame exponent; near the float64 range the blocked factoring is no
+  // longer exact, so the flag asks for the per-position fallback chain
+  auto cexp = [&](double x) -> double {
+    if (x > 600.0 && a.kflag) *a.kflag = 1;
+    return exp(fmin(x, 700.0));
+  };
 
   for (int i = tid; i < C; i += kBT) fk[i] = a.pr.fk[i];
   if (dir == 0 && a.ref_ckpt && out0) {
@@ -203,7 +209,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a, int
     const int nq = tau - bmin;  // far source blocks bmin .. tau-1
     for (int i = tid; i < nq * C; i += kBT) {
       const int q = (bmin + i / C) % NBR, l = i % C;
-      wq[q * C + l] = exp(fmin(fN[q] - N + fd[q * C + l] - fd[fs * C + l], 700.0));
+      wq[q * C + l] = cexp(fN[q] - N + fd[q * C + l] - fd[fs * C + l]);
     }
     __syncthreads();
     double rb = 0.0;
@@ -224,14 +230,14 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a, int
       const int j = i / C, l = i % C;
       const double dd = fd[fs * C + l];
       if (dir == 0) {
-        kap[i] = exp(fmin(ctb[i] + dd + fk[l], 700.0));
-        const double y = exp(fmin(dtb[i] - dd, 700.0));
+        kap[i] = cexp(ctb[i] + dd + fk[l]);
+        const double y = cexp(dtb[i] - dd);
         vb[i] = y;
         ry[(size_t)(fs * P + j) * C + l] = y;
       } else {
         const bool ok = rb > -INFINITY;
-        vb[i] = ok ? exp(fmin(dtb[i] + dd + fk[l] - rb, 700.0)) : 0.0;
-        kap[i] = ok ? exp(fmin(rb + ctb[i] - dd, 700.0)) : 0.0;
+        vb[i] = ok ? cexp(dtb[i] + dd + fk[l] - rb) : 0.0;
+        kap[i] = ok ? cexp(rb + ctb[i] - dd) : 0.0;
       }
     }
     __syncthreads();
@@ -405,6 +411,7 @@ __global__ void __launch_bounds__(kBT, 1) kblk_chain_kernel(const KccArgs a, int
       const int j = i / C, l = i % C, rho = s0 + j;
       const int t = dir == 0 ? rho : Lb - rho;
       const double pv = pend[i];
+      if (!(pv < INFINITY) && a.kflag) *a.kflag = 1;  // an overflowed row (or NaN)
       ra[(size_t)(fs * P + j) * C + l] = pv;
       double v = 0.0;
       if (rho > 0)
@@ -765,6 +772,7 @@ __global__ void kblk_anchor_kernel(const KccArgs a) {
       if (s >= 1 && s <= Lb) me = fmax(me, a.et[(row0 + s) * C + c]);
     }
     a.anc[i] = m > -INFINITY ? m : (me > -INFINITY ? -(me + a.pr.fk[c]) : 0.0);
+    if (i == 0 && a.kflag) *a.kflag = 0;  // kblk_factor_kernel sets it
   }
 }
 
@@ -790,8 +798,12 @@ __global__ void kblk_factor_kernel(const KccArgs a) {
     if (t >= 1 && t <= Lb) {
       const double et = a.et[i];
       if (et > -INFINITY) {
-        ev = exp(fmin(et + A + a.pr.fk[c], 700.0));
-        if (t >= kBP) ev1 = exp(fmin(et + A1 + a.pr.fk[c], 700.0));
+        const double x0 = et + A + a.pr.fk[c], x1 = et + A1 + a.pr.fk[c];
+        // near the float64 range the block factoring loses terms: the gradients
+        // are redone per item in the log domain (launch_kcc_grads)
+        if (a.kflag && (x0 > 600.0 || (t >= kBP && x1 > 600.0))) *a.kflag = 1;
+        ev = exp(fmin(x0, 700.0));
+        if (t >= kBP) ev1 = exp(fmin(x1, 700.0));
       }
     }
     a.al[i] = av;

@@ -156,6 +156,7 @@ __host__ __device__ inline ChainPlan chain_plan(int C, int K) {
 // partial sums per label are combined by one warp per label with shuffles.
 template <int SEMI>
 __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
+  if (a.gate && *a.gate == 0) return;  // fallback pass of the blocked chain, not needed
   extern __shared__ __align__(16) double ksm[];
   const int C = a.C, K = a.K, T = a.T, kcap = a.kcap, R = K;
   const int b = blockIdx.x, dir = blockIdx.y, tid = threadIdx.x;
@@ -487,6 +488,7 @@ __global__ void __launch_bounds__(kKT) kcc_chain_kernel(const KccArgs a) {
 // start term st[s,c] = amax[s] + ps[s,c] - cum[s,c] - logZ (s < len) and end
 // term et[e,c] = beta[e,c] + cum[e,c] + pe[e-1,c] (1 <= e <= len); -inf elsewhere
 __global__ void kcc_terms_kernel(const KccArgs a) {
+  if (a.gate && *a.gate == 0) return;
   const int C = a.C, T = a.T;
   const size_t total = (size_t)a.B * (T + 1) * C;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -515,6 +517,7 @@ __global__ void kcc_terms_kernel(const KccArgs a) {
 // max semiring: the end marginal of every (position, label), summed over its
 // incoming segments (the log semiring has it as exp(alpha + beta - logZ))
 __global__ void kcc_pend_max_kernel(const KccArgs a) {
+  if (a.gate && *a.gate == 0) return;
   const int C = a.C, T = a.T, kcap = a.kcap;
   const size_t total = (size_t)a.B * (T + 1) * C;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -577,6 +580,7 @@ __host__ __device__ inline PosPlan pos_plan(int C, int kcap) {
 // positions g + nsg*j, j < kJ, so each transition factor it loads serves kJ
 // positions.
 __global__ void __launch_bounds__(kKT) kcc_pos_kernel(const KccArgs a) {
+  if (a.gate && *a.gate == 0) return;
   extern __shared__ __align__(16) double psm[];
   const int C = a.C, T = a.T, kcap = a.kcap;
   const PosPlan pp = pos_plan(C, kcap);
@@ -667,6 +671,7 @@ __global__ void __launch_bounds__(kKT) kcc_pos_kernel(const KccArgs a) {
 // One CTA per (column tile, row tile, slice); each thread keeps a 4 x 8 tile
 // of accumulators in registers.
 __global__ void __launch_bounds__(kKT) kcc_tr_kernel(const KccArgs a) {
+  if (a.gate && *a.gate == 0) return;
   const int C = a.C, T = a.T, kcap = a.kcap, B = a.B;
   const int ncol = kcap * C;
   const int col0 = blockIdx.x * kTC, r0 = blockIdx.y * kTR, slice = blockIdx.z;
@@ -739,6 +744,7 @@ __global__ void __launch_bounds__(kKT) kcc_tr_kernel(const KccArgs a) {
 
 // grad_tr[k][c'][c] = ef[k][c'][c] * sum_slice part; grad_db[k][c] = sum_c' grad_tr[k][c'][c]
 __global__ void kcc_reduce_kernel(const KccArgs a, float* grad_tr, float* grad_db) {
+  if (a.gate && *a.gate == 0) return;
   const int C = a.C, K = a.K, kcap = a.kcap;
   const int ncol = kcap * C;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K * C; i += gridDim.x * blockDim.x) {
@@ -818,10 +824,24 @@ cudaError_t launch_kcc_prep(const float* tr, const float* db, int K, int C, cons
   return launch_kblk_prep(tr, db, K, C, pr, s);  // the blocked chain's weights (log semiring)
 }
 
-cudaError_t launch_kcc_chains(const KccArgs& a, int ndir, cudaStream_t s) {
-  if (a.B <= 0) return cudaSuccess;
+cudaError_t launch_kcc_chains(const KccArgs& a0, int ndir, cudaStream_t s) {
+  if (a0.B <= 0) return cudaSuccess;
+  KccArgs a = a0;
   const bool have = a.semiring == SEMICRF_MAX ? (a.pr.rf != nullptr) : (a.pr.xf != nullptr);
-  if (have && kblk_supported(a.C, a.K)) return launch_kblk_chains(a, ndir, s);
+  if (have && kblk_supported(a.C, a.K)) {
+    const bool guard = a.semiring == SEMICRF_LOG && a.kflag;
+    if (guard) {
+      cudaError_t e = cudaMemsetAsync(a.kflag, 0, sizeof(int), s);
+      if (e != cudaSuccess) return e;
+    }
+    cudaError_t e = launch_kblk_chains(a, ndir, s);
+    if (e != cudaSuccess || !guard) return e;
+    // the log chain's float64 factors left their range (very large emission
+    // scores): the per-position chain below redoes the tables in the log
+    // domain; otherwise it returns at once
+    a.gate = a.kflag;
+    a.kflag = nullptr;
+  }
   const size_t bytes = chain_plan(a.C, a.K).total * 8;
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e =
@@ -843,7 +863,19 @@ cudaError_t launch_kcc_grads(const KccArgs& a, float* grad_tr, float* grad_db, c
     e = launch_kblk_grads(a, s);
     if (e != cudaSuccess) return e;
     kcc_reduce_kernel<<<grid_for((size_t)a.K * a.C, 128), 128, 0, s>>>(a, grad_tr, grad_db);
-    return cudaGetLastError();
+    e = cudaGetLastError();
+    if (e != cudaSuccess || !a.kflag) return e;
+    // fallback: when the blocked factors left the float64 range (very large
+    // emission scores) the per-item kernels below redo every gradient in the log
+    // domain; otherwise each of them returns at once
+    KccArgs f = a;
+    f.al = nullptr;
+    f.anc = nullptr;
+    f.ep1 = nullptr;
+    f.gate = a.kflag;
+    f.kflag = nullptr;
+    f.nslice = kcc_tr_slices(a.B, a.K, a.C);
+    return launch_kcc_grads(f, grad_tr, grad_db, s);
   }
   if (a.semiring == SEMICRF_MAX) {
     kcc_pend_max_kernel<<<grid_for(n, 128), 128, 0, s>>>(a);

@@ -333,6 +333,8 @@ struct KccArgs {
   double* al;
   double* anc;
   double* ep1;  // end factors relative to the previous block's anchor
+  int* kflag;    // set by the blocked factor pass when an end factor nears the float64 range
+  int* gate;     // fallback pass: the per-item kernels return at once unless *gate != 0
 };
 bool kcc_supported(int C, int K);
 size_t kcc_prep_doubles(int K, int C, int semiring);
