@@ -308,6 +308,9 @@ KCC_CASES = [
     (12, 120, 30, 6, "cfg2", None, "log"),
     (20, 80, 20, 4, "default", "both", "log"),
     (40, 50, 6, 5, "default", None, "log"),
+    # the max-plus chain with one CTA per chain, and with C > 32 (weights not in registers)
+    (40, 50, 6, 5, "default", "both", "max"),
+    (2, 60, 9, 40, "cfg5", None, "max"),
     # more labels than the blocked kernels take: the per-position gather chain
     (2, 30, 3, 130, "default", "both", "max"),
 ]
