@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libsemicrf.so")
-SOURCES = ["api.cu", "chain.cu", "lchain.cu", "lchain_ws.cu", "lchain_cl.cu", "lchunk.cu", "lmarg.cu", "marginals.cu", "viterbi.cu", "vchain.cu", "kcc.cu", "kblk.cu", "escan.cu", "gold.cu",
+SOURCES = ["api.cu", "chain.cu", "lchain.cu", "lchain_ws.cu", "lchain_fix.cu", "lchain_cl.cu", "lchunk.cu", "lmarg.cu", "marginals.cu", "viterbi.cu", "vchain.cu", "kcc.cu", "kblk.cu", "escan.cu", "gold.cu",
            "noalloc.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

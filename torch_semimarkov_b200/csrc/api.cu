@@ -73,6 +73,7 @@ Prepared carve_prep(Carver& cv, int C, int K, int semiring) {
     pr.mxd_f = cv.take<double>((size_t)C * C);
     pr.mxd_b = cv.take<double>((size_t)C * C);
     pr.dbed = cv.take<double>((size_t)kx * C);
+    pr.ovf = cv.take<int>(1);
   } else {
     pr.mx_f = cv.take<float>((size_t)C * C);
     pr.mx_b = cv.take<float>((size_t)C * C);
@@ -509,8 +510,18 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
           return cuda_status(chunked_chains(p, L, sl, s));
       }
     }
-    if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_ws_supported((int)p->C, (int)p->K))
-      return cuda_status(launch_lchain_ws(L, grid, s));
+    if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_ws_supported((int)p->C, (int)p->K)) {
+      // the log-domain rerun when the chain's float64 frames clip (extreme scores)
+      const bool fix = lchain_fix_supported((int)p->C, (int)p->K);
+      if (fix) {
+        L.dbl = pr.dbl;
+        L.ovf = pr.ovf;
+        if (cudaMemsetAsync(pr.ovf, 0, sizeof(int), s) != cudaSuccess) return SEMICRF_ERR_CUDA;
+      }
+      cudaError_t e2 = launch_lchain_ws(L, grid, s);
+      if (e2 != cudaSuccess || !fix) return cuda_status(e2);
+      return cuda_status(launch_lchain_fix(L, grid, s));
+    }
     if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_cl_supported((int)p->C, (int)p->K))
       return cuda_status(launch_lchain_cl(L, grid, s));
     return cuda_status(launch_lchain(L, grid, s));

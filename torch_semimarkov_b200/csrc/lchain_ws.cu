@@ -361,8 +361,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (e_i[r] == 0) {
           const int cc = e_c[r];
           cA[bf * CP + cc] = pre[r];
-          const double w = exp(fmin(fmax(n_prev - n_tau + csign * (pre[r] - cA[(bf ^ 1) * CP + cc]),
-                                         -700.0), 700.0));
+          const double wx = n_prev - n_tau + csign * (pre[r] - cA[(bf ^ 1) * CP + cc]);
+          if (L.ovf && fabs(wx) > 700.0) *L.ovf = 1;  // the frame change clips
+          const double w = exp(fmin(fmax(wx, -700.0), 700.0));
           wprev[bf * CP + cc] = w;
         }
       }
@@ -393,13 +394,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           const double d = csign * (pre[r] - cA[bf * CP + cc]);
           if (noproj) {
             // |dc| <= 650 keeps exp(dc) and its reciprocal normal
+            if (L.ovf && fabs(d) > 650.0) *L.ovf = 1;
             const double dc = fmin(fmax(d, -650.0), 650.0);
             const double ed = exp(dc);
             gb[(bf * LP + i) * CP + cc] = edb[cc] * ed;
             hb[(bf * LP + i) * CP + cc] = ecm[cc] * __drcp_rn(ed);
           } else {
-            gb[(bf * LP + i) * CP + cc] = exp(fmin(toff_at(u, cc) + dbmax[cc] + d, 700.0));
-            hb[(bf * LP + i) * CP + cc] = exp(fmin(colmax[cc] + soff_at(u, cc) - d, 700.0));
+            const double gx = toff_at(u, cc) + dbmax[cc] + d, hx = colmax[cc] + soff_at(u, cc) - d;
+            if (L.ovf && (gx > 700.0 || hx > 700.0)) *L.ovf = 1;
+            gb[(bf * LP + i) * CP + cc] = exp(fmin(gx, 700.0));
+            hb[(bf * LP + i) * CP + cc] = exp(fmin(hx, 700.0));
           }
         }
       }

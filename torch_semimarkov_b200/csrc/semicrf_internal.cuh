@@ -62,6 +62,7 @@ struct Prepared {
   float* dbl;       // (KX, C): log duration bias by duration k, -inf outside 1..kcap
   float* dbe;       // (KX, C): exp(dbl - dbmax)
   float* dbmax;     // (C)
+  int* ovf;         // log semiring: the chain's overflow flag
   int kx;           // rows of dbl / dbe = kcap + P + 1
 };
 
@@ -151,6 +152,8 @@ struct LChainLaunch {
   int B, T, K, C;
   const double* dbe;   // (kx, C) exp(db - dbmax), zero outside durations 1..kcap
   const float* dbmax;  // (C)
+  const float* dbl;    // (kx, C) log duration bias by duration (the log-domain fallback)
+  int* ovf;            // set by lchain_ws_kernel when an exponent clamp clips; may be null
   int n1;              // CTAs [0, n1) run a0, the rest a1
   LChainArgs a0;
   LChainArgs a1;
@@ -158,6 +161,9 @@ struct LChainLaunch {
 cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s);
 // warp-specialised variant for C <= 64, whole-sequence chains (mode 0) only
 cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s);
+// lchain_fix.cu: log-domain rerun of the lchain_ws chains when L.ovf is set
+bool lchain_fix_supported(int C, int K);
+cudaError_t launch_lchain_fix(const LChainLaunch& L, int grid, cudaStream_t s);
 // cluster variant for 64 < C <= 256 (lchain_cl.cu): one chain per cluster of
 // four CTAs, whole-sequence chains (mode 0) without ring checkpoints
 bool lchain_cl_supported(int C, int K);
