@@ -429,9 +429,10 @@ def main():
         # result is produced in those units (not work this build executes)
         "reference_equivalent": {"edge_terms_per_position_pass": kcap * C * C, "passes": 4,
                                  "edge_terms_per_s": 4 * kcap * C * C * B * T / t_step},
-        # per step: forward = prep (2) + chains (1); backward = pos, blk, tr, db,
-        # db_fix (returns at once unless a sequence was flagged), reduce
-        "gpu_launches": 9 * args.steps,
+        # per step: forward = prep (2) + chains (1) + chain_fix (returns at once
+        # unless a clamp clipped); backward = pos, blk, tr, db, db_fix (returns at
+        # once unless a sequence was flagged), reduce
+        "gpu_launches": 10 * args.steps,
         "clocks": clocks,
     }
     if viterbi:
