@@ -486,3 +486,19 @@ def test_large_emission_scale_vs_oracle(scale, kcc, semiring, oracle):
     inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
            "proj_end": None}
     _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, semiring, oracle)
+
+
+def test_chunked_chains_large_scale_vs_oracle(oracle, monkeypatch):
+    """Time-chunked chains with emissions N(0, 60^2): the chunks' frames clip and
+    the whole chains are rerun in the log domain."""
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_CHUNKS", "8")
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_BACKWARD", "keep")
+    B, T, K, C = 1, 3000, 20, 8
+    g = torch.Generator().manual_seed(9)
+    em = torch.randn(B, T, C, generator=g, dtype=torch.float64) * 60.0
+    cum = torch.cat([torch.zeros(B, 1, C, dtype=torch.float64), em.cumsum(1)], 1).float()
+    tr = (torch.randn(C, C, generator=g, dtype=torch.float64) * 0.1).float()
+    db = (torch.randn(K, C, generator=g, dtype=torch.float64) * 0.1).float()
+    inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
+           "proj_end": None}
+    _check_vs_oracle(inp, np.array([T]), np.array([1.0]), K, "log", oracle)

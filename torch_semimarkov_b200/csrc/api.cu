@@ -506,8 +506,19 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
         L.a0.n_tab = sl.n_tab;
         L.a1 = beta_chain_args(p, pr, sl.b_tab, sl.B_tab, sl.m_tab);
         grid = 2 * (int)p->batch;
-        if (sl.cp.nchunk > 1 && !L.a0.ref_ckpt)
-          return cuda_status(chunked_chains(p, L, sl, s));
+        if (sl.cp.nchunk > 1 && !L.a0.ref_ckpt) {
+          // as below: a log-domain rerun of whole chains when a chunk's frames clip
+          const bool fix = lchain_fix_supported((int)p->C, (int)p->K);
+          if (fix) {
+            L.dbl = pr.dbl;
+            L.ovf = pr.ovf;
+            if (cudaMemsetAsync(pr.ovf, 0, sizeof(int), s) != cudaSuccess)
+              return SEMICRF_ERR_CUDA;
+          }
+          cudaError_t e2 = chunked_chains(p, L, sl, s);
+          if (e2 != cudaSuccess || !fix) return cuda_status(e2);
+          return cuda_status(launch_lchain_fix(L, grid, s));
+        }
       }
     }
     if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_ws_supported((int)p->C, (int)p->K)) {
