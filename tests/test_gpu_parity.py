@@ -488,6 +488,22 @@ def test_large_emission_scale_vs_oracle(scale, kcc, semiring, oracle):
     _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, semiring, oracle)
 
 
+@pytest.mark.parametrize("C", [96, 256])
+def test_cluster_chain_large_scale_vs_oracle(C, oracle):
+    """64 < C <= 256 runs the cluster chain; with emissions N(0, 60^2) its factors
+    clip and the chains are rerun in the log domain (at C = 96 with the
+    transition staged in shared memory, at C = 256 read from global memory)."""
+    B, T, K = 2, 96, 12
+    g = torch.Generator().manual_seed(11)
+    em = torch.randn(B, T, C, generator=g, dtype=torch.float64) * 60.0
+    cum = torch.cat([torch.zeros(B, 1, C, dtype=torch.float64), em.cumsum(1)], 1).float()
+    tr = (torch.randn(C, C, generator=g, dtype=torch.float64) * 0.1).float()
+    db = (torch.randn(K, C, generator=g, dtype=torch.float64) * 0.1).float()
+    inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
+           "proj_end": None}
+    _check_vs_oracle(inp, np.array([T, T - 29]), np.array([1.0, 0.7]), K, "log", oracle)
+
+
 def test_chunked_chains_large_scale_vs_oracle(oracle, monkeypatch):
     """Time-chunked chains with emissions N(0, 60^2): the chunks' frames clip and
     the whole chains are rerun in the log domain."""

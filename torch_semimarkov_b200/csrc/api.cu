@@ -533,8 +533,18 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
       if (e2 != cudaSuccess || !fix) return cuda_status(e2);
       return cuda_status(launch_lchain_fix(L, grid, s));
     }
-    if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_cl_supported((int)p->C, (int)p->K))
-      return cuda_status(launch_lchain_cl(L, grid, s));
+    if (!L.a0.ref_ckpt && !L.a0.write_saved && lchain_cl_supported((int)p->C, (int)p->K)) {
+      // the same log-domain rerun for the cluster chain (64 < C <= 256)
+      const bool fix = lchain_fix_supported((int)p->C, (int)p->K);
+      if (fix) {
+        L.dbl = pr.dbl;
+        L.ovf = pr.ovf;
+        if (cudaMemsetAsync(pr.ovf, 0, sizeof(int), s) != cudaSuccess) return SEMICRF_ERR_CUDA;
+      }
+      cudaError_t e2 = launch_lchain_cl(L, grid, s);
+      if (e2 != cudaSuccess || !fix) return cuda_status(e2);
+      return cuda_status(launch_lchain_fix(L, grid, s));
+    }
     return cuda_status(launch_lchain(L, grid, s));
   }
   ChainLaunch L = base_launch(p, pr);

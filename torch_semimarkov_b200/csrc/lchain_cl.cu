@@ -372,6 +372,9 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
       const double cu = pcu0[w];
       const double lg_ = pto0[w] + rf + dbmax[cc] + csign * cu - n_cur;
       const double lh_ = colmax[cc] + n_cur + pso0[w] - csign * cu - rf;
+      // a clipped factor means the scores span more than the float64 range:
+      // flag the launch for the log-domain rerun that follows it
+      if (L.ovf && (fabs(lg_) > 700.0 || fabs(lh_) > 700.0)) *L.ovf = 1;
       gf0[w] = exp(fmin(fmax(lg_, -700.0), 700.0));
       hf0[w] = exp(fmin(fmax(lh_, -700.0), 700.0));
     }
@@ -458,6 +461,7 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
         if (on) {
           const double e = (ym > 0.0) ? ym * hf0[(gs * kLP + i) * CL + c] : 0.0;
           ev[i] = e;
+          if (L.ovf && !(isfinite(a) && isfinite(e))) *L.ovf = 1;
           ring_me[slot * CL + c] = e;
           const int t = cpos(gs, u);
           if (atab_me) atab_me[(size_t)t * C + gcl] = a;

@@ -12,8 +12,12 @@
 //   v[u,c] = m[u,c] + soff(u,c) - s cum(u,c),   m[u,c] = LSE_c' ( x[u,c'] + M[c',c] )
 // with s = +1 forward (x = alpha, m = A, M = transition) and s = -1 backward
 // (x = G, m = beta, M = transition^T), and the start rows alpha[0] = 0 and
-// beta[len] = 0.  M is read back from the prepared exp(M - colmax) and db from
-// the prepared log duration table.  The rows written are the chain tables
+// beta[len] = 0.  The m row is formed from the prepared exp(M - colmax) as
+// m[c] = xmax + colmax[c] + log sum_c' exp(x[c'] - xmax) exp(M[c',c] - colmax[c]),
+// with a per-term log-domain sum for a column whose products all underflow;
+// exp(M - colmax) is staged in shared memory when C * C doubles fit beside the
+// ring and read from global memory otherwise (C up to 256).  db comes from the
+// prepared log duration table.  The rows written are the chain tables
 // a = exp(x - n), A = exp(m - n) and n (n = the row's largest x or m), and log Z
 // = LSE_c alpha[len, c], exactly what the backward reads.
 
@@ -26,12 +30,15 @@ namespace {
 constexpr int kFT = 256;
 constexpr size_t kFSmemMax = 200 * 1024;
 
-__host__ __device__ inline size_t fix_smem_doubles(int C, int K) {
+// the ring, the row vectors and the reduction scratch; plus C * C when M is staged
+__host__ __device__ inline size_t fix_smem_doubles(int C, int K, bool stage_m) {
   const int kcap = K - 1 > 1 ? K - 1 : 1;
-  return (size_t)kcap * C + (size_t)C * C + 4 * (size_t)C + 2 * kFT + 8;
+  return (size_t)kcap * C + (stage_m ? (size_t)C * C : 0) + 4 * (size_t)C + 2 * kFT + 8;
 }
 
-__global__ void __launch_bounds__(kFT) lchain_fix_kernel(const LChainLaunch L) {
+inline bool fix_stage_m(int C, int K) { return fix_smem_doubles(C, K, true) * 8 <= kFSmemMax; }
+
+__global__ void __launch_bounds__(kFT) lchain_fix_kernel(const LChainLaunch L, int stage_m) {
   if (!L.ovf || *L.ovf == 0) return;
   extern __shared__ __align__(16) double fsm[];
   const int C = L.C, K = L.K, T = L.T;
@@ -45,13 +52,15 @@ __global__ void __launch_bounds__(kFT) lchain_fix_kernel(const LChainLaunch L) {
   const double sg = dir == 0 ? 1.0 : -1.0;
   const long long lraw = A.lengths[b];
   const int Lb = lraw < 0 ? 0 : (lraw > T ? T : (int)lraw);
-  double* ring = fsm;                     // [kcap][C]: v of the last kcap positions
-  double* Ml = ring + (size_t)kcap * C;   // [C][C]: M in log form
-  double* xr = Ml + (size_t)C * C;        // [C]
-  double* mr = xr + C;                    // [C]
-  double* pm = mr + 2 * C;                // [kFT] partial maxima
-  double* ps2 = pm + kFT;                 // [kFT] partial sums
-  double* nrow = ps2 + kFT;               // [1]
+  double* ring = fsm;                                // [kcap][C]: v of the last kcap positions
+  double* Ms = ring + (size_t)kcap * C;              // [C][C]: exp(M - colmax), when staged
+  double* xr = Ms + (stage_m ? (size_t)C * C : 0);   // [C]
+  double* er = xr + C;                               // [C]: exp(x - xmax)
+  double* mr = er + C;                               // [C]
+  double* pm = mr + 2 * C;                           // [kFT] partial maxima
+  double* ps2 = pm + kFT;                            // [kFT] partial sums
+  double* nrow = ps2 + kFT;                          // [2]: n, xmax
+  const double* Mg = stage_m ? Ms : A.mx;
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
   const float* ps_b = A.ps ? A.ps + (size_t)b * T * C : nullptr;
   const float* pe_b = A.pe ? A.pe + (size_t)b * T * C : nullptr;
@@ -67,26 +76,46 @@ __global__ void __launch_bounds__(kFT) lchain_fix_kernel(const LChainLaunch L) {
     return (ps_b && t < T) ? (double)ps_b[(size_t)t * C + c] : 0.0;
   };
   auto cumd = [&](int u, int c) -> double { return (double)cum_b[(size_t)cpos(u) * C + c]; };
-  for (int i = tid; i < C * C; i += kFT) {
-    const double e = A.mx[i];
-    Ml[i] = e > 0.0 ? log(e) + (double)A.colmax[i % C] : -INFINITY;
-  }
+  if (stage_m)
+    for (int i = tid; i < C * C; i += kFT) Ms[i] = A.mx[i];
   double* atab = A.a_tab ? A.a_tab + (size_t)b * (T + 1) * C : nullptr;
   double* Atab = A.A_tab ? A.A_tab + (size_t)b * (T + 1) * C : nullptr;
   double* ntab = A.n_tab ? A.n_tab + (size_t)b * (T + 1) : nullptr;
   __syncthreads();
   // the row's m from its x, its tables, and its v into the ring
   auto finish_row = [&](int u) {
+    if (tid == 0) {
+      double xm = -INFINITY;
+      for (int c = 0; c < C; ++c) xm = fmax(xm, xr[c]);
+      nrow[1] = xm;
+    }
+    __syncthreads();
+    const double xm = nrow[1];
+    for (int q = tid; q < C; q += kFT) er[q] = xr[q] > -INFINITY ? exp(xr[q] - xm) : 0.0;
+    __syncthreads();
     for (int c = tid; c < C; c += kFT) {
-      double mx = -INFINITY;
-      for (int q = 0; q < C; ++q) mx = fmax(mx, xr[q] + Ml[q * C + c]);
       double sm = 0.0;
-      if (mx > -INFINITY)
+      for (int q = 0; q < C; ++q) sm = fma(er[q], Mg[(size_t)q * C + c], sm);
+      double m = -INFINITY;
+      if (sm > 0.0) {
+        m = xm + (double)A.colmax[c] + log(sm);
+      } else if (xm > -INFINITY) {
+        // every product underflowed: the same sum term by term in the log domain
+        double mx = -INFINITY;
         for (int q = 0; q < C; ++q) {
-          const double z = xr[q] + Ml[q * C + c];
-          if (z > -INFINITY) sm += exp(z - mx);
+          const double e = Mg[(size_t)q * C + c];
+          if (e > 0.0 && xr[q] > -INFINITY) mx = fmax(mx, xr[q] + log(e));
         }
-      mr[c] = mx > -INFINITY ? mx + log(sm) : -INFINITY;
+        if (mx > -INFINITY) {
+          double s2 = 0.0;
+          for (int q = 0; q < C; ++q) {
+            const double e = Mg[(size_t)q * C + c];
+            if (e > 0.0 && xr[q] > -INFINITY) s2 += exp(xr[q] + log(e) - mx);
+          }
+          m = mx + log(s2) + (double)A.colmax[c];
+        }
+      }
+      mr[c] = m;
     }
     if (u == 0 && dir == 1)
       for (int c = tid; c < C; c += kFT) mr[c] = 0.0;  // beta[len] = 0
@@ -161,16 +190,17 @@ __global__ void __launch_bounds__(kFT) lchain_fix_kernel(const LChainLaunch L) {
 }  // namespace
 
 bool lchain_fix_supported(int C, int K) {
-  return C <= kFT && fix_smem_doubles(C, K) * 8 <= kFSmemMax;
+  return C <= kFT && fix_smem_doubles(C, K, false) * 8 <= kFSmemMax;
 }
 
 cudaError_t launch_lchain_fix(const LChainLaunch& L, int grid, cudaStream_t s) {
   if (!L.ovf || grid <= 0) return cudaSuccess;
-  const size_t bytes = fix_smem_doubles(L.C, L.K) * 8;
+  const bool stage = fix_stage_m(L.C, L.K);
+  const size_t bytes = fix_smem_doubles(L.C, L.K, stage) * 8;
   cudaError_t e = cudaFuncSetAttribute(lchain_fix_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   if (e != cudaSuccess) return e;
-  lchain_fix_kernel<<<grid, kFT, bytes, s>>>(L);
+  lchain_fix_kernel<<<grid, kFT, bytes, s>>>(L, stage ? 1 : 0);
   return cudaGetLastError();
 }
 
