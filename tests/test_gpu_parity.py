@@ -101,6 +101,32 @@ def test_ring_checkpoints_layout_and_values(name):
     assert torch.all(ck[:, 0, 0] == 0)
 
 
+@pytest.mark.parametrize("C", [6, 96])
+def test_ring_checkpoints_large_scale_vs_oracle(C, oracle):
+    """The reference launcher's ring checkpoints come from the generic chain;
+    with emissions N(0, 60^2) its factors clip and the rerun in the log domain
+    rewrites log Z and the checkpoint rows, which must match the float64 oracle."""
+    from torch_semimarkov_b200 import launch_streaming_triton_kernel
+
+    dev = _dev()
+    B, T, K = 2, 160, 20
+    g = torch.Generator().manual_seed(13)
+    em = torch.randn(B, T, C, generator=g, dtype=torch.float64) * 60.0
+    cum = torch.cat([torch.zeros(B, 1, C, dtype=torch.float64), em.cumsum(1)], 1).float()
+    tr = (torch.randn(C, C, generator=g, dtype=torch.float64) * 0.1).float()
+    db = (torch.randn(K, C, generator=g, dtype=torch.float64) * 0.1).float()
+    lengths = np.array([T, T - 37])
+    part_ref, ck_ref, S_ref = oracle.forward(cum.numpy(), tr.numpy(), db.numpy(), lengths, K)
+    part, ck, S = launch_streaming_triton_kernel(cum.to(dev), tr.to(dev), db.to(dev),
+                                                 torch.as_tensor(lengths).to(dev), K)
+    assert S == S_ref
+    assert_close_rel(part.cpu().numpy(), part_ref, what="partition")
+    got = ck[:, : ck_ref.shape[1]].cpu().numpy()
+    unset = ck_ref <= -1e8
+    np.testing.assert_array_equal(got[unset], np.float32(-1e9))
+    assert_close_rel(got[~unset], ck_ref[~unset], what="checkpoints")
+
+
 HEAD = golden_names("head_")
 
 

@@ -545,7 +545,17 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
       if (e2 != cudaSuccess || !fix) return cuda_status(e2);
       return cuda_status(launch_lchain_fix(L, grid, s));
     }
-    return cuda_status(launch_lchain(L, grid, s));
+    // the generic chain: the same rerun for whole chains (ring checkpoints
+    // included); the recompute-mode forward keeps linear checkpoints and has none
+    const bool fix = !L.a0.write_saved && lchain_fix_supported((int)p->C, (int)p->K);
+    if (fix) {
+      L.dbl = pr.dbl;
+      L.ovf = pr.ovf;
+      if (cudaMemsetAsync(pr.ovf, 0, sizeof(int), s) != cudaSuccess) return SEMICRF_ERR_CUDA;
+    }
+    cudaError_t e2 = launch_lchain(L, grid, s);
+    if (e2 != cudaSuccess || !fix) return cuda_status(e2);
+    return cuda_status(launch_lchain_fix(L, grid, s));
   }
   ChainLaunch L = base_launch(p, pr);
   ChainArgs a = base_args(p);

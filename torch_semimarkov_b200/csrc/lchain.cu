@@ -427,6 +427,9 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
       const double cu = pcu[i * CP + cc];
       const double lg_ = pto[i * CP + cc] + ref[cc] + dbmax[cc] + csign * cu - n_cur;
       const double lh_ = colmax[cc] + n_cur + pso[i * CP + cc] - csign * cu - ref[cc];
+      // a clipped factor means the scores span more than the float64 range:
+      // flag the launch for the log-domain rerun that follows it
+      if (L.ovf && (fabs(lg_) > 700.0 || fabs(lh_) > 700.0)) *L.ovf = 1;
       gf[i * CP + cc] = exp(fmin(fmax(lg_, -700.0), 700.0));
       hf[i * CP + cc] = exp(fmin(fmax(lh_, -700.0), 700.0));
     }
@@ -506,6 +509,7 @@ __global__ void __launch_bounds__(kNT, 1) lchain_kernel(const __grid_constant__ 
           if (cv) {
             const double e = (ym > 0.0) ? ym * hf[i * CP + c] : 0.0;
             ev[i] = e;
+            if (L.ovf && !(isfinite(a) && isfinite(e))) *L.ovf = 1;
             ring[slot * C + c] = e;
             const int t = cpos(u);
             if (atab_b) atab_b[(size_t)t * C + c] = a;

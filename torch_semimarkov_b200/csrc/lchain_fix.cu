@@ -19,7 +19,10 @@
 // ring and read from global memory otherwise (C up to 256).  db comes from the
 // prepared log duration table.  The rows written are the chain tables
 // a = exp(x - n), A = exp(m - n) and n (n = the row's largest x or m), and log Z
-// = LSE_c alpha[len, c], exactly what the backward reads.
+// = LSE_c alpha[len, c], exactly what the backward reads; for a forward that
+// also returns the reference's ring checkpoints (launch_streaming_triton_kernel
+// layout, (B, nref, K, C) float32 log alpha) the rows inside each checkpoint's
+// window are rewritten too.
 
 #include "semicrf_internal.cuh"
 
@@ -171,6 +174,14 @@ __global__ void __launch_bounds__(kFT) lchain_fix_kernel(const LChainLaunch L, i
       xr[cc] = mm > -INFINITY ? toff(u, cc) + sg * cumd(u, cc) + mm + log(ss) : -INFINITY;
     }
     __syncthreads();
+    if (dir == 0 && A.ref_ckpt) {
+      // checkpoint ic holds alpha of the positions (ic S - K, ic S], slot u % K
+      const int Sr = A.sref, ic = (u + Sr - 1) / Sr;
+      if (ic < A.nref && ic * Sr <= Lb && ic * Sr - u < K)
+        for (int cc = tid; cc < C; cc += kFT)
+          A.ref_ckpt[(((size_t)b * A.nref + ic) * K + (u % K)) * C + cc] =
+              xr[cc] > -INFINITY ? (float)xr[cc] : kRefNegInf;
+    }
     finish_row(u);
   }
   if (dir == 0 && tid == 0) {
