@@ -66,16 +66,26 @@ def dist_env():
 # clocks sampler (nvidia-smi during the timed region)
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons of this rank's GPU while the timed region
+    runs.  An NVML thread polls every 5 ms (queries only; nothing is set); the
+    first sample is taken before start() returns, so a timed region of a few
+    tens of milliseconds still gets a dozen samples.  nvidia-smi is the fallback
+    when the NVML bindings are missing."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.thread = None
 
     def start(self):
+        if self._start_nvml():
+            return
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -84,10 +94,53 @@ class ClockSampler:
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
+            t0 = time.time()
+            while time.time() - t0 < 5 and os.path.getsize(self.path) == 0:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
 
+    def _start_nvml(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None)
+            if reasons is None:
+                reasons = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            return False
+        self.samples = []
+        self.halt = threading.Event()
+
+        def poll():
+            while not self.halt.is_set():
+                try:
+                    self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(
+                        h, pynvml.NVML_CLOCK_SM)), int(reasons(h))))
+                except Exception:
+                    pass
+                self.halt.wait(0.005)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 2:
+            time.sleep(0.001)
+        return True
+
     def stop(self):
+        if self.thread is not None:
+            self.halt.set()
+            self.thread.join(timeout=2)
+            if not self.samples:
+                return None
+            reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS if r & bit})
+            return {"sm_mhz": statistics.median(c for c, _ in self.samples),
+                    "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, 5 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -110,7 +163,7 @@ class ClockSampler:
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi, 50 ms"}
 
 
 # ---------------------------------------------------------------------------
