@@ -186,9 +186,10 @@ __global__ void __launch_bounds__(kMT) lmarg_blk_kernel(const LMargArgs a) {
 // X <= 1 and Y is bounded by a segment marginal, so both stay in range, and a
 // source that underflows in Ylin is negligible beside its block's maximum.
 // An item is a (label, kLG consecutive k) pair: MI items per thread.  A thread
-// forms 8 targets x kLG lags per step from 8 + (8 + kLG - 1) staged values, so
-// each shared-memory load serves four FMAs.
+// forms 16 targets x kLG lags per step from 16 + (16 + kLG - 1) staged values,
+// so each shared-memory load serves more than five FMAs.
 constexpr int kLG = 16;
+static_assert(kTT % 16 == 0, "lmarg_db_kernel steps over targets in groups of 16");
 template <int MI>
 __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LMargArgs a) {
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -283,19 +284,20 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
       if (it < nitems) {
         const int cc = it % cgn, kg = it / cgn;
         const int k_lo = 1 + kLG * kg;
-        // target i pairs with Y[i + k - 1]: for targets i0 .. i0+7 the window
-        // y[m] = Y[i0 + k_lo - 1 + m], m < kLG + 7, covers all kLG lags (X is
-        // zero beyond the last target, so whole groups of 8 are safe)
-        for (int i0 = 0; i0 < n; i0 += 8) {
-          double y[kLG + 7], x[8];
+        // target i pairs with Y[i + k - 1]: for targets i0 .. i0+15 the window
+        // y[m] = Y[i0 + k_lo - 1 + m], m < kLG + 15, covers all kLG lags (X is
+        // zero beyond the last target and kTT is a multiple of 16, so whole
+        // groups of 16 are safe; the last row read, kTT + kcap + 13, is staged)
+        for (int i0 = 0; i0 < n; i0 += 16) {
+          double y[kLG + 15];
 #pragma unroll
-          for (int m = 0; m < kLG + 7; ++m) y[m] = Y[(i0 + k_lo - 1 + m) * CG + cc];
+          for (int m = 0; m < kLG + 15; ++m) y[m] = Y[(i0 + k_lo - 1 + m) * CG + cc];
 #pragma unroll
-          for (int d = 0; d < 8; ++d) x[d] = X[(i0 + d) * CG + cc];
+          for (int d = 0; d < 16; ++d) {
+            const double xd = X[(i0 + d) * CG + cc];
 #pragma unroll
-          for (int d = 0; d < 8; ++d)
-#pragma unroll
-            for (int q = 0; q < kLG; ++q) acc[jt][q] = fma(x[d], y[d + q], acc[jt][q]);
+            for (int q = 0; q < kLG; ++q) acc[jt][q] = fma(xd, y[d + q], acc[jt][q]);
+          }
         }
       }
     }
