@@ -77,6 +77,80 @@ __global__ void __launch_bounds__(kMT) lmarg_pos_kernel(const LMargArgs a) {
   }
 }
 
+// ---- transition partials for C <= 24: the same sums, with every thread busy ----
+// 8x8 threads hold 3x3 tiles of the 24x24 pair block (9 FMAs per 6 shared-memory
+// loads); the four 64-thread groups take every fourth staged position, and
+// their partial tiles are added in group order at the end.
+__global__ void __launch_bounds__(kMT) lmarg_tr24_kernel(const LMargArgs a) {
+  constexpr int PB = 24, TS = 32, NG = kMT / 64;
+  __shared__ __align__(16) double xs[TS][PB];
+  __shared__ __align__(16) double ys[TS][PB];
+  __shared__ double fs[TS];
+  __shared__ double red[NG - 1][9][64];
+  const int C = a.C, T = a.T;
+  const int ch = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, grp = tid >> 6, l = tid & 63, tx = l & 7, ty = l >> 3;
+  const int Lb = seq_len(a.lengths, b, T);
+  const int per = (T + a.nchunk - 1) / a.nchunk;
+  const int t_lo = ch * per;
+  const int t_hi = min(t_lo + per, Lb);
+  double acc[3][3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) acc[i][j] = 0.0;
+  const double lz = a.logz[b];
+  const size_t rowb = (size_t)b * (T + 1);
+  for (int t0 = t_lo; t0 < t_hi; t0 += TS) {
+    const int n = min(TS, t_hi - t0);
+    __syncthreads();
+    if (tid < TS) fs[tid] = tid < n ? exp(a.xn[rowb + t0 + tid] + a.yn[rowb + t0 + tid] - lz) : 0.0;
+    __syncthreads();
+    for (int e = tid; e < TS * PB; e += kMT) {
+      const int i = e / PB, q = e % PB;
+      double x = 0.0, y = 0.0;
+      if (i < n && q < C) {
+        const size_t row = (rowb + t0 + i) * C;
+        x = a.xa[row + q] * fs[i];
+        y = a.ya[row + q];
+      }
+      xs[i][q] = x;
+      ys[i][q] = y;
+    }
+    __syncthreads();
+    for (int i = grp; i < n; i += NG) {
+      double xv[3], yv[3];
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        xv[q] = xs[i][ty * 3 + q];
+        yv[q] = ys[i][tx * 3 + q];
+      }
+#pragma unroll
+      for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int q = 0; q < 3; ++q) acc[p][q] = fma(xv[p], yv[q], acc[p][q]);
+    }
+  }
+  if (grp > 0)
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+      for (int q = 0; q < 3; ++q) red[grp - 1][p * 3 + q][l] = acc[p][q];
+  __syncthreads();
+  if (grp > 0) return;
+  double* out = a.part_tr + ((size_t)b * a.nchunk + ch) * C * C;
+#pragma unroll
+  for (int p = 0; p < 3; ++p)
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      double v = acc[p][q];
+#pragma unroll
+      for (int g = 0; g < NG - 1; ++g) v += red[g][p * 3 + q][l];
+      const int cs = ty * 3 + p, cd = tx * 3 + q;
+      if (cs < C && cd < C) out[(size_t)cs * C + cd] = v;
+    }
+}
+
 // ---- transition partials: part_tr[b][chunk][c'][c] = sum_t xa f * ya --------
 // CTA = (pair block, chunk, sequence); 16x16 threads, each a RT x RT tile of
 // a (16 RT) x (16 RT) pair block; positions staged TS at a time.
@@ -473,7 +547,9 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   lmarg_blk_kernel<<<g, kMT, 0, s>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (a.C <= 32) {
+  if (a.C <= 24) {
+    lmarg_tr24_kernel<<<dim3(1, a.nchunk, a.B), kMT, 0, s>>>(a);
+  } else if (a.C <= 32) {
     const int npb = (a.C + 31) / 32;
     lmarg_tr_kernel<2><<<dim3(npb * npb, a.nchunk, a.B), kMT, 0, s>>>(a);
   } else {
