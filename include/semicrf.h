@@ -189,9 +189,13 @@ int semicrf_edge_scan_backward(int64_t B, int64_t N, int64_t K, int64_t C, const
  *    reads, in stream order).
  *  - Calls on one device share that scratch: overlapping calls (different
  *    streams, unordered) race; the caller must order them.
- *  - The first call on a device resolves the scratch address
- *    (cudaGetSymbolAddress) with that device current; make it before
- *    capturing any stream on that device. */
+ *  - Every call looks the scratch address up (cudaGetSymbolAddress) in the
+ *    CUDA context current on the calling thread, so the address always
+ *    belongs to that context (the device's primary context for runtime-API
+ *    callers, or the driver-API context a host made current); nothing is
+ *    cached across calls or contexts.  The first call in a context may load
+ *    the library's device code into it; make that call before capturing any
+ *    stream in that context. */
 int semicrf_forward_noalloc(const semicrf_problem* p, float* partition, void* stream);
 
 const char* semicrf_strerror(int status);

@@ -23,10 +23,10 @@ def _lib():
     return _lib
 
 
-def _problem(B, T, K, C, seed, semiring, gen="default", proj=None):
+def _problem(B, T, K, C, seed, semiring, gen="default", proj=None, kcc=False):
     L = _lib()
     dev = torch.device("cuda:0")
-    inp = make_streaming_inputs(B, T, K, C, seed, gen=gen, proj=proj)
+    inp = make_streaming_inputs(B, T, K, C, seed, gen=gen, proj=proj, kcc=kcc)
     g = torch.Generator().manual_seed(seed + 7)
     lengths = torch.randint(max(1, T // 2), T + 1, (B,), generator=g)
     lengths[0] = T
@@ -54,7 +54,11 @@ def test_noalloc_matches_forward_two_calls(semiring):
     L = _lib()
     cases = [(_problem(4, 300, 40, 24, 11, semiring, gen="cfg2"), "cfg2"),
              (_problem(3, 200, 12, 7, 12, semiring, proj="both"), "proj"),
-             (_problem(2, 150, 64, 256, 13, semiring, gen="cfg4"), "c256")]
+             (_problem(2, 150, 64, 256, 13, semiring, gen="cfg4"), "c256"),
+             # duration-dependent (K, C, C) transitions: their per-duration
+             # factor tables and the blocked chain's overflow flag live in the
+             # same scratch
+             (_problem(3, 90, 12, 8, 14, semiring, kcc=True), "kcc")]
     for prob, what in cases:
         got = _noalloc(prob)
         ref, _, _ = L.forward(prob, want_saved=False)
@@ -97,6 +101,38 @@ def test_noalloc_size_checks_without_gpu():
         want = lib.semicrf_forward(ctypes.byref(big), None, None, 0, None, None, 0, None)
         assert want != L.SEMICRF_OK and lib.semicrf_forward_noalloc(ctypes.byref(big), None,
                                                                     None) == want
+    # (K, C, C) transitions: the per-duration tables grow as K*C*C, so a shape
+    # just past 2 MiB of forward workspace is refused with SEMICRF_ERR_WORKSPACE
+    # (before any device work), and the one just below it is accepted
+    for semiring in (0, 1):
+        C = 16
+        lo, hi = 2, 1024
+        while lo < hi:
+            mid = (lo + hi + 1) // 2
+            p = _shape(C=C, K=mid, transition_ndim=3, semiring=semiring,
+                       checkpoint_interval=max(mid, 1000))
+            if 0 < lib.semicrf_forward_workspace_size(ctypes.byref(p)) <= (2 << 20):
+                lo = mid
+            else:
+                hi = mid - 1
+        ok = _shape(C=C, K=lo, transition_ndim=3, semiring=semiring,
+                    checkpoint_interval=max(lo, 1000))
+        assert 0 < lib.semicrf_forward_workspace_size(ctypes.byref(ok)) <= (2 << 20)
+        assert lib.semicrf_forward_noalloc(ctypes.byref(ok), None, None) == L.SEMICRF_OK
+        # a one-sequence problem, so that the calls get past the empty-batch
+        # return; its pointers are host addresses that are never dereferenced,
+        # because both calls stop at the workspace check, before any CUDA call
+        host = (ctypes.c_double * 4)()
+        addr = ctypes.addressof(host)
+        big = _shape(C=C, K=lo + 1, transition_ndim=3, semiring=semiring,
+                     checkpoint_interval=max(lo + 1, 1000), batch=1, cum_scores=addr,
+                     transition=addr, duration_bias=addr, lengths=addr)
+        assert lib.semicrf_forward_workspace_size(ctypes.byref(big)) > (2 << 20)
+        # semicrf_forward itself accepts the shape (it only lacks a workspace)
+        assert lib.semicrf_forward(ctypes.byref(big), ctypes.c_void_p(addr), None, 0, None,
+                                   None, 0, None) == L.SEMICRF_ERR_WORKSPACE
+        assert lib.semicrf_forward_noalloc(ctypes.byref(big), ctypes.c_void_p(addr),
+                                           None) == L.SEMICRF_ERR_WORKSPACE, semiring
     # shapes the scan rejects get semicrf_forward's code, before any device work
     for kw in [dict(K=0), dict(semiring=7), dict(C=300), dict(batch=2)]:
         p = _shape(**kw)

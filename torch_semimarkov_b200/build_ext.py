@@ -23,33 +23,63 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompil
          "-Xptxas", "-warn-spills"]
 
 
-def _stale() -> bool:
-    if not os.path.exists(LIB):
+def _headers():
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    hs.append(os.path.join(HERE, "..", "include", "semicrf.h"))
+    return [h for h in hs if os.path.exists(h)]
+
+
+def _newer(target: str, deps) -> bool:
+    """True when target is missing or older than any of deps."""
+    if not os.path.exists(target):
         return True
-    t = os.path.getmtime(LIB)
-    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
-    deps.append(os.path.join(HERE, "..", "include", "semicrf.h"))
-    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
-        return LIB
+def build(force: bool = False, verbose: bool = False, jobs: int = 0) -> str:
+    """Compile each stale object (its .cu or a shared header is newer), in
+    parallel, then link the library when any object is newer than it."""
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
+    headers = _headers()
+    objs, todo = [], []
     for src in SOURCES:
+        path = os.path.join(CSRC, src)
         obj = os.path.join(objdir, src.replace(".cu", ".o"))
-        cmd = [NVCC, *ARCH, *FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
-        if verbose:
-            cmd.insert(1, "-Xptxas=-v")
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
         objs.append(obj)
-    tmp = LIB + ".tmp"
-    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"], check=True)
-    os.replace(tmp, LIB)
+        if force or _newer(obj, [path, *headers]):
+            cmd = [NVCC, *ARCH, *FLAGS, "-c", path, "-o", obj + ".tmp"]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            todo.append((cmd, obj))
+    jobs = jobs or max(1, min(len(todo), os.cpu_count() or 1))
+    running = []
+    failed = None
+    for cmd, obj in todo:
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        running.append((subprocess.Popen(cmd), cmd, obj))
+        while len(running) >= jobs:
+            failed = _reap(running) or failed
+    while running:
+        failed = _reap(running) or failed
+    if failed:
+        raise subprocess.CalledProcessError(1, failed)
+    if force or todo or _newer(LIB, objs):
+        tmp = LIB + ".tmp"
+        subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"], check=True)
+        os.replace(tmp, LIB)
     return LIB
+
+
+def _reap(running):
+    """Wait for the oldest compile; returns its command when it failed."""
+    proc, cmd, obj = running.pop(0)
+    if proc.wait() != 0:
+        return cmd
+    os.replace(obj + ".tmp", obj)
+    return None
 
 
 if __name__ == "__main__":

@@ -13,6 +13,19 @@
 
 using namespace semicrf;
 
+int semicrf::device_sm_count() {
+  constexpr int kMaxDev = 64;
+  static int cache[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev < kMaxDev && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;  // no device answer: the B200's count, for planning only
+  if (dev < kMaxDev) cache[dev] = n;
+  return n;
+}
+
 namespace {
 
 constexpr int kP = 8;  // chain block size (chain_block_size)

@@ -244,7 +244,7 @@ __global__ void escan_path_kernel(int B, int N, int K, int C, const int64_t* len
 
 int es_grid(size_t n, int threads) {
   size_t g = (n + threads - 1) / threads;
-  if (g > 148 * 32) g = 148 * 32;
+  if (g > device_sm_count() * 32) g = device_sm_count() * 32;
   return g < 1 ? 1 : (int)g;
 }
 

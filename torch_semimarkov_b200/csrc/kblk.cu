@@ -1116,7 +1116,7 @@ cudaError_t launch_kblk_prep(const float* tr, const float* db, int K, int C, con
   if (e != cudaSuccess) return e;
   const size_t n = (size_t)K * C * C;
   size_t g = (n + 255) / 256;
-  if (g > 148 * 8) g = 148 * 8;
+  if (g > device_sm_count() * 8) g = device_sm_count() * 8;
   kblk_weights_kernel<<<(int)(g < 1 ? 1 : g), 256, 0, s>>>(tr, db, K, C, pr);
   return cudaGetLastError();
 }
@@ -1130,9 +1130,7 @@ cudaError_t launch_kblk_chains(const KccArgs& a, int ndir, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     // a cluster of Q CTAs per chain when the chains alone leave SMs idle and
     // all the clusters fit at once
-    int dev = 0, nsm = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int nsm = device_sm_count();
     const int nchain = a.B * ndir;
     for (int Q = kBMaxQ; Q >= 2; Q /= 2) {
       if (nchain * Q > nsm) continue;
@@ -1187,7 +1185,7 @@ int kblk_tr_slices(int B, int K, int C) {
   int npg, tpb;
   tr_shape(C, npg, tpb);
   const long long per = (long long)npg * ((K + kBP - 1) / kBP);  // CTAs per slice
-  const long long want = 148LL * 2 * 4;                          // four waves of two CTAs per SM
+  const long long want = device_sm_count() * 2LL * 4;                        // four waves of two CTAs per SM
   long long ns = (want + per - 1) / per;
   if (ns < 1) ns = 1;
   // slices cover sequences first, then chunks of each sequence's source blocks
@@ -1199,7 +1197,8 @@ cudaError_t launch_kblk_grads(const KccArgs& a, cudaStream_t s) {
   const int nb = a.T / kBP + 1;
   auto grid = [](size_t n, int t) {
     size_t g = (n + t - 1) / t;
-    if (g > 148 * 16) g = 148 * 16;
+    const size_t gmax = (size_t)device_sm_count() * 16;
+    if (g > gmax) g = gmax;
     return (int)(g < 1 ? 1 : g);
   };
   kblk_anchor_kernel<<<grid((size_t)a.B * nb * a.C, 256), 256, 0, s>>>(a);

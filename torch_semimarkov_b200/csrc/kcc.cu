@@ -767,7 +767,7 @@ __global__ void kcc_reduce_kernel(const KccArgs a, float* grad_tr, float* grad_d
 
 int grid_for(size_t n, int threads) {
   size_t g = (n + threads - 1) / threads;
-  if (g > 148 * 16) g = 148 * 16;
+  if (g > device_sm_count() * 16) g = device_sm_count() * 16;
   return g < 1 ? 1 : (int)g;
 }
 
@@ -809,7 +809,7 @@ KccPrep kcc_prep_carve(double* base, int K, int C, int semiring) {
 int kcc_tr_slices(int B, int K, int C) {
   const int kcap = K - 1;
   const int tiles = ((kcap * C + kTC - 1) / kTC) * ((C + kTR - 1) / kTR);
-  int ns = (2 * 148 + tiles - 1) / tiles;
+  int ns = (2 * device_sm_count() + tiles - 1) / tiles;
   const int bmax = 4 * (B > 0 ? B : 1);
   if (ns > bmax) ns = bmax;
   return ns < 1 ? 1 : ns;

@@ -163,7 +163,7 @@ ChunkPlan chunk_plan(int B, int T, int K, int C, int nroles, int warm_override) 
   if (warm < kcap) warm = kcap;  // the hand-off window must lie in the warm-up
   warm = ((warm + kLP - 1) / kLP) * kLP;
   // as many chunks as idle SMs allow, each at least twice the warm-up long
-  const int sms = 148;
+  const int sms = device_sm_count();
   int nch = sms / (B * nroles);
   const int by_len = T / (2 * warm);
   if (warm_override > 0 && nch < 2) nch = 2;
@@ -195,7 +195,7 @@ cudaError_t launch_chunk_fix(const ChunkFix& f, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const size_t total = (size_t)f.B * (f.T + 1);
   int g = (int)((total + 255) / 256);
-  if (g > 148 * 8) g = 148 * 8;
+  if (g > device_sm_count() * 8) g = device_sm_count() * 8;
   chunk_apply_kernel<<<g, 256, 0, s>>>(f);
   return cudaGetLastError();
 }

@@ -273,7 +273,9 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
   const int sp = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x;
   const int nblk = (T + 1 + kTT - 1) / kTT;
-  // Y rows read by a tile: up to kTT - 8 + (kcap + 7) - 1 + 15 < kTT + kcap + 16
+  // Y rows read by a tile: targets i0 <= kTT - 16 in groups of 16, lag groups
+  // k_lo <= 16*(nkg-1) + 1, window m < kLG + 15, so the last row read is
+  // kTT - 16 + 16*nkg + 14 <= kTT + kcap + 13 < ny
   const int ny = kTT + kcap + 16;
   const int nq = ny / kTT + 2;  // source blocks a tile touches
   double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
@@ -470,23 +472,13 @@ __global__ void __launch_bounds__(kMT) lmarg_reduce_kernel(const LMargArgs a, fl
   }
 }
 
-int sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-      n = 148;
-  }
-  return n;
-}
 
 }  // namespace
 
 LMargPlan lmarg_plan(int B, int T, int K, int C) {
   LMargPlan p{};
   const int kcap = K > 1 ? K - 1 : 1;
-  const int sms = 148;
+  const int sms = device_sm_count();
   // transition partials
   const int pb = C <= 32 ? 32 : 64;
   const int npb = (C + pb - 1) / pb;
@@ -534,7 +526,7 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   const LMargPlan p = lmarg_plan(a.B, a.T, a.K, a.C);
   if (!p.ok || p.nchunk != a.nchunk || p.nsplit != a.nsplit || p.cg != a.cg)
     return cudaErrorInvalidValue;
-  const int gmax = sm_count() * 16;
+  const int gmax = device_sm_count() * 16;
   const size_t n = (size_t)a.B * (a.T + 1) * a.C;
   int g = (int)((n + kMT - 1) / kMT);
   if (g > gmax) g = gmax;

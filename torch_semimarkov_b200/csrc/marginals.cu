@@ -161,7 +161,7 @@ __global__ void reduce_kernel(int B, int n, const float* __restrict__ part,
 
 static int grid_for(size_t n, int bs) {
   size_t g = (n + bs - 1) / bs;
-  if (g > 148 * 16) g = 148 * 16;
+  if (g > device_sm_count() * 16) g = device_sm_count() * 16;
   if (g < 1) g = 1;
   return (int)g;
 }

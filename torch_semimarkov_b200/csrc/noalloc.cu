@@ -27,38 +27,30 @@
 //    Calls that can overlap in time (different streams, or different host
 //    threads without ordering between their streams) race on it; the caller
 //    must order them.
-//  - The first call on a device (with that device current) resolves the
-//    scratch's device address once with cudaGetSymbolAddress, which may load
-//    this library's device code into the context.  Make that first call
-//    before capturing any stream on that device.
-
-#include <mutex>
+//  - Every call resolves the scratch's device address with
+//    cudaGetSymbolAddress in the CUDA context current on the calling thread
+//    (the device's primary context for runtime-API callers, or a driver-API
+//    context that a JNI/cgo host made current).  Module addresses belong to a
+//    context, so nothing is cached across calls: after cudaDeviceReset, or
+//    when the host switches contexts, the address is looked up afresh.  After
+//    the first call in a context this is a host-side table lookup.  The first
+//    call in a context may load this library's device code into it; make that
+//    first call before capturing any stream in that context.
 
 #include "semicrf_internal.cuh"
 
 namespace {
 
 constexpr size_t kNoallocScratchBytes = size_t(2) << 20;
-constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
-
-// Device address of this device's scratch; resolved once per device.
+// Device address of the scratch in the current context.
 int noalloc_scratch(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr)
     return SEMICRF_ERR_CUDA;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr)
-      return SEMICRF_ERR_CUDA;
-    g_noalloc_ptr[dev] = ptr;
-  }
-  *out = g_noalloc_ptr[dev];
+  *out = ptr;
   return SEMICRF_OK;
 }
 

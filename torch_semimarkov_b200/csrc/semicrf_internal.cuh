@@ -158,6 +158,9 @@ struct LChainLaunch {
   LChainArgs a0;
   LChainArgs a1;
 };
+// Number of SMs of the current device (cudaDevAttrMultiProcessorCount),
+// cached per device index; launch planning sizes grids and time chunks by it.
+int device_sm_count();
 cudaError_t launch_lchain(const LChainLaunch& L, int grid, cudaStream_t s);
 // warp-specialised variant for C <= 64, whole-sequence chains (mode 0) only
 cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s);

@@ -42,7 +42,8 @@ inline bool vplan(VPlan& p, int B, int C, int K) {
   const size_t shared = 4 * (size_t)(p.kcap + 1) * C;  // duration bias table
   const size_t per_warp = 17 * (size_t)p.R * C;        // (sv, cum) ring (twice) + argmax ring
   // spread small batches over the SMs: about one warp per SM sub-partition
-  int wpb = (B + 147) / 148;
+  const int nsm = device_sm_count();
+  int wpb = (B + nsm - 1) / nsm;
   if (wpb < 1) wpb = 1;
   if (wpb > kVMaxWarps) wpb = kVMaxWarps;
   while (wpb > 1 && shared + wpb * per_warp > kVSmemMax) --wpb;
