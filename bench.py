@@ -1,19 +1,25 @@
 """Benchmark of the streaming semi-CRF scan on B200 (one JSON line on rank 0).
 
-Workload ("batched genomic-window training"): per rank a
+Workload ("batched genomic-window training"): a global
 batch of B=64 sequences, T=10,000, C=24, K=300, lengths uniform in
 [8000, 10000]; cum_scores = prefix sums of N(0,1)/sqrt(C) emissions,
 transition / duration_bias ~ N(0, 0.1^2); one step = log-semiring forward +
 backward (partition.sum().backward()) through ``semi_crf_streaming_forward``,
 plus (N > 1) the NCCL all-reduce of [grad_transition | grad_duration_bias |
-loss].  Metric: fwd+bwd positions/s = ranks * B * T / step time (the
-reference's definition, benchmarks/benchmark_streaming_scale.py:191-193).
+loss].  Metric: fwd+bwd positions/s = B * T / step time (the reference's
+definition, benchmarks/benchmark_streaming_scale.py:191-193).
+
+Scaling is strong: the same global batch is split over the N ranks (32/16/8
+sequences per GPU at N = 2/4/8, longest first to the least-loaded rank), and
+the step time is the maximum over ranks.  At N > 1 a "weak" sub-object also
+reports B=64 sequences per rank.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 ``--impl reference`` times the reference algorithm on the host CPU (the
 float32 oracle port of streaming/pytorch_reference.py, all host threads) on a
-bounded sample of the same workload.
+bounded sample of the same workload, by the slope method (two sequence
+lengths past the K ramp; their time difference is the steady-state cost).
 """
 
 from __future__ import annotations
@@ -167,59 +173,138 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# reference arm: the float32 oracle port of the reference algorithm on the host
+# CPU legs: the float32 oracle port of the reference algorithm (the reference
+# arm) and the reference's own PyTorch path, timed on the host cores
 # ---------------------------------------------------------------------------
-def cpu_reference_sample(budget_s: float):
-    """Time the reference algorithm (float32 oracle, all host threads) on a
-    bounded sample of the configuration-2 workload.  Returns (pos/s, info)."""
-    import numpy as np
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+class PortSample:
+    """Steady-state fwd+bwd rate of the float32 oracle port on all host threads,
+    by the slope method: B = threads sequences of configuration 2 at lengths T1
+    and T2 (both past the K-1 ramp); one sample = B * (T2 - T1) positions in
+    t(T2) - t(T1) seconds.  The thread count is passed explicitly, because
+    torchrun sets OMP_NUM_THREADS=1."""
+
+    def __init__(self, T1=400, T2=800):
+        import numpy as np
+
+        from inputs import make_streaming_inputs
+        from oracle import oracle
+
+        oracle.build()
+        self.np, self.oracle = np, oracle
+        self.threads = host_threads()
+        self.B, self.T1, self.T2 = self.threads, T1, T2
+        inp = make_streaming_inputs(self.B, T2, K, C, seed=2, gen="cfg2")
+        self.cum = inp["cum_scores"].numpy()
+        self.tr = inp["transition"].numpy()
+        self.db = inp["duration_bias"].numpy()
+        self.sample = (f"float32 oracle port, B={self.B} (one sequence per thread), K={K}, "
+                       f"C={C}, fwd+bwd at T={T1} and T={T2}, slope")
+
+    def _run(self, Tn):
+        np = self.np
+        t0 = time.perf_counter()
+        self.oracle.forward_backward(self.cum[:, : Tn + 1], self.tr, self.db,
+                                     np.full(self.B, Tn), K, dtype=np.float32,
+                                     threads=self.threads)
+        return time.perf_counter() - t0
+
+    def step(self):
+        """(positions, seconds) of one slope sample."""
+        return self.B * (self.T2 - self.T1), self._run(self.T2) - self._run(self.T1)
+
+
+def reference_pytorch_sample(T1=300, T2=340, Bs=64, budget_s=120.0):
+    """The reference's own CPU streaming path (torch_semimarkov 0.2.0 installed
+    offline in baseline/_ref, ``semi_crf_streaming_forward(..., use_triton=False)``
+    forward + backward, float32, torch on all host threads) on configuration 2's
+    inputs, by the slope method: B=64 at T1 and T2 just past the K-1 ramp,
+    after a short warm-up call.  Its Python loop dispatches about ten torch
+    ops per (position, duration) whatever the batch, so each length costs tens
+    of seconds; if T1 alone exceeds budget_s the rate is B*T1/t(T1), which
+    includes the cheaper ramp and so overstates the steady state.  Returns
+    None when the reference is not installed."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "torch_semimarkov")):
+        return None
+    import torch
+
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from torch_semimarkov.streaming import semi_crf_streaming_forward as ref_forward
 
     from inputs import make_streaming_inputs
-    from oracle import oracle
 
-    oracle.build()
-    threads = oracle.max_threads()
-    Ts = 600
-    Bs = threads
-    inp = make_streaming_inputs(Bs, Ts, K, C, seed=2, gen="cfg2")
-    lengths = np.full(Bs, Ts)
-    args = (inp["cum_scores"].numpy(), inp["transition"].numpy(), inp["duration_bias"].numpy(),
-            lengths, K)
-    t0 = time.perf_counter()
-    oracle.forward_backward(*args, dtype=np.float32, threads=threads)
-    dt = time.perf_counter() - t0
-    return Bs * Ts / dt, {"threads": threads, "sample": f"B={Bs} T={Ts} K={K} C={C} fwd+bwd "
-                                                        "(float32 oracle port, steady-state "
-                                                        "truncated T)", "seconds": dt,
-                          "fn": lambda: oracle.forward_backward(*args, dtype=np.float32,
-                                                                threads=threads),
-                          "positions": Bs * Ts}
+    threads = host_threads()
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        inp = make_streaming_inputs(Bs, T2, K, C, seed=2, gen="cfg2")
+
+        def run(Tn):
+            cum = inp["cum_scores"][:, : Tn + 1].clone().requires_grad_(True)
+            tr = inp["transition"].clone().requires_grad_(True)
+            db = inp["duration_bias"].clone().requires_grad_(True)
+            t0 = time.perf_counter()
+            ref_forward(cum, tr, db, torch.full((Bs,), Tn), K, use_triton=False).sum().backward()
+            return time.perf_counter() - t0
+
+        run(8)  # warm-up: torch's lazy initialisation of the ops involved
+        t1 = run(T1)
+        t2 = run(T2) if t1 <= budget_s else None
+    finally:
+        torch.set_num_threads(old)
+    base = (f"reference PyTorch path (torch_semimarkov 0.2.0, use_triton=False), float32, "
+            f"B={Bs}, K={K}, C={C}, fwd+bwd")
+    if t2 is not None and t2 - t1 > 0.1 * t1:
+        return {"value": Bs * (T2 - T1) / (t2 - t1), "unit": UNIT, "cores": threads,
+                "kind": "reference",
+                "sample": f"{base} at T={T1} and T={T2}, slope ({t1:.1f} s and {t2:.1f} s)"}
+    return {"value": Bs * T1 / t1, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{base} at T={T1} ({t1:.1f} s), one point: includes the K-1 ramp, "
+                      "which overstates the steady-state rate"}
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    rate, info = cpu_reference_sample(budget_s=10)
+    ps = PortSample()
     for _ in range(args.warmup):
-        pass  # the calibration call above is the warm-up
-    times = []
+        ps.step()
+    pos = secs = 0.0
     for _ in range(args.steps):
-        t0 = time.perf_counter()
-        info["fn"]()
-        times.append(time.perf_counter() - t0)
-    step = statistics.mean(times)
-    value = info["positions"] / step
+        n, dt = ps.step()
+        pos += n
+        secs += dt
+    value = pos / secs
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": B * T / value * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"cfg2 sample ({info['sample']})", "B": B, "T": T, "K": K, "C": C},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": info["threads"],
-                         "kind": "port", "sample": info["sample"]},
+        "config": {"workload": f"cfg2 genomic windows (B={B} T={T} K={K} C={C}), sampled: "
+                               f"{ps.sample}", "global_batch": B, "seq_len": T, "K": K, "C": C},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": ps.threads, "kind": "port",
+                         "sample": ps.sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "ms_per_step extrapolates the sampled steady-state rate to one full "
+                "configuration-2 step",
     }
+    if args.gpus == 1:
+        # the reference's own PyTorch code beside the port (informational)
+        try:
+            ref_pt = reference_pytorch_sample()
+        except Exception as exc:
+            ref_pt = {"unavailable": f"{type(exc).__name__}: {exc}"}
+        if ref_pt:
+            line["cpu_baseline_reference_pytorch"] = ref_pt
     print(json.dumps(line), flush=True)
 
 
@@ -227,7 +312,7 @@ def run_reference(args):
 # B200 arm
 # ---------------------------------------------------------------------------
 def profiled_traffic():
-    """DRAM bytes (read + write) per launch of the dominant kernel from the
+    """DRAM bytes (read + write) per launch of the dominant kernel at B=64 from the
     committed ncu summary (profiles/lchain_ws_kernel_cfg2.txt), or None."""
     try:
         for line in open(os.path.join(ROOT, "profiles", "lchain_ws_kernel_cfg2.txt")):
@@ -238,15 +323,53 @@ def profiled_traffic():
     return None
 
 
-def make_workload(rank, device):
-    import torch
-
+def global_workload(Bg, Tg, seed=2):
+    """Configuration 2's global batch (CPU tensors): every rank generates the
+    same one and keeps its shard."""
     from inputs import config_lengths, make_streaming_inputs
 
-    inp = make_streaming_inputs(B, T, K, C, seed=2 + 1000 * rank, gen="cfg2")
-    lengths = config_lengths("cfg2", B, T, seed=2 + 1000 * rank)
-    return (inp["cum_scores"], inp["transition"].to(device), inp["duration_bias"].to(device),
-            lengths)
+    inp = make_streaming_inputs(Bg, Tg, K, C, seed=seed, gen="cfg2")
+    lengths = config_lengths("cfg2", Bg, Tg, seed=seed)
+    return inp["cum_scores"], inp["transition"], inp["duration_bias"], lengths
+
+
+def fp64_probe(dev):
+    """Measured float64 FMA peak of this GPU (TFLOP/s, all SMs, 8 independent
+    chains per thread) and the cycles of one dependent float64 FMA."""
+    import ctypes
+
+    import torch
+
+    path = os.path.join(ROOT, "torch_semimarkov_b200", "libsemicrf_probe.so")
+    lib = ctypes.CDLL(path)
+    lib.semicrf_probe_fp64_fma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                           ctypes.c_void_p]
+    lib.semicrf_probe_fp64_latency.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_void_p]
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    grid, iters, nt = nsm * 8, 4096, 256
+    out = torch.empty(grid * nt, dtype=torch.float64, device=dev)
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    best = None
+    for _ in range(4):
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        assert lib.semicrf_probe_fp64_fma(grid, iters, ctypes.c_void_p(out.data_ptr()), st) == 0
+        b_.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b_)
+        best = ms if best is None else min(best, ms)
+    fmas = grid * nt * iters * 32
+    cyc = torch.zeros(1, dtype=torch.int64, device=dev)
+    o32 = torch.empty(32, dtype=torch.float64, device=dev)
+    assert lib.semicrf_probe_fp64_latency(1024, ctypes.c_void_p(cyc.data_ptr()),
+                                          ctypes.c_void_p(o32.data_ptr()), st) == 0
+    torch.cuda.synchronize()
+    return {"fp64_tflops": 2 * fmas / (best / 1e3) / 1e12,
+            "dfma_latency_cycles": float(cyc) / (1024 * 16),
+            "how": f"{grid} CTAs x {nt} threads x 8 independent FMA chains x {iters * 4} "
+                   "FMAs, best of 4, CUDA events (probe.cu); latency: one warp, one chain, "
+                   "clock64"}
 
 
 def main():
@@ -260,7 +383,7 @@ def main():
     import torch.distributed as dist
 
     from torch_semimarkov_b200 import _lib, semi_crf_streaming_forward
-    from torch_semimarkov_b200.distributed import SharedGradReducer
+    from torch_semimarkov_b200.distributed import SharedGradReducer, shard_sequences
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -274,7 +397,7 @@ def main():
         if rank == 0:
             flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
             print(json.dumps(bench_fwd_bwd(
-                dev, flush, "cfg2", B, T, K, C,
+                dev, flush, "cfg2", B, T, K, C, 2,
                 f"cfg2 shape with (K, C, C) transitions: B={B} T={T} K={K} C={C}", kcc=True)),
                 flush=True)
         return
@@ -284,32 +407,49 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    cum_host, tr, db, lengths_h = make_workload(rank, dev)
+    # ---- this rank's shard of the global batch (strong scaling) ----
+    cum_all, tr_h, db_h, len_all = global_workload(B, T)
+    mine = shard_sequences(len_all, world, rank)
+    Bl = int(mine.numel())
+    cum_host = cum_all[mine].contiguous()
+    lengths_h = len_all[mine].contiguous()
+    del cum_all
+    tr, db = tr_h.to(dev), db_h.to(dev)
     cum_pinned = cum_host.pin_memory()
     cum = cum_host.to(dev)
     lengths = lengths_h.to(dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     reducer = SharedGradReducer(C, K, dev)
 
-    def step(cum_in):
-        cum_l = cum_in.detach().requires_grad_(True)
-        tr_l = tr.detach().requires_grad_(True)
-        db_l = db.detach().requires_grad_(True)
-        part = semi_crf_streaming_forward(cum_l, tr_l, db_l, lengths, K)
-        loss = part.sum()
-        loss.backward()
-        if world > 1:
-            # the step's one collective: [grad_tr | grad_db | loss] summed over ranks
-            gt, gd, lsum = reducer(tr_l.grad, db_l.grad, loss)
-            return lsum, gt, gd
-        return loss, tr_l.grad, db_l.grad
+    def make_step(lengths_d):
+        def step(cum_in):
+            cum_l = cum_in.detach().requires_grad_(True)
+            tr_l = tr.detach().requires_grad_(True)
+            db_l = db.detach().requires_grad_(True)
+            part = semi_crf_streaming_forward(cum_l, tr_l, db_l, lengths_d, K)
+            loss = part.sum()
+            loss.backward()
+            if world > 1:
+                # the step's one collective: [grad_tr | grad_db | loss] summed over ranks
+                gt, gd, lsum = reducer(tr_l.grad, db_l.grad, loss)
+                return lsum, gt, gd
+            return loss, tr_l.grad, db_l.grad
+        return step
+
+    step = make_step(lengths)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(max(args.warmup, 1)):
+    def max_over_ranks(x):
+        tt = torch.tensor([x], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt)
+
+    for _ in range(max(args.warmup, 3)):
         step(cum)
     barrier()
 
@@ -326,13 +466,8 @@ def main():
         evs[i][1].record()
     barrier()
     clocks = sampler.stop()
-    ms = [a.elapsed_time(b) for a, b in evs]
-    t_step = statistics.mean(ms) / 1e3
-    tt = torch.tensor([t_step], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    t_step = float(tt)
-    value = world * B * T / t_step
+    t_step = max_over_ranks(statistics.mean(a.elapsed_time(b_) for a, b_ in evs) / 1e3)
+    value = B * T / t_step
 
     # ---- end to end: pinned host -> device, fwd+bwd, result -> host ----
     # As a data loader runs it: a copy stream uploads step i+1's cum_scores
@@ -341,13 +476,13 @@ def main():
     out_host = torch.empty(2, C * C + K * C + 1, dtype=torch.float32).pin_memory()
     bufs = [cum, torch.empty_like(cum)]
     copy_stream = torch.cuda.Stream(device=dev)
-    main = torch.cuda.current_stream(dev)
+    main_s = torch.cuda.current_stream(dev)
     uploaded = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
 
     def pipeline(n):
         # step 0's upload is exposed; steps 1.. upload behind the previous step
-        copy_stream.wait_stream(main)
+        copy_stream.wait_stream(main_s)
         with torch.cuda.stream(copy_stream):
             bufs[0].copy_(cum_pinned, non_blocking=True)
             uploaded[0].record(copy_stream)
@@ -360,31 +495,35 @@ def main():
                         copy_stream.wait_event(consumed[nxt])  # step i-1 is done with it
                     bufs[nxt].copy_(cum_pinned, non_blocking=True)
                     uploaded[nxt].record(copy_stream)
-            main.wait_event(uploaded[cur])
+            main_s.wait_event(uploaded[cur])
             loss, gt, gd = step(bufs[cur])
             res = torch.cat([gt.flatten(), gd.flatten(), loss.detach().view(1)])
             out_host[cur].copy_(res, non_blocking=True)
-            consumed[cur].record(main)
+            consumed[cur].record(main_s)
 
     pipeline(3)  # untimed: warms the second buffer and the allocator's blocks for it
     n_e2e = max(10, args.steps)
     flush.zero_()
     barrier()
     a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(main)
+    a.record(main_s)
     pipeline(n_e2e)
-    b_.record(main)
+    b_.record(main_s)
     torch.cuda.synchronize()
-    te = torch.tensor([a.elapsed_time(b_) / n_e2e / 1e3], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * T / float(te)
+    te = max_over_ranks(a.elapsed_time(b_) / n_e2e / 1e3)
+    e2e_value = B * T / te
     del bufs
 
     # ---- the kernels of one step, timed alone: the forward launch (alpha and
     # beta chains side by side, the dominant kernel) and the backward kernels
     prob = _lib.Problem(cum, tr, db, lengths, K, "log")
-    gout = torch.ones(B, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    import ctypes
+
+    p_off = _lib.SemicrfProblem.from_buffer_copy(prob.c)
+    p_off.chunk_warmup = -1
+    chunked = lib.semicrf_saved_size(prob.cref) > lib.semicrf_saved_size(ctypes.byref(p_off))
+    gout = torch.ones(Bl, dtype=torch.float32, device=dev)
     saved = None
     for _ in range(2):
         _, _, saved = _lib.forward(prob, want_saved=True)
@@ -404,24 +543,56 @@ def main():
     t_bwd = statistics.mean(e[2].elapsed_time(e[3]) for e in fe) / 1e3
     del saved
 
+    # ---- weak scaling beside it (N > 1): B=64 sequences per rank ----
+    weak = None
+    if world > 1:
+        cw, _, _, lw = global_workload(B, T, seed=2 + 1000 * rank)
+        cw, lw = cw.to(dev), lw.to(dev)
+        step_w = make_step(lw)
+        for _ in range(3):
+            step_w(cw)
+        barrier()
+        ew = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(10)]
+        for e0, e1 in ew:
+            flush.zero_()
+            e0.record()
+            step_w(cw)
+            e1.record()
+        barrier()
+        tw = max_over_ranks(statistics.mean(x.elapsed_time(y) for x, y in ew) / 1e3)
+        weak = {"metric": METRIC, "value": world * B * T / tw, "unit": UNIT,
+                "ms_per_step": tw * 1e3, "scaling": "weak",
+                "config": f"B={B} sequences per rank (global {world * B}), 10 steps"}
+        del cw
+
+    probe = fp64_probe(dev)
+
     viterbi = None
     others = {}
-    if not args.no_viterbi and rank == 0:
+    if not args.no_viterbi and world == 1:
         viterbi = bench_viterbi(dev, flush)
-        others["chromosome"] = bench_fwd_bwd(dev, flush, "cfg3", 1, 1_000_000, 1000, 8,
+        others["head_cfg1"] = bench_head_cfg1(dev, flush)
+        others["chromosome"] = bench_fwd_bwd(dev, flush, "cfg3", 1, 1_000_000, 1000, 8, 3,
                                              "cfg3: B=1 T=1e6 K=1000 C=8, one GPU")
-        others["large_C"] = bench_fwd_bwd(dev, flush, "cfg4", 32, 4096, 64, 256,
+        others["large_C"] = bench_fwd_bwd(dev, flush, "cfg4", 32, 4096, 64, 256, 4,
                                           "cfg4: B=32 T=4096 K=64 C=256")
         others["duration_transitions"] = bench_fwd_bwd(
-            dev, flush, "cfg2", 64, 10000, 300, 24,
+            dev, flush, "cfg2", 64, 10000, 300, 24, 2,
             "cfg2 shape with (K, C, C) duration-dependent transitions ~N(0, 0.1^2): "
             "B=64 T=10000 K=300 C=24", kcc=True)
 
-    cpu = None
+    cpu = cpu_ref = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, info = cpu_reference_sample(budget_s=10)
-        cpu = {"value": rate, "unit": UNIT, "cores": info["threads"], "kind": "port",
-               "sample": info["sample"]}
+        ps = PortSample()
+        ps.step()  # warm
+        n, dt = ps.step()
+        cpu = {"value": n / dt, "unit": UNIT, "cores": ps.threads, "kind": "port",
+               "sample": ps.sample}
+        try:
+            cpu_ref = reference_pytorch_sample()
+        except Exception as exc:  # the reference leg is informational
+            cpu_ref = {"unavailable": f"{type(exc).__name__}: {exc}"}
 
     if world > 1:
         torch.cuda.synchronize()
@@ -437,77 +608,105 @@ def main():
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    # algorithmic bytes of one forward launch over the actual lengths (rows
-    # 0..L of each sequence): cum_scores read by each of the two chains, their
-    # float64 tables written (2C+1 doubles per row and chain), log Z and the
-    # partition written
+    # Algorithmic bytes of one forward launch (the survey's per-position
+    # figures, over this rank's actual lengths): the cum_scores stream read
+    # once per pass (alpha and beta chains: 2 x 4C bytes per row) plus the
+    # reference's ring checkpoints, K*C*4/S bytes per position.  The float64
+    # tables this design writes for its parallel backward are reported apart
+    # as design_bytes.
     lsum = int(lengths_h.sum())
-    rows = lsum + B
-    bytes_fwd = 2 * (4 * C + 8 * (2 * C + 1)) * rows + B * (4 + 8)
-    achieved = bytes_fwd / t_fwd / 1e9
+    rows = lsum + Bl
+    S = max(K, int(math.sqrt(T * K)))
+    bytes_alg = 2 * 4 * C * rows + lsum * K * C * 4 / S
+    design_bytes = 2 * 8 * (2 * C + 1) * rows + Bl * (4 + 8)
+    achieved = bytes_alg / t_fwd / 1e9
+    traffic = profiled_traffic()
+    if traffic is not None:
+        # the capture was of the B=64 launch; a shard's launch moves the same
+        # bytes per row
+        traffic *= rows / (int(len_all.sum()) + len(len_all))
     # float64 FMAs of the factorised recurrence per forward launch: per
     # position and chain, the C x C mat-vec and the (K-1) x C duration sums
     kcap = max(K - 1, 1)
     fmas = 2 * lsum * (C * C + kcap * C)
-    traffic = profiled_traffic()
+    fp64_tf = 2 * fmas / t_fwd / 1e12
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    launches_fwd = 4 + (7 if chunked else 0)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"cfg2 genomic windows: per rank B={B} T={T} K={K} C={C}, "
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"cfg2 genomic windows: global B={B} T={T} K={K} C={C}, "
                                "lengths U[0.8T,T], log fwd+bwd (float32 in/out, float64 "
-                               "arithmetic)",
-                   "global_batch": B * world, "seq_len": T, "K": K, "C": C,
-                   "parallelism": f"dp{world} (batch-sharded, weak)",
+                               "arithmetic), batch split over the ranks",
+                   "global_batch": B, "per_rank_batch": Bl, "seq_len": T, "K": K, "C": C,
+                   "parallelism": f"dp{world} (batch-sharded, strong)",
+                   "time_chunked": bool(chunked),
                    "l2": "flushed (256 MiB write) between timed steps"},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * (T + 1) * C,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * Bl * (T + 1) * C,
                 "d2h_bytes_per_step": 4 * (C * C + K * C + 1),
-                "note": "pinned uploads on a copy stream, double-buffered against compute; every timed step uploads its own inputs (step 0 exposed)"},
+                "note": "per rank: pinned uploads of its shard on a copy stream, "
+                        "double-buffered against compute; every timed step uploads its own "
+                        "inputs (step 0 exposed); max over ranks"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
                      "peak_source": peak_src,
-                     "kernel": "lchain_ws_kernel<32,8>: alpha and beta chains, 2B CTAs",
+                     "algorithmic_bytes_per_launch": bytes_alg,
+                     "design_bytes_per_launch": design_bytes,
+                     "kernel": "lchain_ws_kernel<32,8>: alpha and beta chains"
+                               + (" in time chunks" if chunked else ", 2B CTAs"),
                      "kernel_ms": t_fwd * 1e3, "backward_kernels_ms": t_bwd * 1e3,
-                     "note": "HBM is not binding: each chain is a serial recurrence over T "
-                             "(one CTA per chain), bound by its per-position latency; see "
+                     "note": "algorithmic bytes per the survey: 4C per row and pass of the "
+                             "cum_scores stream plus K*C*4/S checkpoint bytes per position; "
+                             "HBM is not binding (each chain is a serial recurrence); see "
                              "compute_roofline"},
-        "compute_roofline": {"fp64_fma_per_launch": fmas,
-                             "achieved_fp64_tflops": 2 * fmas / t_fwd / 1e12,
-                             "ns_per_position_step": t_fwd / T * 1e9,
-                             "ctas": 2 * B, "sms": torch.cuda.get_device_properties(dev)
-                             .multi_processor_count},
+        "compute_roofline": {"bound": "fp64", "unit": "TFLOP/s",
+                             "fp64_fma_per_launch": fmas, "achieved": fp64_tf,
+                             "peak": probe["fp64_tflops"], "frac": fp64_tf / probe["fp64_tflops"],
+                             "peak_source": "measured in this run: " + probe["how"],
+                             "dfma_latency_cycles": probe["dfma_latency_cycles"],
+                             "ns_per_position_step": t_fwd / int(lengths_h.max()) * 1e9,
+                             "ctas": 2 * Bl, "sms": nsm,
+                             "note": "the factorised recurrence's float64 FMAs (C*C + (K-1)*C "
+                                     "per position and chain) over the forward launch time"},
         # the reference's O(T K C^2) formulation does (K-1) C^2 semiring edge
         # terms per position and pass, four passes per fwd+bwd (forward, alpha
         # recompute, beta, marginals); this is the rate at which the same
         # result is produced in those units (not work this build executes)
         "reference_equivalent": {"edge_terms_per_position_pass": kcap * C * C, "passes": 4,
                                  "edge_terms_per_s": 4 * kcap * C * C * B * T / t_step},
-        # per step: forward = prep (2) + chains (1) + chain_fix (returns at once
-        # unless a clamp clipped); backward = pos, blk, tr, db, db_fix (returns at
-        # once unless a sequence was flagged), reduce
-        "gpu_launches": 10 * args.steps,
+        # per step: forward = prep_max, prep, chains, chain_fix (returns at once
+        # unless a clamp clipped), and when time-chunked the boundary check,
+        # prefix and fix-up per direction and the rerun of unjoined sequences;
+        # backward = pos, blk, tr, db, db_fix (returns at once unless a sequence
+        # was flagged), reduce
+        "gpu_launches": (launches_fwd + 6) * args.steps,
         "clocks": clocks,
     }
+    if weak:
+        line["weak"] = weak
     if viterbi:
         line["viterbi"] = viterbi
     line.update(others)
     if cpu:
         line["cpu_baseline"] = cpu
+    if cpu_ref:
+        line["cpu_baseline_reference_pytorch"] = cpu_ref
     print(json.dumps(line), flush=True)
 
 
-def bench_fwd_bwd(dev, flush, gen, Bc, Tc, Kc, Cc, label, kcc=False):
+def bench_fwd_bwd(dev, flush, gen, Bc, Tc, Kc, Cc, seed, label, kcc=False):
     """fwd+bwd positions/s of another configuration (inputs resident)."""
     import torch
 
     from inputs import config_lengths, make_streaming_inputs
     from torch_semimarkov_b200 import semi_crf_streaming_forward
 
-    inp = make_streaming_inputs(Bc, Tc, Kc, Cc, seed=3, gen=gen, kcc=kcc)
+    inp = make_streaming_inputs(Bc, Tc, Kc, Cc, seed=seed, gen=gen, kcc=kcc)
     cum = inp["cum_scores"].to(dev)
     tr = inp["transition"].to(dev)
     db = inp["duration_bias"].to(dev)
-    lengths = torch.full((Bc,), Tc, dtype=torch.int64, device=dev)
+    lengths = config_lengths(gen, Bc, Tc, seed=seed).to(dev)
 
     def one():
         c = cum.detach().requires_grad_(True)
@@ -529,6 +728,51 @@ def bench_fwd_bwd(dev, flush, gen, Bc, Tc, Kc, Cc, label, kcc=False):
     t = statistics.mean(ms) / 1e3
     return {"metric": "fwd+bwd positions/s", "value": Bc * Tc / t, "unit": UNIT,
             "ms": t * 1e3, "config": label}
+
+
+def bench_head_cfg1(dev, flush):
+    """Configuration 1 through the public module: SemiMarkovCRFHead(24, 100,
+    hidden_dim=512) with a Xavier-initialised projection; one step =
+    compute_loss (projection, cumsum, partition, gold score) + backward +
+    decode_with_traceback, B=4, T=1000."""
+    import torch
+
+    from inputs import make_hidden
+    from torch_semimarkov_b200 import SemiMarkovCRFHead
+
+    Bh, Th, Kh, Ch, H = 4, 1000, 100, 24, 512
+    h = make_hidden(Bh, Th, Ch, Kh, seed=1, gen="cfg1", hidden_dim=H)
+    head = SemiMarkovCRFHead(Ch, Kh, hidden_dim=H).to(dev)
+    with torch.no_grad():
+        head.transition.copy_(h["transition"])
+        head.duration_dist.duration_bias.copy_(h["duration_bias"])
+        head.projection.weight.copy_(h["proj_weight"])
+        head.projection.bias.copy_(h["proj_bias"])
+    hidden = h["hidden"].to(dev)
+    labels = h["labels"].to(dev)
+    lengths = torch.full((Bh,), Th, dtype=torch.int64, device=dev)
+
+    def one():
+        head.zero_grad(set_to_none=True)
+        head.compute_loss(hidden, lengths, labels).backward()
+        return head.decode_with_traceback(hidden, lengths)
+
+    for _ in range(3):
+        one()
+    ms = []
+    for _ in range(5):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        one()
+        torch.cuda.synchronize()
+        ms.append((time.perf_counter() - t0) * 1e3)
+    t = statistics.median(ms) / 1e3
+    return {"metric": "head positions/s (compute_loss + backward + decode_with_traceback)",
+            "value": Bh * Th / t, "unit": UNIT, "ms": t * 1e3,
+            "config": "cfg1: SemiMarkovCRFHead(24, 100, hidden_dim=512), B=4 T=1000, "
+                      "host wall clock around each step (decode_with_traceback returns "
+                      "host Segment lists)"}
 
 
 def bench_viterbi(dev, flush):

@@ -2,7 +2,8 @@
 
 Run once, in the container where the reference is mounted:
 
-    PYTHONPATH=/path/to/torch-semimarkov/src python tests/golden/make_golden.py [case ...]
+    TORCH_SEMIMARKOV_REF_SRC=/path/to/torch-semimarkov/src \
+        python tests/golden/make_golden.py [case ...]
 
 It imports the reference package (torch-semimarkov 0.2.0) and runs its CPU
 PyTorch path -- ``semi_crf_streaming_forward(..., use_triton=False)`` with
@@ -36,7 +37,11 @@ from inputs import (  # noqa: E402
     make_streaming_inputs,
 )
 
-REF_SRC = os.environ.get("TORCH_SEMIMARKOV_REF_SRC", "/root/reference/src")
+# the reference's source tree (its src/ directory) must be named explicitly
+REF_SRC = os.environ.get("TORCH_SEMIMARKOV_REF_SRC")
+if not REF_SRC:
+    sys.exit("set TORCH_SEMIMARKOV_REF_SRC to the reference's src/ directory "
+             "(the one holding the torch_semimarkov package)")
 if REF_SRC not in sys.path:
     sys.path.insert(0, REF_SRC)
 

@@ -15,6 +15,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libsemicrf.so")
+# device-rate probes for bench.py's roofline denominators (not part of the scan)
+PROBE_LIB = os.path.join(HERE, "libsemicrf_probe.so")
+PROBE_SOURCES = ["probe.cu"]
 SOURCES = ["api.cu", "chain.cu", "lchain.cu", "lchain_ws.cu", "lchain_fix.cu", "lchain_cl.cu", "lchunk.cu", "lmarg.cu", "marginals.cu", "viterbi.cu", "vchain.cu", "kcc.cu", "kblk.cu", "escan.cu", "gold.cu",
            "noalloc.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -70,6 +73,12 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 0) -> str:
         tmp = LIB + ".tmp"
         subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"], check=True)
         os.replace(tmp, LIB)
+    srcs = [os.path.join(CSRC, f) for f in PROBE_SOURCES]
+    if force or _newer(PROBE_LIB, srcs):
+        tmp = PROBE_LIB + ".tmp"
+        subprocess.run([NVCC, *ARCH, *FLAGS, "-shared", "-o", tmp, *srcs, "-lcudart"],
+                       check=True)
+        os.replace(tmp, PROBE_LIB)
     return LIB
 
 
