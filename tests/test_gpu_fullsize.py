@@ -36,11 +36,12 @@ def _dev():
 def _inputs(g, gen):
     B, T, K, C = (int(g[k]) for k in ("B", "T", "K", "C"))
     inp = make_streaming_inputs(B, T, K, C, seed=int(g["seed"]), gen=gen)
-    np.testing.assert_allclose(checksum(inp["cum_scores"]), g["cum_checksum"], rtol=0, atol=0)
-    if "tr_checksum" in g:
-        np.testing.assert_allclose(checksum(inp["transition"]), g["tr_checksum"], rtol=0, atol=0)
-        np.testing.assert_allclose(checksum(inp["duration_bias"]), g["db_checksum"], rtol=0,
-                                   atol=0)
+    # the checksums are float64 sums over up to 10^7 elements, whose
+    # parallel summation order differs between host CPUs by an ulp or two
+    for key, name in (("cum_scores", "cum_checksum"), ("transition", "tr_checksum"),
+                      ("duration_bias", "db_checksum")):
+        if name in g:
+            np.testing.assert_allclose(checksum(inp[key]), g[name], rtol=1e-12, atol=0)
     return inp, config_lengths(gen, B, T, seed=int(g["seed"]))
 
 

@@ -544,3 +544,49 @@ def test_chunked_chains_large_scale_vs_oracle(oracle, monkeypatch):
     inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
            "proj_end": None}
     _check_vs_oracle(inp, np.array([T]), np.array([1.0]), K, "log", oracle)
+
+
+@pytest.mark.parametrize("proj", [None, "both"])
+def test_backward_launcher_raw(proj, oracle):
+    """launch_streaming_triton_kernel -> launch_streaming_triton_backward called
+    as the reference's raw-launcher tests call them
+    (tests/test_streaming_triton.py:322-356 and :522-560 of torch-semimarkov):
+    shapes and finiteness, then the gradients against the float64 oracle, and
+    mismatched checkpoints / log Z rejected with ValueError."""
+    from inputs import make_streaming_inputs
+
+    from torch_semimarkov_b200 import (launch_streaming_triton_backward,
+                                       launch_streaming_triton_kernel)
+
+    dev = _dev()
+    B, T, K, C = 2, 30, 5, 4
+    inp = make_streaming_inputs(B, T, K, C, seed=61, proj=proj)
+    cum, tr, db = (inp[k].to(dev) for k in ("cum_scores", "transition", "duration_bias"))
+    ps = None if inp["proj_start"] is None else inp["proj_start"].to(dev)
+    pe = None if inp["proj_end"] is None else inp["proj_end"].to(dev)
+    lengths = torch.tensor([T, 21], device=dev)
+    part, ck, S = launch_streaming_triton_kernel(cum, tr, db, lengths, K, proj_start=ps,
+                                                 proj_end=pe)
+    gout = torch.tensor([1.0, 0.5], device=dev)
+    gc, gt, gd, gps, gpe = launch_streaming_triton_backward(
+        cum, tr, db, lengths, part, ck, S, gout, proj_start=ps, proj_end=pe)
+    assert gc.shape == cum.shape and gt.shape == tr.shape and gd.shape == db.shape
+    for g in (gc, gt, gd, gps, gpe):
+        assert g is None or torch.isfinite(g).all()
+    np_in = {k: (None if v is None else v.numpy()) for k, v in inp.items()}
+    _, ref = oracle.forward_backward(np_in["cum_scores"], np_in["transition"],
+                                     np_in["duration_bias"], lengths.cpu().numpy(), K,
+                                     grad_output=gout.cpu().numpy(),
+                                     proj_start=np_in["proj_start"], proj_end=np_in["proj_end"])
+    assert_grad_close(gc.cpu().numpy(), ref["cum_scores"], what="grad_cum")
+    assert_grad_close(gt.cpu().numpy(), ref["transition"], what="grad_transition")
+    assert_grad_close(gd.cpu().numpy(), ref["duration_bias"], what="grad_duration_bias")
+    if proj:
+        assert_grad_close(gps.cpu().numpy(), ref["proj_start"], what="grad_proj_start")
+        assert_grad_close(gpe.cpu().numpy(), ref["proj_end"], what="grad_proj_end")
+    with pytest.raises(ValueError):  # checkpoints of another layout
+        launch_streaming_triton_backward(cum, tr, db, lengths, part, ck[:, :-1], S, gout,
+                                         proj_start=ps, proj_end=pe)
+    with pytest.raises(ValueError):  # log Z of other inputs
+        launch_streaming_triton_backward(cum, tr, db, lengths, part + 1.0, ck, S, gout,
+                                         proj_start=ps, proj_end=pe)

@@ -28,12 +28,16 @@ SEMICRF_ERR_SEMIRING = 5
 SEMIRINGS = {"log": 0, "max": 1}
 KEEP_ALPHA, RECOMPUTE = 0, 1
 # Keep the float64 tables of both chains (alpha, and beta computed beside it
-# in the forward launch) for the backward while they stay under this many
-# bytes; above it the forward keeps sqrt(T)-spaced ring checkpoints and the
-# backward recomputes alpha between them and runs the beta chain itself.  The
-# environment variable TORCH_SEMIMARKOV_B200_BACKWARD=keep|recompute forces
-# one or the other.
-KEEP_ALPHA_MAX_BYTES = 16 << 30
+# in the forward launch) for the backward when they fit comfortably in the
+# memory this process can still get: below KEEP_ALPHA_ALWAYS_BYTES always;
+# above it while they take at most KEEP_ALPHA_FREE_FRACTION of the device's
+# free memory plus the caching allocator's unused reserve.  Otherwise the
+# forward keeps sqrt(T)-spaced ring checkpoints and the backward recomputes
+# alpha between them and runs the beta chain itself.  The environment
+# variable TORCH_SEMIMARKOV_B200_BACKWARD=keep|recompute forces one or the
+# other.
+KEEP_ALPHA_ALWAYS_BYTES = 1 << 30
+KEEP_ALPHA_FREE_FRACTION = 0.5
 
 
 def chunk_warmup_from_env() -> int:
@@ -48,14 +52,26 @@ def chunk_warmup_from_env() -> int:
     return max(1, int(env))
 
 
-def backward_mode_for(B: int, T: int, C: int) -> int:
+def keep_table_bytes(B: int, T: int, C: int) -> int:
+    """Bytes of the float64 tables the keep mode saves: a, A and n per chain."""
+    return 16 * B * (T + 1) * (2 * C + 1)
+
+
+def backward_mode_for(B: int, T: int, C: int, device=None) -> int:
     env = os.environ.get("TORCH_SEMIMARKOV_B200_BACKWARD", "").lower()
     if env == "recompute":
         return RECOMPUTE
     if env == "keep":
         return KEEP_ALPHA
-    table_bytes = 16 * B * (T + 1) * (2 * C + 1)
-    return KEEP_ALPHA if table_bytes <= KEEP_ALPHA_MAX_BYTES else RECOMPUTE
+    need = keep_table_bytes(B, T, C)
+    if need <= KEEP_ALPHA_ALWAYS_BYTES:
+        return KEEP_ALPHA
+    if device is None or not torch.cuda.is_available():
+        return RECOMPUTE
+    free, _ = torch.cuda.mem_get_info(device)
+    spare = torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+    return KEEP_ALPHA if need <= KEEP_ALPHA_FREE_FRACTION * (free + spare) else RECOMPUTE
+
 
 # every symbol include/semicrf.h declares
 EXPORTED_SYMBOLS = (
@@ -243,7 +259,7 @@ class Problem:
             S = max(int(checkpoint_interval_), K)
         self.S = S
         self.device = dev
-        self.backward_mode = (backward_mode_for(B, T, C) if backward_mode is None
+        self.backward_mode = (backward_mode_for(B, T, C, dev) if backward_mode is None
                               else int(backward_mode))
         self.c = SemicrfProblem(
             batch=B, T=T, K=K, C=C, cum_scores=self.cum.data_ptr(),

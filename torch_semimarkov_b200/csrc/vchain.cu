@@ -7,15 +7,24 @@
 //     m[s,c]  = max_c' ( x[s,c'] + tr[c',c] ),      sv[s,c] = m[s,c] + ps[s,c]
 // with x[0,c] = 0, K' = max(1, K-1), ties to the smallest k (strict >,
 // nn.py:494) and to the first c' (nn.py:491); the score is max_c x[L,c] with
-// the first maximising label (nn.py:501).  Float32 throughout, as the
-// reference computes it, with the content difference taken first as the
-// reference's edge does (pytorch_reference.py:87-92).
+// the first maximising label (nn.py:501).
 //
-// Lane c of the warp owns label c.  Its source values and cum values of the
-// last K' positions live in a per-warp shared-memory ring that only that
-// lane reads and writes, so the recurrence needs no barrier; the label
-// maximum m is 32 shuffles and a stable argmax tree.  Several sequences run
-// per CTA, one per warp, so a batch of B sequences is B warps across the GPU.
+// Float64 arithmetic on the float32 inputs.  A path score grows about
+// linearly with t (to thousands at T = 2048), where float32 rounding would
+// reach 1e-4 per step and flip decisions between paths whose scores differ by
+// that little; in float64 only ties closer than about 1e-12 can resolve
+// differently from an exact evaluation.  Each ring entry is the single double
+// E[s,c] = sv[s,c] - cum[s,c], so a candidate is E[t-k,c] + db[k,c] and the
+// common cum[t,c] is added to the winner only.
+//
+// Lane c of the warp owns label c.  Its ring of the last K' positions lives
+// in per-warp shared memory that only that lane reads and writes, so the
+// recurrence needs no barrier.  The duration maximum is a tree over groups of
+// 16 candidates (all loaded and added independently, then 4 levels of
+// compare-select that keep the smaller k on ties), the groups combined in
+// order; the label maximum m is NC shuffles and the same stable tree.
+// Several sequences run per CTA, one per warp, so a batch of B sequences is B
+// warps across the GPU.
 
 #include "semicrf_internal.cuh"
 
@@ -25,6 +34,7 @@ namespace {
 
 constexpr int kVMaxWarps = 4;
 constexpr size_t kVSmemMax = 200 * 1024;
+constexpr double kDNegInf = -__builtin_huge_val();
 
 struct VPlan {
   int kcap, R, wpb;
@@ -39,8 +49,8 @@ inline bool vplan(VPlan& p, int B, int C, int K) {
   if (p.kcap > 64) return false;
   p.R = 1;
   while (p.R < p.kcap + 1) p.R <<= 1;
-  const size_t shared = 4 * (size_t)(p.kcap + 1) * C;  // duration bias table
-  const size_t per_warp = 17 * (size_t)p.R * C;        // (sv, cum) ring (twice) + argmax ring
+  const size_t shared = 8 * (size_t)(p.kcap + 1) * C;  // duration bias table (doubles)
+  const size_t per_warp = 17 * (size_t)p.R * C;        // E ring (twice, doubles) + argmax ring
   // spread small batches over the SMs: about one warp per SM sub-partition
   const int nsm = device_sm_count();
   int wpb = (B + nsm - 1) / nsm;
@@ -53,32 +63,48 @@ inline bool vplan(VPlan& p, int B, int C, int K) {
   return true;
 }
 
+// stable maximum of v[0..N) (N a power of two): the lowest index among equal
+// maxima, as a strict > scan in index order would pick
+template <int N>
+__device__ __forceinline__ void stable_max(double (&v)[N], int (&ix)[N]) {
+#pragma unroll
+  for (int w = 1; w < N; w <<= 1)
+#pragma unroll
+    for (int q = 0; q < N; q += 2 * w)
+      if (v[q + w] > v[q]) {  // strict: ties keep the lower index
+        v[q] = v[q + w];
+        ix[q] = ix[q + w];
+      }
+}
+
 // NC: labels rounded up to 8/16/32 (the lanes that take part in the label
-// maximum).  KM: durations rounded up to 8/16/32/64, with the duration-bias
-// row held in registers and the k-scan unrolled.
+// maximum).  KM: durations rounded up to 16/32/64; the k-scan runs in groups
+// of 16, with the duration-bias row held in registers up to KM = 32.
 template <int NC, int KM>
 __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArgs a, int kcap,
                                                                  int R, int wpb) {
-  extern __shared__ __align__(16) float vsm[];
+  extern __shared__ __align__(16) double vsm[];
+  constexpr int KG = 16;               // candidates per tree
+  constexpr int NG = KM / KG;          // groups
+  constexpr bool kDbReg = KM <= 32;    // duration biases in registers
   const int C = a.C, K = a.K, T = a.T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* dbl = vsm;  // [kcap + 1][C], row k = db[min(k, K-1)]
+  double* dbl = vsm;  // [kcap + 1][C], row k = db[min(k, K-1)]
   for (int i = threadIdx.x; i < (kcap + 1) * C; i += blockDim.x) {
     const int k = i / C, cc = i % C;
-    dbl[i] = k >= 1 ? a.db[(size_t)(k < K - 1 ? k : K - 1) * C + cc] : kNegInf;
+    dbl[i] = k >= 1 ? (double)a.db[(size_t)(k < K - 1 ? k : K - 1) * C + cc] : kDNegInf;
   }
   __syncthreads();
   const int b = blockIdx.x * wpb + warp;
   if (warp >= wpb || b >= a.B) return;
-  // (sv, cum) of the last R positions, each held twice (slots s and s + R of
-  // [2R][C] float2) so that positions t-1 .. t-KM are at fixed offsets below
-  // slot (t mod R) + R; slots never written hold (-inf, 0).
-  const size_t dbl_floats = ((size_t)(kcap + 1) * C + 1) & ~size_t(1);
-  float2* ring = reinterpret_cast<float2*>(vsm + dbl_floats) + (size_t)warp * 2 * R * C;
+  // E of the last R positions, each held twice (slots s and s + R of [2R][C])
+  // so that positions t-1 .. t-KM are at fixed offsets below slot
+  // (t mod R) + R; slots never written hold -inf.
+  double* ring = vsm + (size_t)(kcap + 1) * C + (size_t)warp * 2 * R * C;
   // the label argmax of the same positions (for the packed backpointer)
-  uint8_t* rarg = reinterpret_cast<uint8_t*>(reinterpret_cast<float2*>(vsm + dbl_floats) +
+  uint8_t* rarg = reinterpret_cast<uint8_t*>(vsm + (size_t)(kcap + 1) * C +
                                              (size_t)wpb * 2 * R * C) + (size_t)warp * R * C;
-  for (int i = lane; i < 2 * R * C; i += 32) ring[i] = make_float2(kNegInf, 0.f);
+  for (int i = lane; i < 2 * R * C; i += 32) ring[i] = kDNegInf;
   __syncwarp();
   const int c = lane;
   const bool cv = c < C;
@@ -91,43 +117,38 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
   uint16_t* bp_b = a.bp ? a.bp + (size_t)b * (T + 1) * C : nullptr;
 
   // column c of the transition matrix (sources q), -inf beyond C
-  float trc[NC];
+  double trc[NC];
 #pragma unroll
-  for (int q = 0; q < NC; ++q) trc[q] = (cv && q < C) ? a.tr[(size_t)q * C + c] : kNegInf;
-  // duration-bias row of label c in registers (KM > 0)
-  float dbr[KM + 1];
+  for (int q = 0; q < NC; ++q)
+    trc[q] = (cv && q < C) ? (double)a.tr[(size_t)q * C + c] : kDNegInf;
+  // duration-bias row of label c (k = 0 .. KM; -inf outside 1 .. kcap)
+  double dbr[kDbReg ? KM + 1 : 1];
 #pragma unroll
-  for (int k = 0; k <= KM; ++k) dbr[k] = (cv && k >= 1 && k <= kcap) ? dbl[k * C + c] : kNegInf;
+  for (int k = 0; k < (kDbReg ? KM + 1 : 1); ++k)
+    dbr[k] = (kDbReg && cv && k >= 1 && k <= kcap) ? dbl[k * C + c] : kDNegInf;
 
   // m = max_q (x_q + tr[q,c]) and its first maximiser
-  auto label_max = [&](float x, int& arg) -> float {
-    float v[NC];
+  auto label_max = [&](double x, int& arg) -> double {
+    double v[NC];
     int ix[NC];
 #pragma unroll
     for (int q = 0; q < NC; ++q) {
       v[q] = __shfl_sync(0xffffffffu, x, q) + trc[q];
       ix[q] = q;
     }
-#pragma unroll
-    for (int w = 1; w < NC; w <<= 1)
-#pragma unroll
-      for (int q = 0; q < NC; q += 2 * w)
-        if (v[q + w] > v[q]) {  // strict: ties keep the lower index
-          v[q] = v[q + w];
-          ix[q] = ix[q + w];
-        }
+    stable_max<NC>(v, ix);
     arg = ix[0];
     return v[0];
   };
 
   // position 0: x = 0 for every label
   int arg = 0;
-  float x = 0.f;
+  double x = 0.0;
   {
-    const float m = label_max(cv ? 0.f : kNegInf, arg);
+    const double m = label_max(cv ? 0.0 : kDNegInf, arg);
     if (cv) {
-      const float ps = (a.ps && T > 0) ? a.ps[(size_t)b * T * C + c] : 0.f;
-      ring[c] = ring[(size_t)R * C + c] = make_float2(m + ps, cum_b[c]);
+      const double ps = (a.ps && T > 0) ? (double)a.ps[(size_t)b * T * C + c] : 0.0;
+      ring[c] = ring[(size_t)R * C + c] = (m + ps) - (double)cum_b[c];
       rarg[c] = (uint8_t)arg;
       if (bpc_b) bpc_b[c] = (uint8_t)arg;
     }
@@ -138,41 +159,48 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
   float q2 = (cv && Lb >= 3) ? cum_b[(size_t)3 * C + c] : 0.f;
   float q3 = (cv && Lb >= 4) ? cum_b[(size_t)4 * C + c] : 0.f;
   for (int t = 1; t <= Lb; ++t) {
-    const float cum_t = q0;
+    const double cum_t = (double)q0;
     q0 = q1;
     q1 = q2;
     q2 = q3;
     if (t + 4 <= Lb && cv) q3 = cum_b[(size_t)(t + 4) * C + c];
-    float best = kNegInf;
+    double best = kDNegInf;
     int bk = 0;
     if (cv) {
       // durations past K-1 have a -inf bias and positions before 0 a -inf
       // source, so the scan needs no bounds
-      const float2* top = ring + ((size_t)(t & Rm) + R) * C + c;
-      float2 e[KM + 1];
+      const double* top = ring + ((size_t)(t & Rm) + R) * C + c;
 #pragma unroll
-      for (int k = 1; k <= KM; ++k) e[k] = top[-k * C];
+      for (int g = 0; g < NG; ++g) {
+        double v[KG];
+        int ix[KG];
 #pragma unroll
-      for (int k = 1; k <= KM; ++k) {
-        const float v = (cum_t - e[k].y) + e[k].x + dbr[k];
-        if (v > best) {  // strict: ties keep the smaller k
-          best = v;
-          bk = k;
+        for (int j = 0; j < KG; ++j) {
+          const int k = g * KG + j + 1;
+          const double db_k = kDbReg ? dbr[k] : (k <= kcap ? dbl[k * C + c] : kDNegInf);
+          v[j] = top[-k * C] + db_k;
+          ix[j] = k;
+        }
+        stable_max<KG>(v, ix);
+        if (v[0] > best) {  // groups in k order: ties keep the earlier group
+          best = v[0];
+          bk = ix[0];
         }
       }
     }
+    if (best != kDNegInf) best += cum_t;
     x = best;
-    if (cv && best != kNegInf && a.pe) x = best + a.pe[((size_t)b * T + t - 1) * C + c];
+    if (cv && best != kDNegInf && a.pe) x = best + (double)a.pe[((size_t)b * T + t - 1) * C + c];
     if (cv && bpk_b) bpk_b[(size_t)t * C + c] = (int16_t)bk;
     if (cv && bp_b) {
       // duration in the low byte, the source label at the segment start above
       const int src = bk > 0 ? rarg[((t - bk) & Rm) * C + c] : 0;
       bp_b[(size_t)t * C + c] = (uint16_t)(bk | (src << 8));
     }
-    const float m = label_max(cv ? x : kNegInf, arg);
+    const double m = label_max(cv ? x : kDNegInf, arg);
     if (cv) {
-      const float ps = (a.ps && t < T) ? a.ps[((size_t)b * T + t) * C + c] : 0.f;
-      const float2 ne = make_float2(m + ps, cum_t);
+      const double ps = (a.ps && t < T) ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
+      const double ne = (m + ps) - cum_t;
       ring[(size_t)(t & Rm) * C + c] = ne;
       ring[((size_t)(t & Rm) + R) * C + c] = ne;
       rarg[(t & Rm) * C + c] = (uint8_t)arg;
@@ -180,16 +208,16 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
     }
   }
   // score = max_c x[Lb,c] and the first maximising label
-  float mv = cv ? x : kNegInf;
-  if (Lb == 0) mv = cv ? 0.f : kNegInf;
-  float mx = mv;
+  double mv = cv ? x : kDNegInf;
+  if (Lb == 0) mv = cv ? 0.0 : kDNegInf;
+  double mx = mv;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   int cand = (cv && mv == mx) ? c : 0x7fffffff;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
   if (lane == 0) {
-    const double sc = (Lb == 0 || mx == kNegInf) ? (double)kRefNegInf : (double)mx;
+    const double sc = (Lb == 0 || mx == kDNegInf) ? (double)kRefNegInf : mx;
     if (a.partition) a.partition[b] = (float)sc;
     if (a.logz) a.logz[b] = sc;
     if (a.final_c) a.final_c[b] = (cand == 0x7fffffff) ? 0 : cand;
@@ -205,7 +233,6 @@ cudaError_t launch_nc(const VChainArgs& a, const VPlan& p, cudaStream_t s) {
     kern<<<(a.B + p.wpb - 1) / p.wpb, 32 * p.wpb, p.smem + 8, s>>>(a, p.kcap, p.R, p.wpb);
     return cudaGetLastError();
   };
-  if (p.kcap <= 8) return go(vchain_kernel<NC, 8>);
   if (p.kcap <= 16) return go(vchain_kernel<NC, 16>);
   if (p.kcap <= 32) return go(vchain_kernel<NC, 32>);
   return go(vchain_kernel<NC, 64>);

@@ -129,13 +129,38 @@ def launch_streaming_triton_backward(cum_scores, transition, duration_bias, leng
     """Backward launcher with the reference contract (triton_backward.py:556-790):
     returns (grad_cum, grad_transition, grad_duration_bias, grad_proj_start,
     grad_proj_end), shared-parameter gradients already reduced with
-    grad_output.  The float32 ring checkpoints of the reference format are too
-    coarse (absolute alpha values) for the 1e-5 gradient contract, so the
-    normalised checkpoints are regenerated by a forward pass here; ``log_Z``
-    and ``ring_checkpoints`` are accepted for signature compatibility.  K is
-    taken from duration_bias.shape[0]."""
+    grad_output.  K is taken from duration_bias.shape[0].
+
+    The caller's forward outputs are checked, not trusted:
+      * ``ring_checkpoints`` must have the launcher's layout (batch,
+        ceil(T/S) + 1, K, C) for S = ``checkpoint_interval`` (S >= K), else
+        ValueError;
+      * ``log_Z`` (batch,) must agree with this call's float64 log partition to
+        float32 rounding (1e-4 relative), else ValueError: the checkpoints and
+        log Z then belong to other inputs.
+    The gradients come from this library's float64 state, recomputed from the
+    inputs (time-chunked when the batch leaves SMs idle): float32 checkpoints of
+    absolute log-alpha values carry rounding of |log alpha| * 6e-8 (about 2e-3
+    at T = 10^4), which the 1e-5 gradient contract cannot absorb -- the
+    reference's own tests compare its Triton gradients at 1e-2."""
     K = duration_bias.shape[0]
     prob = _lib.Problem(cum_scores, transition, duration_bias, lengths, K, "log",
                         proj_start, proj_end, checkpoint_interval)
-    _, _, saved = _lib.forward(prob, want_saved=True)
+    n_ck = (prob.T + prob.S - 1) // prob.S + 1
+    want = (prob.B, n_ck, K, prob.C)
+    if not isinstance(ring_checkpoints, torch.Tensor) or tuple(ring_checkpoints.shape) != want:
+        got = tuple(ring_checkpoints.shape) if isinstance(ring_checkpoints, torch.Tensor) else None
+        raise ValueError(f"ring_checkpoints must have shape {want} (batch, ceil(T/S)+1, K, C) "
+                         f"for checkpoint_interval S={prob.S}, got {got}")
+    if not isinstance(log_Z, torch.Tensor) or tuple(log_Z.shape) != (prob.B,):
+        raise ValueError(f"log_Z must have shape ({prob.B},)")
+    partition, _, saved = _lib.forward(prob, want_saved=True)
+    lz = log_Z.detach().to(device=partition.device, dtype=torch.float64)
+    ours = partition.double()
+    bad = (lz - ours).abs() > 1e-4 * ours.abs() + 1e-3
+    if bool(bad.any()):
+        i = int(bad.nonzero()[0])
+        raise ValueError(f"log_Z[{i}] = {float(lz[i])!r} does not match the log partition of "
+                         f"these inputs ({float(ours[i])!r}): the checkpoints and log Z come "
+                         "from other inputs")
     return _lib.backward(prob, saved, grad_output)
