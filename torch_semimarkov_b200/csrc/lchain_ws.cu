@@ -75,6 +75,7 @@ __device__ __forceinline__ void bar_sync(int id, int n) {
 
 struct WsPlan {
   int C, Cs, CP, K, kcap, LP, R, NR, kx, nbr, nbulk, np, nsplit, nwt;
+  int nsplit1, bpc1;  // single-label far-sum items: splits per label, source blocks per split
   int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_nring, o_ca, o_far, o_g,
       o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast;
   int bytes;
@@ -101,6 +102,11 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.nbulk = kWsThreads - (kWsThreads / 128) * CP;
   p.np = p.Cs / 2;
   p.nsplit = p.nbulk / p.np > 0 ? p.nbulk / p.np : 1;
+  // single-label items (label, split): each covers bpc1 consecutive source
+  // blocks of the at most ceil(kcap / LP) - 1 a target block reaches
+  p.nsplit1 = p.nbulk / C > 0 ? p.nbulk / C : 1;
+  const int nq_max = (p.kcap + LP - 1) / LP - 1;
+  p.bpc1 = nq_max > 0 ? (nq_max + p.nsplit1 - 1) / p.nsplit1 : 0;
   p.nwt = (p.kcap + LP - 1) / LP + 4;  // source blocks a k-window reaches, plus margin
   int o = 0;
   auto take = [&](int n) {
@@ -145,7 +151,10 @@ bool lchain_ws_supported(int C, int K) {
 }
 
 // ---------------------------------------------------------------------------
-template <int CP, int LP>
+// BPC > 0: the far sums run as single-label items whose duration-bias lags
+// stay in registers for the whole chain (BPC source blocks per item, at least
+// pl.bpc1); BPC = 0: label-pair items reading the lags from shared memory.
+template <int CP, int LP, int BPC>
 __global__ void __launch_bounds__(kWsThreads, 1)
     lchain_ws_kernel(const __grid_constant__ LChainLaunch L) {
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -327,6 +336,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const int QW = min(NWT, (kcap + LP - 1) / LP + 4);  // blocks a k-window reaches
     const int wc = btid % C, wq0 = btid / C, wqs = NBT / C > 0 ? NBT / C : 1;
     const bool wact = btid < wqs * C;
+    // single-label far-sum item of this thread: label fc, source blocks
+    // q = fqa .. fqa + BPC - 1, and their duration lags fqa*LP - (LP-1) + m
+    // (m < BPC*LP + LP - 1) held in registers; lags outside 1..kcap are 0
+    const int fc = btid % C, fj = btid / C;
+    const bool fact = BPC > 0 && fj < pl.nsplit1;
+    const int fqa = 2 + fj * BPC;
+    constexpr int NW = BPC > 0 ? BPC * LP + LP - 1 : 1;
+    double dw[NW];
+#pragma unroll
+    for (int m = 0; m < NW; ++m) {
+      const int k = fqa * LP - (LP - 1) + m;
+      dw[m] = (BPC > 0 && fact && k >= 0 && k < pl.kx) ? dbd[k * Cs + fc] : 0.0;
+    }
 
     // prepare(tau): frame, factors and far sums of block tau into buffer tau&1
     auto prepare = [&](int tau) {
@@ -421,9 +443,44 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int s_lo = (u0 - kcap) > u_begin ? (u0 - kcap) : u_begin;
       const int qmax = (u0 - s_lo + LP - 1) / LP;  // the block holding s_lo
       const int nq = qmax - 1;                      // blocks q = 2 .. qmax
-      const int nsplit = pl.nsplit, np = pl.np;
+      const int nsplit = BPC > 0 ? pl.nsplit1 : pl.nsplit, np = pl.np;
       const double* wcur = wt + (size_t)bf * NWT * Cs;
-      if (nq > 0) {
+      if (BPC > 0 && nq > 0) {
+        if (fact) {
+          double acc[LP];
+#pragma unroll
+          for (int i = 0; i < LP; ++i) acc[i] = 0.0;
+#pragma unroll
+          for (int mq = 0; mq < BPC; ++mq) {
+            const int q = fqa + mq;
+            if (q <= qmax) {
+              const int sb = u0 - q * LP;
+              int bq = (tau - q) % NR;
+              if (bq < 0) bq += NR;
+              const double* rp = ring + (size_t)bq * LP * Cs + fc;
+              const double Wq = wcur[q * Cs + fc];
+              double x[LP];
+#pragma unroll
+              for (int r = 0; r < LP; ++r) x[r] = (sb + r >= s_lo) ? rp[(size_t)r * Cs] * Wq : 0.0;
+#pragma unroll
+              for (int r = 0; r < LP; ++r)
+#pragma unroll
+                for (int i = 0; i < LP; ++i)
+                  acc[i] = fma(x[r], dw[mq * LP + (LP - 1) + i - r], acc[i]);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < LP; ++i) part[(fj * LP + i) * Cs + fc] = acc[i];
+        }
+        bar_sync(kBarBulk, NBT);
+        WT_ADD(3);
+        for (int w = btid; w < LP * C; w += NBT) {
+          const int i = w / C, cc = w % C;
+          double s = 0.0;
+          for (int j = 0; j < nsplit; ++j) s += part[(j * LP + i) * Cs + cc];
+          farb[(bf * LP + i) * CP + cc] = s;
+        }
+      } else if (nq > 0) {
         const int bpc = (nq + nsplit - 1) / nsplit;  // source blocks per chunk
         for (int w = btid; w < np * nsplit; w += NBT) {
           const int c0 = 2 * (w % np), j = w / np;
@@ -687,9 +744,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-template <int CP>
+template <int CP, int BPC>
 static cudaError_t launch_ws_cp(const LChainLaunch& L, int grid, size_t smem, cudaStream_t s) {
-  auto kern = lchain_ws_kernel<CP, 8>;
+  auto kern = lchain_ws_kernel<CP, 8, BPC>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -707,8 +764,20 @@ cudaError_t launch_lchain_ws(const LChainLaunch& L, int grid, cudaStream_t s) {
   if (L.B <= 0 || grid <= 0) return cudaSuccess;
   WsPlan p;
   if (!ws_choose(p, L.C, L.K)) return cudaErrorInvalidValue;
-  if (ws_cp(L.C) == 32) return launch_ws_cp<32>(L, grid, (size_t)p.bytes, s);
-  return launch_ws_cp<64>(L, grid, (size_t)p.bytes, s);
+  // the smallest register window that covers the plan's source blocks per
+  // split; longer windows take the label-pair items
+  const int need = p.bpc1;
+  if (ws_cp(L.C) == 32) {
+    if (need <= 1) return launch_ws_cp<32, 1>(L, grid, (size_t)p.bytes, s);
+    if (need <= 2) return launch_ws_cp<32, 2>(L, grid, (size_t)p.bytes, s);
+    if (need <= 3) return launch_ws_cp<32, 3>(L, grid, (size_t)p.bytes, s);
+    if (need <= 5) return launch_ws_cp<32, 5>(L, grid, (size_t)p.bytes, s);
+    if (need <= 7) return launch_ws_cp<32, 7>(L, grid, (size_t)p.bytes, s);
+    return launch_ws_cp<32, 0>(L, grid, (size_t)p.bytes, s);
+  }
+  if (need <= 3) return launch_ws_cp<64, 3>(L, grid, (size_t)p.bytes, s);
+  if (need <= 7) return launch_ws_cp<64, 7>(L, grid, (size_t)p.bytes, s);
+  return launch_ws_cp<64, 0>(L, grid, (size_t)p.bytes, s);
 }
 
 }  // namespace semicrf
