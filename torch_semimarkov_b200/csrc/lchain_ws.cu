@@ -33,6 +33,8 @@
 // measured scale of the state (float64 leaves a very wide margin for the
 // prediction error).
 
+#include <type_traits>
+
 #include "semicrf_internal.cuh"
 
 namespace semicrf {
@@ -58,14 +60,6 @@ constexpr size_t kWsSmemMax = 227 * 1024;
 enum : int { kBarFull0 = 1, kBarFull1 = 2, kBarDone0 = 3, kBarDone1 = 4, kBarBulk = 5,
              kBarSerial = 6 };
 
-// log(m) to within ln 2, from the exponent bits (m > 0; 0 otherwise): enough
-// for a normaliser, which only keeps the linear-domain values in range
-__device__ __forceinline__ double log_scale(double m) {
-  if (!(m > 0.0)) return 0.0;
-  const long long bits = __double_as_longlong(m);
-  return (double)((int)((bits >> 52) & 0x7ff) - 1023) * 0.6931471805599453;
-}
-
 __device__ __forceinline__ void bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
@@ -76,8 +70,8 @@ __device__ __forceinline__ void bar_sync(int id, int n) {
 struct WsPlan {
   int C, Cs, CP, K, kcap, LP, R, NR, kx, nbr, nbulk, np, nsplit, nwt;
   int nsplit1, bpc1;  // single-label far-sum items: splits per label, source blocks per split
-  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_nring, o_ca, o_far, o_g,
-      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast;
+  int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_nring, o_ca, o_da, o_far, o_g,
+      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast, o_tab;
   int bytes;
 };
 
@@ -120,10 +114,11 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_dbmax = take(8 * CP);
   p.o_colmax = take(8 * CP);
   p.o_nring = take(8 * (p.nbr + 2));
-  p.o_ca = take(8 * 2 * CP);
+  p.o_ca = take(8 * 4 * CP);      // anchors cA of the last four blocks (slot tau mod 4)
+  p.o_da = take(8 * 2 * 4 * CP);  // [exp | raw] anchor change csign*(cA_tau - cA_tau-1)
   p.o_far = take(8 * 2 * LP * CP);
-  p.o_g = take(8 * 2 * LP * CP);
-  p.o_h = take(8 * 2 * LP * CP);
+  p.o_g = take(8 * 4 * LP * CP);  // g and h of the last four blocks (slot tau mod 4)
+  p.o_h = take(8 * 4 * LP * CP);
   p.o_wprev = take(8 * 2 * CP);
   p.o_part = take(8 * p.nsplit * LP * p.Cs);
   p.o_abuf = take(8 * CP);
@@ -132,6 +127,7 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_edb = take(8 * CP);
   p.o_ecm = take(8 * CP);
   p.o_alast = take(8 * 2 * CP);  // the state at the end of the last two blocks
+  p.o_tab = take(8 * 2 * 4 * LP * CP);  // [a | A][block mod 4][LP][CP]: table rows in flight
   p.bytes = o;
 }
 
@@ -203,7 +199,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* dbmax = reinterpret_cast<double*>(smraw + pl.o_dbmax);
   double* colmax = reinterpret_cast<double*>(smraw + pl.o_colmax);
   double* nring = reinterpret_cast<double*>(smraw + pl.o_nring);  // n_gamma
-  double* cA = reinterpret_cast<double*>(smraw + pl.o_ca);        // [2][CP] anchors (bulk)
+  double* cA = reinterpret_cast<double*>(smraw + pl.o_ca);        // [4][CP] anchors (bulk)
+  double* dae = reinterpret_cast<double*>(smraw + pl.o_da);       // [4][CP] exp(anchor change)
+  double* dar = dae + 4 * CP;                                      // [4][CP] anchor change
   double* farb = reinterpret_cast<double*>(smraw + pl.o_far);     // [2][LP][CP]
   double* gb = reinterpret_cast<double*>(smraw + pl.o_g);
   double* hb = reinterpret_cast<double*>(smraw + pl.o_h);
@@ -217,6 +215,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* edb = reinterpret_cast<double*>(smraw + pl.o_edb);  // exp(dbmax)
   double* ecm = reinterpret_cast<double*>(smraw + pl.o_ecm);  // exp(colmax)
   double* alast = reinterpret_cast<double*>(smraw + pl.o_alast);  // [2 blocks][CP]
+  // the serial warp's table rows of the last four blocks: a at [0][tau mod 4],
+  // A at [1][tau mod 4]; the bulk warps copy a finished block to global
+  // memory while the serial warp runs the next two
+  double* stab = reinterpret_cast<double*>(smraw + pl.o_tab);
   auto lidx = [&](int gamma) { return (gamma + NBR) & (NBR - 1); };  // gamma >= -NBR
 
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int t0 = cpos(u_begin);
       if (jc == 0 && atab_b) atab_b[(size_t)t0 * C + c] = a0;
       if (jc == 0 && Atab_b) Atab_b[(size_t)t0 * C + c] = ym0 * exp(colmax[c]);
-      cA[1 * CP + c] = cumd(u_begin, c);  // anchor of block -1 (parity of -1 is 1)
+      cA[3 * CP + c] = cumd(u_begin, c);  // anchor of block -1 (slot (-1) mod 4 = 3)
     }
     if (tid == 0) {
       if (jc == 0 && ntab_b) ntab_b[cpos(u_begin)] = 0.0;
@@ -325,20 +327,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       e_c[r] = (w < LP * C) ? w % C : 0;
       pre[r] = 0.0;
     }
-    auto prefetch_cum = [&](int tau) {
-      const int u0 = u_begin + 1 + tau * LP;
-#pragma unroll
-      for (int r = 0; r < kMaxE; ++r)
-        pre[r] = (e_i[r] >= 0 && u0 + e_i[r] <= u_end) ? cumd(u0 + e_i[r], e_c[r]) : 0.0;
-    };
-    double lend3 = 0.0;  // scale at the end of block tau-3 (block -1: 0)
     // frame-table entries this thread updates: label wc, blocks q = wq0 + m*wqs
     const int QW = min(NWT, (kcap + LP - 1) / LP + 4);  // blocks a k-window reaches
     const int wc = btid % C, wq0 = btid / C, wqs = NBT / C > 0 ? NBT / C : 1;
     const bool wact = btid < wqs * C;
     // single-label far-sum item of this thread: label fc, source blocks
     // q = fqa .. fqa + BPC - 1, and their duration lags fqa*LP - (LP-1) + m
-    // (m < BPC*LP + LP - 1) held in registers; lags outside 1..kcap are 0
+    // (m < BPC*LP + LP - 1) held in registers; lags outside 2*LP..kcap are 0
+    // (the serial warp's window covers durations 1 .. 2*LP-1)
     const int fc = btid % C, fj = btid / C;
     const bool fact = BPC > 0 && fj < pl.nsplit1;
     const int fqa = 2 + fj * BPC;
@@ -347,18 +343,70 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
     for (int m = 0; m < NW; ++m) {
       const int k = fqa * LP - (LP - 1) + m;
-      dw[m] = (BPC > 0 && fact && k >= 0 && k < pl.kx) ? dbd[k * Cs + fc] : 0.0;
+      dw[m] = (BPC > 0 && fact && k >= 2 * LP && k < pl.kx) ? dbd[k * Cs + fc] : 0.0;
     }
 
-    // prepare(tau): frame, factors and far sums of block tau into buffer tau&1
-    auto prepare = [&](int tau) {
-      const int bf = tau & 1;
+    // The bulk work of block tau splits in two.  precompute(tau) needs only
+    // the inputs: the block's anchors cA (cum at its first position), the
+    // factor exp(csign*(cA_tau - cA_tau-1)) of the anchor change, and the g / h
+    // factors of its targets; it runs a block ahead, after the FULL arrive of
+    // the block before.  critical(tau) depends on the chain's state: the
+    // normaliser n_tau = e_tau * ln 2 (an integer exponent, so a frame change
+    // is an exact power of two), the frame factors W, the far sums.
+    int e_m1 = 0, e_m2 = 0;  // exponents of blocks tau-1 and tau-2 (block -1: 0)
+    int lend3e = 0;          // scale exponent at the end of block tau-3 (block -1: 0)
+    double pre0[kMaxE];      // cum at the first position of the block, per element label
+    auto prefetch_cum = [&](int tau) {
+      const int u0 = u_begin + 1 + tau * LP;
+#pragma unroll
+      for (int r = 0; r < kMaxE; ++r) {
+        const bool in = e_i[r] >= 0 && u0 + e_i[r] <= u_end;
+        pre[r] = in ? cumd(u0 + e_i[r], e_c[r]) : 0.0;
+        pre0[r] = (e_i[r] >= 0 && u0 <= u_end) ? cumd(u0, e_c[r]) : 0.0;
+      }
+    };
+    auto precompute = [&](int tau) {
+      const int sl = tau & 3, sp = (tau + 3) & 3;  // this block's slot, the previous block's
       const int u0 = u_begin + 1 + tau * LP;
       const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
-      // normaliser prediction for this block from the scales at the end of
-      // blocks tau-2 and tau-3; every bulk warp derives it from the state the
-      // serial warp left in alast
-      double n_tau = 0.0;
+      const bool noproj = ps_b == nullptr && pe_b == nullptr;
+#pragma unroll
+      for (int r = 0; r < kMaxE; ++r) {
+        const int i = e_i[r], cc = e_c[r];
+        if (i == 0) {
+          // the thread that holds label cc's first position owns its anchor
+          // in every block, so it reads the previous anchor it wrote itself
+          const double da = csign * (pre[r] - cA[sp * CP + cc]);
+          cA[sl * CP + cc] = pre[r];
+          dar[sl * CP + cc] = da;
+          dae[sl * CP + cc] = exp(fmin(fmax(da, -700.0), 700.0));
+        }
+        if (i >= 0 && i < nP) {
+          const int u = u0 + i;
+          const double d = csign * (pre[r] - pre0[r]);
+          if (noproj) {
+            // |dc| <= 650 keeps exp(dc) and its reciprocal normal
+            if (L.ovf && fabs(d) > 650.0) *L.ovf = 1;
+            const double dc = fmin(fmax(d, -650.0), 650.0);
+            const double ed = exp(dc);
+            gb[(sl * LP + i) * CP + cc] = edb[cc] * ed;
+            hb[(sl * LP + i) * CP + cc] = ecm[cc] * __drcp_rn(ed);
+          } else {
+            const double gx = toff_at(u, cc) + dbmax[cc] + d, hx = colmax[cc] + soff_at(u, cc) - d;
+            if (L.ovf && (gx > 700.0 || hx > 700.0)) *L.ovf = 1;
+            gb[(sl * LP + i) * CP + cc] = exp(fmin(gx, 700.0));
+            hb[(sl * LP + i) * CP + cc] = exp(fmin(hx, 700.0));
+          }
+        }
+      }
+      prefetch_cum(tau + 1);
+    };
+    // critical(tau): normaliser, frame factors and far sums of block tau
+    // (far sums into buffer tau & 1); every bulk thread derives e_tau itself
+    auto critical = [&](int tau) {
+      const int bf = tau & 1, sl = tau & 3;
+      const int u0 = u_begin + 1 + tau * LP;
+      int e_tau = 0;
       if (tau >= 2) {
         const double* al = alast + ((tau - 2) & 1) * CP;
         double m;
@@ -369,31 +417,23 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
         }
-        const double l2 = nring[lidx(tau - 2)] + log_scale(m);
-        const double gr = fmin(fmax(l2 - lend3, -150.0), 150.0);
-        n_tau = l2 + 2.0 * gr;
-        lend3 = l2;
+        // the block-end scale as a power of two (its binary exponent)
+        const int xm = m > 0.0 ? (int)((__double_as_longlong(m) >> 52) & 0x7ff) - 1023 : 0;
+        const int l2e = e_m2 + xm;
+        const int gre = min(max(l2e - lend3e, -216), 216);  // 216 ln 2 = 149.7
+        e_tau = l2e + 2 * gre;
+        lend3e = l2e;
       }
-      if (btid == 0) nring[lidx(tau)] = n_tau;
-      const double n_prev = nring[lidx(tau - 1)];  // written by prepare(tau-1)
-      // anchors (the cum values of the block's first position) and w_{tau-1}
-      // (frame tau-1 -> tau), by the threads that hold those cum values
-#pragma unroll
-      for (int r = 0; r < kMaxE; ++r) {
-        if (e_i[r] == 0) {
-          const int cc = e_c[r];
-          cA[bf * CP + cc] = pre[r];
-          const double wx = n_prev - n_tau + csign * (pre[r] - cA[(bf ^ 1) * CP + cc]);
-          if (L.ovf && fabs(wx) > 700.0) *L.ovf = 1;  // the frame change clips
-          const double w = exp(fmin(fmax(wx, -700.0), 700.0));
-          wprev[bf * CP + cc] = w;
-        }
-      }
-      bar_sync(kBarBulk, NBT);
+      if (btid == 0) nring[lidx(tau)] = (double)e_tau * 0.6931471805599453;
+      // frame tau-1 -> tau: w = 2^(e_tau-1 - e_tau) * exp(csign*(cA_tau - cA_tau-1)),
+      // per label, computed by each thread for the label it updates
+      const int de = e_m1 - e_tau;
       if (wact) {
+        const double wl = ldexp(dae[sl * CP + wc], de);  // w_{tau-1}
+        if (L.ovf && fabs(de * 0.6931471805599453 + dar[sl * CP + wc]) > 700.0) *L.ovf = 1;
+        if (wq0 == 0) wprev[bf * CP + wc] = wl;
         double* wcur = wt + (size_t)bf * NWT * Cs;
         const double* wold = wt + (size_t)(bf ^ 1) * NWT * Cs;
-        const double wl = wprev[bf * CP + wc];  // w_{tau-1}
         for (int q = wq0; q < QW; q += wqs) {
           double v;
           if (q == 0) {
@@ -406,31 +446,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           wcur[q * Cs + wc] = v;
         }
       }
-      // g / h of the targets: g = exp(toff + dbmax + d), h = exp(colmax + soff - d)
-      const bool noproj = ps_b == nullptr && pe_b == nullptr;
-#pragma unroll
-      for (int r = 0; r < kMaxE; ++r) {
-        const int i = e_i[r], cc = e_c[r];
-        if (i >= 0 && i < nP) {
-          const int u = u0 + i;
-          const double d = csign * (pre[r] - cA[bf * CP + cc]);
-          if (noproj) {
-            // |dc| <= 650 keeps exp(dc) and its reciprocal normal
-            if (L.ovf && fabs(d) > 650.0) *L.ovf = 1;
-            const double dc = fmin(fmax(d, -650.0), 650.0);
-            const double ed = exp(dc);
-            gb[(bf * LP + i) * CP + cc] = edb[cc] * ed;
-            hb[(bf * LP + i) * CP + cc] = ecm[cc] * __drcp_rn(ed);
-          } else {
-            const double gx = toff_at(u, cc) + dbmax[cc] + d, hx = colmax[cc] + soff_at(u, cc) - d;
-            if (L.ovf && (gx > 700.0 || hx > 700.0)) *L.ovf = 1;
-            gb[(bf * LP + i) * CP + cc] = exp(fmin(gx, 700.0));
-            hb[(bf * LP + i) * CP + cc] = exp(fmin(hx, 700.0));
-          }
-        }
-      }
-      // the next block's cum values: the loads complete during the far sums
-      prefetch_cum(tau + 1);
+      e_m2 = e_m1;
+      e_m1 = e_tau;
       bar_sync(kBarBulk, NBT);
       WT_ADD(2);
       // far sums over sources s in [s_lo, s_hi], s_hi = u0-LP-1 (end of block tau-2).
@@ -494,8 +511,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
             for (int m = 0; m < 2 * LP - 1; ++m) {
               const double2 v = dp[(size_t)m * (Cs / 2)];
-              d[m][0] = v.x;
-              d[m][1] = v.y;
+              // durations below 2*LP are the serial warp's window
+              const bool near = qa * LP - (LP - 1) + m < 2 * LP;
+              d[m][0] = near ? 0.0 : v.x;
+              d[m][1] = near ? 0.0 : v.y;
             }
           }
           for (int q = qa; q <= qb; ++q) {
@@ -560,24 +579,51 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 
     prefetch_cum(0);
     if (NB > 0) {
-      prepare(0);
+      precompute(0);
+      critical(0);
       bar_arrive(kBarFull0, NPART);
     }
     if (NB > 1) {
-      prepare(1);
+      precompute(1);
+      critical(1);
       bar_arrive(kBarFull1, NPART);
     }
+    if (NB > 2) precompute(2);
     for (int tau = 2; tau < NB + 2; ++tau) {
       WT_ADD(5);
       // buffer (tau & 1) is free once the serial warp is done with block tau-2
       bar_sync(((tau - 2) & 1) ? kBarDone1 : kBarDone0, NPART);
       WT_ADD(0);
+
       // the warm-up is over: hand off this chunk's guess of the state
       if (tau - 2 == tau_out) export_state(0, u_out, btid, NBT);
       if (tau < NB) {
-        prepare(tau);
+        critical(tau);
         bar_arrive((tau & 1) ? kBarFull1 : kBarFull0, NPART);
       }
+      {
+        // block tau-2 is final: its table rows (a, A and the normaliser) to
+        // global memory, past the warm-up only.  Its buffer (tau-2) mod 4 is
+        // next written by block tau+2, which starts only after this thread
+        // arrives at FULL of block tau+2, so the copy runs off the serial
+        // warp's path.
+        const int tb = tau - 2, pb = tb & 3;
+        const int ub0 = u_begin + 1 + tb * LP;
+        const int nPb = (u_end - ub0 + 1) < LP ? (u_end - ub0 + 1) : LP;
+        for (int w = btid; w < LP * C; w += NBT) {
+          const int i = w / C, cc = w % C;
+          const int u = ub0 + i;
+          if (i < nPb && u > u_out) {
+            const size_t row = (size_t)cpos(u);
+            if (atab_b) atab_b[row * C + cc] = stab[(pb * LP + i) * CP + cc];
+            if (Atab_b) Atab_b[row * C + cc] = stab[((4 + pb) * LP + i) * CP + cc];
+            if (cc == 0 && ntab_b) ntab_b[row] = nring[lidx(tb)];
+          }
+        }
+      }
+      // the next block's input-only factors (its slot (tau+1) mod 4 was last
+      // read by the serial warp in block tau-3, which is done)
+      if (tau + 1 < NB) precompute(tau + 1);
     }
     WT_FLUSH(0);
   } else {
@@ -636,72 +682,76 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       return r;
     };
 
-    // near window: sources of the previous block (index j <-> u0 - LP + j)
-    double ep[LP];
+    // near window: win[j] = E[u-1-j] for the next target u, j < NWIN, in the
+    // current block's frame (the far sums cover durations NWIN+1 and up)
+    constexpr int NWIN = 2 * LP - 1;
+    double win[NWIN];
 #pragma unroll
-    for (int j = 0; j < LP; ++j) ep[j] = 0.0;
-    ep[LP - 1] = cv ? ring[(R - 1) * Cs + c] : 0.0;  // position 0
+    for (int j = 0; j < NWIN; ++j) win[j] = 0.0;
+    win[0] = cv ? ring[(R - 1) * Cs + c] : 0.0;  // position u_begin
     double a_last = a0;
     double n_last = 0.0;
     for (int tau = 0; tau < NB; ++tau) {
-      const int bf = tau & 1;
+      const int bf = tau & 1, sl = tau & 3;
       WT_ADD(12);
       bar_sync(bf ? kBarFull1 : kBarFull0, NPART);
       WT_ADD(8);
       const int u0 = u_begin + 1 + tau * LP;
       const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
       const double n_tau = nring[lidx(tau)];
+      // the window's sources are in the previous blocks' frames: one factor
+      // w_{tau-1} brings all of them to this block's
       const double wp = cv ? wprev[bf * CP + c] : 0.0;
-      // this block's far sums and g factors, loaded once per block rather than
-      // once per position on the critical path
-      double fr[LP], gr[LP];
 #pragma unroll
-      for (int i = 0; i < LP; ++i) {
-        fr[i] = cv ? farb[(bf * LP + i) * CP + c] : 0.0;
-        gr[i] = cv ? gb[(bf * LP + i) * CP + c] : 0.0;
+      for (int j = 0; j < NWIN; ++j) win[j] *= wp;
+      const double* far_b = farb + (size_t)bf * LP * CP + c;
+      const double* g_b = gb + (size_t)sl * LP * CP + c;
+      const double* h_b = hb + (size_t)sl * LP * CP + c;
+      // R = far sum + the window's terms of durations 2 .. NWIN+1 ... of the
+      // first target; the newest source's term (duration 1) is added when it
+      // is known
+      double rn;
+      {
+        double q4[4] = {cv ? far_b[0] : 0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+        for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j + 1], dbk[j + 2], q4[j & 3]);
+        rn = (q4[0] + q4[1]) + (q4[2] + q4[3]);
       }
-#pragma unroll
-      for (int j = 0; j < LP; ++j) ep[j] *= wp;
-      double ec[LP];
-#pragma unroll
-      for (int i = 0; i < LP; ++i) ec[i] = 0.0;
       int slot = (tau % NR) * LP;  // slot of position u0: (u0 - 1) mod R
-#pragma unroll
-      for (int i = 0; i < LP; ++i) {
-        if (i < nP) {
-          const int u = u0 + i;
-          double S = 0.0, a = 0.0;
-          if (cv) {
-            double pp[4] = {fr[i], 0.0, 0.0, 0.0};
-#pragma unroll
-            for (int j = 0; j < LP; ++j) pp[j & 3] = fma(ep[j], dbk[LP + i - j], pp[j & 3]);
-#pragma unroll
-            for (int j = 0; j + 1 < i; ++j) pp[(j + 1) & 3] = fma(ec[j], dbk[i - j], pp[(j + 1) & 3]);
-            const double part0 = (pp[0] + pp[1]) + (pp[2] + pp[3]);
-            S = (i >= 1) ? fma(ec[i - 1], dbk[1], part0) : part0;
-            a = (S > 0.0) ? gr[i] * S : 0.0;
-          }
-          WT_ADD(9);
-          // h is needed right after the mat-vec: load it before, so its
-          // latency overlaps the mat-vec's
-          const double hcur = cv ? hb[(bf * LP + i) * CP + c] : 0.0;
-          const double ym = matvec(a);
-          WT_ADD(10);
-          if (cv) {
-            const double e = (ym > 0.0) ? ym * hcur : 0.0;
-            ec[i] = e;
-            ring[slot * Cs + c] = e;
-            const int t = cpos(u);
-            if (u > u_out) {
-              if (atab_b) atab_b[(size_t)t * C + c] = a;
-              if (Atab_b) Atab_b[(size_t)t * C + c] = ym * ecol;
-            }
-          }
-          if (tid == 0 && ntab_b && u > u_out) ntab_b[cpos(u)] = n_tau;
-          a_last = a;
-          ++slot;
-          WT_ADD(11);
+      // one position per iteration, identical code for every position (a
+      // short loop body instead of a block-long unrolled sequence)
+#pragma unroll 1
+      for (int i = 0; i < nP; ++i) {
+        double a = 0.0;
+        const double gi = cv ? g_b[i * CP] : 0.0;
+        const double hcur = cv ? h_b[i * CP] : 0.0;
+        if (cv) {
+          const double S = fma(win[0], dbk[1], rn);
+          a = (S > 0.0) ? gi * S : 0.0;
         }
+        WT_ADD(9);
+        // the next target's R from the sources known now (its duration-1
+        // source is this position's, still to come), while the mat-vec runs
+        if (i + 1 < nP) {
+          double q4[4] = {cv ? far_b[(i + 1) * CP] : 0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+          for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j], dbk[j + 2], q4[j & 3]);
+          rn = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+        }
+        const double ym = matvec(a);
+        WT_ADD(10);
+        double e = 0.0;
+        if (cv) {
+          e = (ym > 0.0) ? ym * hcur : 0.0;
+          ring[(slot + i) * Cs + c] = e;
+          stab[(sl * LP + i) * CP + c] = a;
+          stab[((4 + sl) * LP + i) * CP + c] = ym * ecol;
+        }
+#pragma unroll
+        for (int j = NWIN - 1; j > 0; --j) win[j] = win[j - 1];
+        win[0] = e;
+        a_last = a;
+        WT_ADD(11);
       }
       // the state at the end of the block, from which the bulk derives the
       // block's scale for its normaliser prediction: its per-warp maxima when
@@ -715,12 +765,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         alast[bf * CP + c] = cv ? a_last : 0.0;
       }
       n_last = n_tau;
-      // the near window of the next block is this block (padded with zeros)
-#pragma unroll
-      for (int j = 0; j < LP; ++j) ep[j] = ec[j];
-      if (nP < LP) {
-        // only the last block can be short; no next block reads ep
-      }
       __threadfence_block();
       bar_arrive(bf ? kBarDone1 : kBarDone0, NPART);
     }
