@@ -71,7 +71,7 @@ struct WsPlan {
   int C, Cs, CP, K, kcap, LP, R, NR, kx, nbr, nbulk, np, nsplit, nwt;
   int nsplit1, bpc1;  // single-label far-sum items: splits per label, source blocks per split
   int o_ring, o_dbd, o_mx, o_dbmax, o_colmax, o_nring, o_ca, o_da, o_far, o_g,
-      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast, o_tab;
+      o_h, o_wprev, o_part, o_abuf, o_wt, o_misc, o_edb, o_ecm, o_alast;
   int bytes;
 };
 
@@ -127,7 +127,6 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_edb = take(8 * CP);
   p.o_ecm = take(8 * CP);
   p.o_alast = take(8 * 2 * CP);  // the state at the end of the last two blocks
-  p.o_tab = take(8 * 2 * 4 * LP * CP);  // [a | A][block mod 4][LP][CP]: table rows in flight
   p.bytes = o;
 }
 
@@ -215,10 +214,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   double* edb = reinterpret_cast<double*>(smraw + pl.o_edb);  // exp(dbmax)
   double* ecm = reinterpret_cast<double*>(smraw + pl.o_ecm);  // exp(colmax)
   double* alast = reinterpret_cast<double*>(smraw + pl.o_alast);  // [2 blocks][CP]
-  // the serial warp's table rows of the last four blocks: a at [0][tau mod 4],
-  // A at [1][tau mod 4]; the bulk warps copy a finished block to global
-  // memory while the serial warp runs the next two
-  double* stab = reinterpret_cast<double*>(smraw + pl.o_tab);
   auto lidx = [&](int gamma) { return (gamma + NBR) & (NBR - 1); };  // gamma >= -NBR
 
   const float* cum_b = A.cum + (size_t)b * (T + 1) * C;
@@ -573,7 +568,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           farb[(bf * LP + i) * CP + cc] = 0.0;
         }
       }
-      __threadfence_block();
+      // (bar.arrive orders these shared-memory writes before the serial
+      // warp's bar.sync on FULL: no separate fence)
       WT_ADD(4);
     };
 
@@ -602,24 +598,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         bar_arrive((tau & 1) ? kBarFull1 : kBarFull0, NPART);
       }
       {
-        // block tau-2 is final: its table rows (a, A and the normaliser) to
-        // global memory, past the warm-up only.  Its buffer (tau-2) mod 4 is
-        // next written by block tau+2, which starts only after this thread
-        // arrives at FULL of block tau+2, so the copy runs off the serial
-        // warp's path.
-        const int tb = tau - 2, pb = tb & 3;
+        // block tau-2 is final: its normalisers to global memory, past the
+        // warm-up only (the serial warp writes the a and A rows itself)
+        const int tb = tau - 2;
         const int ub0 = u_begin + 1 + tb * LP;
         const int nPb = (u_end - ub0 + 1) < LP ? (u_end - ub0 + 1) : LP;
-        for (int w = btid; w < LP * C; w += NBT) {
-          const int i = w / C, cc = w % C;
-          const int u = ub0 + i;
-          if (i < nPb && u > u_out) {
-            const size_t row = (size_t)cpos(u);
-            if (atab_b) atab_b[row * C + cc] = stab[(pb * LP + i) * CP + cc];
-            if (Atab_b) Atab_b[row * C + cc] = stab[((4 + pb) * LP + i) * CP + cc];
-            if (cc == 0 && ntab_b) ntab_b[row] = nring[lidx(tb)];
-          }
-        }
+        if (btid < nPb && ub0 + btid > u_out && ntab_b) ntab_b[cpos(ub0 + btid)] = nring[lidx(tb)];
       }
       // the next block's input-only factors (its slot (tau+1) mod 4 was last
       // read by the serial warp in block tau-3, which is done)
@@ -630,10 +614,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     // =====================================================================
     // serial warp(s)
     // =====================================================================
-    double mxr[CP == 32 ? 32 : 1];
-#pragma unroll
-    for (int q = 0; q < (CP == 32 ? 32 : 1); ++q)
-      mxr[q] = (CP == 32 && cv && q < C) ? mx[q * C + c] : 0.0;
     const double ecol = cv ? exp(colmax[c]) : 0.0;
     double dbk[2 * LP];  // Db[k] for k = 0 .. 2LP-1 (index 0 unused)
 #pragma unroll
@@ -643,33 +623,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         __syncwarp();
       else
         bar_sync(kBarSerial, CP);
-    };
-    auto matvec = [&](double a) -> double {
-      abuf[c] = cv ? a : 0.0;
-      sync_serial();
-      double y[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) y[q] = 0.0;
-      if (CP == 32) {
-        const double2* ab2 = reinterpret_cast<const double2*>(abuf);
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const double2 v = ab2[q];
-          y[(2 * q) & 7] = fma(v.x, mxr[2 * q], y[(2 * q) & 7]);
-          y[(2 * q + 1) & 7] = fma(v.y, mxr[2 * q + 1], y[(2 * q + 1) & 7]);
-        }
-      } else if (cv) {
-        const double2* ab2 = reinterpret_cast<const double2*>(abuf);
-#pragma unroll 4
-        for (int q = 0; q < CP / 2; ++q) {
-          const double2 v = ab2[q];
-          const int q0 = 2 * q, q1 = 2 * q + 1;
-          y[q0 & 7] = fma(v.x, q0 < C ? mx[q0 * C + c] : 0.0, y[q0 & 7]);
-          y[q1 & 7] = fma(v.y, q1 < C ? mx[q1 * C + c] : 0.0, y[q1 & 7]);
-        }
-      }
-      sync_serial();
-      return ((y[0] + y[1]) + (y[2] + y[3])) + ((y[4] + y[5]) + (y[6] + y[7]));
     };
     auto group_sumd = [&](double v) -> double {
 #pragma unroll
@@ -682,92 +635,158 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       return r;
     };
 
-    // near window: win[j] = E[u-1-j] for the next target u, j < NWIN, in the
-    // current block's frame (the far sums cover durations NWIN+1 and up)
-    constexpr int NWIN = 2 * LP - 1;
-    double win[NWIN];
-#pragma unroll
-    for (int j = 0; j < NWIN; ++j) win[j] = 0.0;
-    win[0] = cv ? ring[(R - 1) * Cs + c] : 0.0;  // position u_begin
     double a_last = a0;
     double n_last = 0.0;
-    for (int tau = 0; tau < NB; ++tau) {
-      const int bf = tau & 1, sl = tau & 3;
-      WT_ADD(12);
-      bar_sync(bf ? kBarFull1 : kBarFull0, NPART);
-      WT_ADD(8);
-      const int u0 = u_begin + 1 + tau * LP;
-      const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
-      const double n_tau = nring[lidx(tau)];
-      // the window's sources are in the previous blocks' frames: one factor
-      // w_{tau-1} brings all of them to this block's
-      const double wp = cv ? wprev[bf * CP + c] : 0.0;
+    // The block loop, instantiated for MV mat-vec terms (C rounded up to a
+    // multiple of 8 when one warp holds the labels, CP otherwise), so that a
+    // chain of C = 24 labels issues 24 float64 FMAs per position, not 32.
+    auto run_serial = [&](auto mv_tag) {
+      constexpr int MV = decltype(mv_tag)::value;
+      double mxr[CP == 32 ? MV : 1];
 #pragma unroll
-      for (int j = 0; j < NWIN; ++j) win[j] *= wp;
-      const double* far_b = farb + (size_t)bf * LP * CP + c;
-      const double* g_b = gb + (size_t)sl * LP * CP + c;
-      const double* h_b = hb + (size_t)sl * LP * CP + c;
-      // R = far sum + the window's terms of durations 2 .. NWIN+1 ... of the
-      // first target; the newest source's term (duration 1) is added when it
-      // is known
-      double rn;
-      {
-        double q4[4] = {cv ? far_b[0] : 0.0, 0.0, 0.0, 0.0};
+      for (int q = 0; q < (CP == 32 ? MV : 1); ++q)
+        mxr[q] = (CP == 32 && cv && q < C) ? mx[q * C + c] : 0.0;
+      auto matvec = [&](double a) -> double {
+        abuf[c] = cv ? a : 0.0;
+        sync_serial();
+        double y[8];
 #pragma unroll
-        for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j + 1], dbk[j + 2], q4[j & 3]);
-        rn = (q4[0] + q4[1]) + (q4[2] + q4[3]);
-      }
-      int slot = (tau % NR) * LP;  // slot of position u0: (u0 - 1) mod R
-      // one position per iteration, identical code for every position (a
-      // short loop body instead of a block-long unrolled sequence)
-#pragma unroll 1
-      for (int i = 0; i < nP; ++i) {
-        double a = 0.0;
-        const double gi = cv ? g_b[i * CP] : 0.0;
-        const double hcur = cv ? h_b[i * CP] : 0.0;
-        if (cv) {
-          const double S = fma(win[0], dbk[1], rn);
-          a = (S > 0.0) ? gi * S : 0.0;
+        for (int q = 0; q < 8; ++q) y[q] = 0.0;
+        if (CP == 32) {
+          const double2* ab2 = reinterpret_cast<const double2*>(abuf);
+#pragma unroll
+          for (int q = 0; q < MV / 2; ++q) {
+            const double2 v = ab2[q];
+            y[(2 * q) & 7] = fma(v.x, mxr[2 * q], y[(2 * q) & 7]);
+            y[(2 * q + 1) & 7] = fma(v.y, mxr[2 * q + 1], y[(2 * q + 1) & 7]);
+          }
+        } else if (cv) {
+          const double2* ab2 = reinterpret_cast<const double2*>(abuf);
+#pragma unroll 4
+          for (int q = 0; q < CP / 2; ++q) {
+            const double2 v = ab2[q];
+            const int q0 = 2 * q, q1 = 2 * q + 1;
+            y[q0 & 7] = fma(v.x, q0 < C ? mx[q0 * C + c] : 0.0, y[q0 & 7]);
+            y[q1 & 7] = fma(v.y, q1 < C ? mx[q1 * C + c] : 0.0, y[q1 & 7]);
+          }
         }
-        WT_ADD(9);
-        // the next target's R from the sources known now (its duration-1
-        // source is this position's, still to come), while the mat-vec runs
-        if (i + 1 < nP) {
-          double q4[4] = {cv ? far_b[(i + 1) * CP] : 0.0, 0.0, 0.0, 0.0};
+        sync_serial();
+        return ((y[0] + y[1]) + (y[2] + y[3])) + ((y[4] + y[5]) + (y[6] + y[7]));
+      };
+
+      // near window: win[j] = E[u-1-j] for the next target u, j < NWIN, in the
+      // current block's frame (the far sums cover durations NWIN+1 and up)
+      constexpr int NWIN = 2 * LP - 1;
+      double win[NWIN];
 #pragma unroll
-          for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j], dbk[j + 2], q4[j & 3]);
+      for (int j = 0; j < NWIN; ++j) win[j] = 0.0;
+      win[0] = cv ? ring[(R - 1) * Cs + c] : 0.0;  // position u_begin
+      for (int tau = 0; tau < NB; ++tau) {
+        const int bf = tau & 1, sl = tau & 3;
+        WT_ADD(12);
+        bar_sync(bf ? kBarFull1 : kBarFull0, NPART);
+        WT_ADD(8);
+        const int u0 = u_begin + 1 + tau * LP;
+        const int nP = (u_end - u0 + 1) < LP ? (u_end - u0 + 1) : LP;
+        const double n_tau = nring[lidx(tau)];
+        // the window's sources are in the previous blocks' frames: one factor
+        // w_{tau-1} brings all of them to this block's
+        const double wp = cv ? wprev[bf * CP + c] : 0.0;
+        const double* far_b = farb + (size_t)bf * LP * CP + c;
+        const double* g_b = gb + (size_t)sl * LP * CP + c;
+        const double* h_b = hb + (size_t)sl * LP * CP + c;
+        // the factors of the first two positions; each position then loads
+        // the ones two positions ahead, so that no shared-memory load (which
+        // queues behind the bulk warps' traffic) sits on the critical path
+        double gA = g_b[0], hA = h_b[0];
+        double gB = g_b[CP], hB = h_b[CP], fB = far_b[CP];
+#pragma unroll
+        for (int j = 0; j < NWIN; ++j) win[j] *= wp;
+        // R = far sum + the window's terms of durations 2 .. NWIN+1 ... of the
+        // first target; the newest source's term (duration 1) is added when it
+        // is known
+        double rn;
+        {
+          double q4[4] = {cv ? far_b[0] : 0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+          for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j + 1], dbk[j + 2], q4[j & 3]);
           rn = (q4[0] + q4[1]) + (q4[2] + q4[3]);
         }
-        const double ym = matvec(a);
-        WT_ADD(10);
-        double e = 0.0;
-        if (cv) {
-          e = (ym > 0.0) ? ym * hcur : 0.0;
-          ring[(slot + i) * Cs + c] = e;
-          stab[(sl * LP + i) * CP + c] = a;
-          stab[((4 + sl) * LP + i) * CP + c] = ym * ecol;
+        int slot = (tau % NR) * LP;  // slot of position u0: (u0 - 1) mod R
+        // one position per iteration, identical code for every position (a
+        // short loop body: a block-long unrolled sequence runs slower)
+#pragma unroll 1
+        for (int i = 0; i < nP; ++i) {
+          const double gi = gA, hcur = hA, fn = fB;
+          gA = gB;
+          hA = hB;
+          {
+            const int ip = i + 2 < LP ? i + 2 : LP - 1;  // in the block's buffers
+            gB = g_b[ip * CP];
+            hB = h_b[ip * CP];
+            fB = far_b[ip * CP];
+          }
+          WT_ADD(13);
+          double a = 0.0;
+          if (cv) {
+            const double S = fma(win[0], dbk[1], rn);
+            a = (S > 0.0) ? gi * S : 0.0;
+          }
+          WT_ADD(9);
+          // the next target's R from the sources known now (its duration-1
+          // source is this position's, still to come), while the mat-vec runs
+          if (i + 1 < nP) {
+            double q4[4] = {cv ? fn : 0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+            for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j], dbk[j + 2], q4[j & 3]);
+            rn = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+          }
+          const double ym = matvec(a);
+          WT_ADD(10);
+          double e = 0.0;
+          if (cv) {
+            e = (ym > 0.0) ? ym * hcur : 0.0;
+            ring[(slot + i) * Cs + c] = e;
+            // table rows straight to global memory (the load/store queue,
+            // not the shared-memory pipe the bulk warps keep busy)
+            if (u0 + i > u_out) {
+              const size_t row = (size_t)cpos(u0 + i) * C + c;
+              if (atab_b) atab_b[row] = a;
+              if (Atab_b) Atab_b[row] = ym * ecol;
+            }
+          }
+#pragma unroll
+          for (int j = NWIN - 1; j > 0; --j) win[j] = win[j - 1];
+          win[0] = e;
+          a_last = a;
+          WT_ADD(11);
         }
+        // the state at the end of the block, from which the bulk derives the
+        // block's scale for its normaliser prediction: its per-warp maxima when
+        // the bulk is the busier side (long duration windows), else the state
+        if (serial_scale) {
+          double mm = cv ? a_last : 0.0;
 #pragma unroll
-        for (int j = NWIN - 1; j > 0; --j) win[j] = win[j - 1];
-        win[0] = e;
-        a_last = a;
-        WT_ADD(11);
+          for (int o = 16; o > 0; o >>= 1) mm = fmax(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+          if (lane == 0) alast[bf * CP + warp] = mm;
+        } else {
+          alast[bf * CP + c] = cv ? a_last : 0.0;
+        }
+        n_last = n_tau;
+        // bar.arrive orders this block's ring and alast writes before the
+        // bulk warps' bar.sync on DONE (no fence: it would also wait for the
+        // table rows' global stores)
+        bar_arrive(bf ? kBarDone1 : kBarDone0, NPART);
       }
-      // the state at the end of the block, from which the bulk derives the
-      // block's scale for its normaliser prediction: its per-warp maxima when
-      // the bulk is the busier side (long duration windows), else the state
-      if (serial_scale) {
-        double mm = cv ? a_last : 0.0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mm = fmax(mm, __shfl_xor_sync(0xffffffffu, mm, o));
-        if (lane == 0) alast[bf * CP + warp] = mm;
-      } else {
-        alast[bf * CP + c] = cv ? a_last : 0.0;
-      }
-      n_last = n_tau;
-      __threadfence_block();
-      bar_arrive(bf ? kBarDone1 : kBarDone0, NPART);
-    }
+    };
+    if (CP == 32 && C <= 8)
+      run_serial(std::integral_constant<int, 8>{});
+    else if (CP == 32 && C <= 16)
+      run_serial(std::integral_constant<int, 16>{});
+    else if (CP == 32 && C <= 24)
+      run_serial(std::integral_constant<int, 24>{});
+    else
+      run_serial(std::integral_constant<int, 32>{});
     WT_FLUSH(8);
     // forward output: logZ = n(Lb) + log sum_c a[Lb,c] (the chunk that ends
     // the sequence; a later chunk fix-up adds the chunk's offset)
