@@ -58,6 +58,12 @@ def parse():
     ap.add_argument("--viterbi-only", action="store_true")
     # only the (K, C, C)-transition fwd+bwd sub-benchmark, at --batch / --seq-len
     ap.add_argument("--kcc-only", action="store_true")
+    ap.add_argument("--large-c-only", action="store_true",
+                    help="only configuration 4's fwd+bwd (B=32 T=4096 K=64 C=256), for "
+                         "profiler captures; with --batch/--seq-len below the defaults, "
+                         "that smaller shape")
+    ap.add_argument("--probe-only", action="store_true",
+                    help="only the float64 FMA / tensor-core rate probes")
     ap.add_argument("--batch", type=int, default=B)
     ap.add_argument("--seq-len", type=int, default=T)
     return ap.parse_args()
@@ -365,8 +371,31 @@ def fp64_probe(dev):
     assert lib.semicrf_probe_fp64_latency(1024, ctypes.c_void_p(cyc.data_ptr()),
                                           ctypes.c_void_p(o32.data_ptr()), st) == 0
     torch.cuda.synchronize()
+    dfma_lat = float(cyc) / (1024 * 16)
+    # the float64 tensor-core path (mma.sync m8n8k4 f64), the candidate for
+    # the large-C contraction: throughput and dependent latency
+    lib.semicrf_probe_dmma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_void_p]
+    lib.semicrf_probe_dmma_latency.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_void_p]
+    dbest = None
+    diters = 1024
+    for _ in range(4):
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        assert lib.semicrf_probe_dmma(grid, diters, ctypes.c_void_p(out.data_ptr()), st) == 0
+        b_.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b_)
+        dbest = ms if dbest is None else min(dbest, ms)
+    dfmas = grid * (nt // 32) * diters * 16 * 256
+    assert lib.semicrf_probe_dmma_latency(256, ctypes.c_void_p(cyc.data_ptr()),
+                                          ctypes.c_void_p(o32.data_ptr()), st) == 0
+    torch.cuda.synchronize()
     return {"fp64_tflops": 2 * fmas / (best / 1e3) / 1e12,
-            "dfma_latency_cycles": float(cyc) / (1024 * 16),
+            "dfma_latency_cycles": dfma_lat,
+            "fp64_tensor_tflops": 2 * dfmas / (dbest / 1e3) / 1e12,
+            "dmma_latency_cycles": float(cyc) / (256 * 16),
             "how": f"{grid} CTAs x {nt} threads x 8 independent FMA chains x {iters * 4} "
                    "FMAs, best of 4, CUDA events (probe.cu); latency: one warp, one chain, "
                    "clock64"}
@@ -392,6 +421,18 @@ def main():
         if rank == 0:
             flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
             print(json.dumps(bench_viterbi(dev, flush)), flush=True)
+        return
+    if args.large_c_only:
+        if rank == 0:
+            flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+            bc = 32 if B == 64 else B
+            tc = 4096 if T == 10000 else T
+            print(json.dumps(bench_fwd_bwd(dev, flush, "cfg4", bc, tc, 64, 256, 4,
+                                           f"cfg4: B={bc} T={tc} K=64 C=256")), flush=True)
+        return
+    if args.probe_only:
+        if rank == 0:
+            print(json.dumps(fp64_probe(dev)), flush=True)
         return
     if args.kcc_only:
         if rank == 0:
@@ -665,6 +706,8 @@ def main():
                              "peak": probe["fp64_tflops"], "frac": fp64_tf / probe["fp64_tflops"],
                              "peak_source": "measured in this run: " + probe["how"],
                              "dfma_latency_cycles": probe["dfma_latency_cycles"],
+                             "fp64_tensor_tflops": probe["fp64_tensor_tflops"],
+                             "dmma_latency_cycles": probe["dmma_latency_cycles"],
                              "ns_per_position_step": t_fwd / int(lengths_h.max()) * 1e9,
                              "ctas": 2 * Bl, "sms": nsm,
                              "note": "the factorised recurrence's float64 FMAs (C*C + (K-1)*C "

@@ -21,6 +21,9 @@
 // re-referenced per tile of targets so that both stay inside float64 range.
 // Partials are per (sequence, chunk) and summed in a fixed order: no atomics.
 
+#include <cstdlib>
+#include <cstring>
+
 #include "semicrf_internal.cuh"
 
 namespace semicrf {
@@ -217,6 +220,129 @@ __global__ void __launch_bounds__(kMT) lmarg_tr_kernel(const LMargArgs a) {
       const int cs = pr * PB + ty * RT + p, cd = pc * PB + tx * RT + q;
       if (cs < C && cd < C) out[(size_t)cs * C + cd] = acc[p][q];
     }
+}
+
+// ---- transition partials on the float64 tensor cores (C > 64) -------------
+// The same sums as lmarg_tr_kernel, as a GEMM over positions: per (pair block,
+// chunk, sequence) D[c'][c] += sum_t (xa[t][c'] f_t) ya[t][c] with mma.sync
+// m8n8k4 f64 (8 x 8 tiles, 4 positions per step, float64 products and sums).
+// A CTA holds a 128 x 128 pair block: 8 warps of 32 x 64 (4 x 8 MMA tiles,
+// 64 accumulators per lane).  Positions arrive kTMS at a time through a
+// kTMN-stage cp.async pipeline (raw table rows, zero-filled past the chunk or
+// the label range); f_t scales the A fragments in registers.  Rows are
+// kTMR = 132 doubles apart, so that a fragment load (lane = 4 * column + step
+// row) touches 16 distinct bank pairs per half warp.
+constexpr int kTM = 128, kTMS = 16, kTMR = kTM + 4, kTMN = 3;
+
+__device__ __forceinline__ void dmma_884(double& d0, double& d1, double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+               : "+d"(d0), "+d"(d1)
+               : "d"(a), "d"(b));
+}
+__device__ __forceinline__ void tm_cp8(double* dst, const double* src, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(src),
+               "r"(valid ? 8 : 0)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kMT) lmarg_trmma_kernel(const LMargArgs a) {
+  extern __shared__ __align__(16) double tsm[];
+  // stage s: xs [kTMS][kTMR], ys [kTMS][kTMR], fs [kTMS]
+  constexpr int kStage = 2 * kTMS * kTMR + kTMS;
+  const int C = a.C, T = a.T;
+  const int npb = (C + kTM - 1) / kTM;
+  const int pr = blockIdx.x / npb, pc = blockIdx.x % npb;
+  const int ch = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = warp >> 1, wn = warp & 1;  // 4 x 2 warps of 32 x 64
+  const int fr = lane & 3, fc = lane >> 2;  // fragment step row, column
+  const int Lb = seq_len(a.lengths, b, T);
+  const int per = (T + a.nchunk - 1) / a.nchunk;
+  const int t_lo = ch * per;
+  const int t_hi = min(t_lo + per, Lb);
+  const int nst = t_hi > t_lo ? (t_hi - t_lo + kTMS - 1) / kTMS : 0;
+  const double lz = a.logz[b];
+  const size_t rowb = (size_t)b * (T + 1);
+  const double* xa_b = a.xa + rowb * C;
+  const double* ya_b = a.ya + rowb * C;
+  // issue stage st into buffer st % kTMN (one commit group per stage, empty
+  // groups past the end keep the group count uniform)
+  auto issue = [&](int st) {
+    if (st < nst) {
+      double* xs = tsm + (st % kTMN) * kStage;
+      double* ys = xs + kTMS * kTMR;
+      double* fs = ys + kTMS * kTMR;
+      const int t0 = t_lo + st * kTMS;
+      for (int e = tid; e < kTMS * kTM; e += kMT) {
+        const int i = e / kTM, q = e % kTM;
+        const int cs = pr * kTM + q, cd = pc * kTM + q;
+        const bool in = t0 + i < t_hi;
+        const size_t row = (size_t)(t0 + i) * C;
+        tm_cp8(xs + i * kTMR + q, xa_b + (in && cs < C ? row + cs : 0), in && cs < C);
+        tm_cp8(ys + i * kTMR + q, ya_b + (in && cd < C ? row + cd : 0), in && cd < C);
+      }
+      if (tid < kTMS) {
+        const int t = t0 + tid;
+        fs[tid] = t < t_hi ? exp(a.xn[rowb + t] + a.yn[rowb + t] - lz) : 0.0;
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  double d[4][8][2];
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 8; ++ni) d[mi][ni][0] = d[mi][ni][1] = 0.0;
+#pragma unroll
+  for (int st = 0; st < kTMN - 1; ++st) issue(st);
+  for (int st = 0; st < nst; ++st) {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kTMN - 2) : "memory");
+    __syncthreads();  // stage st is in place; the buffer of st - 1 is free
+    issue(st + kTMN - 1);
+    const double* xs = tsm + (st % kTMN) * kStage;
+    const double* ys = xs + kTMS * kTMR;
+    const double* fs = ys + kTMS * kTMR;
+#pragma unroll
+    for (int kk = 0; kk < kTMS / 4; ++kk) {
+      const int r = (kk * 4 + fr) * kTMR;
+      const double f = fs[kk * 4 + fr];
+      double av[4], bv[8];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi) av[mi] = xs[r + wm * 32 + mi * 8 + fc] * f;
+#pragma unroll
+      for (int ni = 0; ni < 8; ++ni) bv[ni] = ys[r + wn * 64 + ni * 8 + fc];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 8; ++ni) dmma_884(d[mi][ni][0], d[mi][ni][1], av[mi], bv[ni]);
+    }
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  // D fragment: row fc, columns 2 fr and 2 fr + 1 of each 8 x 8 tile
+  double* out = a.part_tr + ((size_t)b * a.nchunk + ch) * C * C;
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 8; ++ni) {
+      const int cs = pr * kTM + wm * 32 + mi * 8 + fc;
+      const int cd = pc * kTM + wn * 64 + ni * 8 + 2 * fr;
+      if (cs < C && cd < C) out[(size_t)cs * C + cd] = d[mi][ni][0];
+      if (cs < C && cd + 1 < C) out[(size_t)cs * C + cd + 1] = d[mi][ni][1];
+    }
+}
+
+// The transition-partial kernel for C > 64: the tensor-core GEMM unless the
+// environment variable SEMICRF_TRANSITION_GEMM=fma selects the CUDA-core
+// kernel (the measured comparison of the two is this switch's purpose).
+bool tr_use_mma(int C) {
+  if (C <= 64) return false;
+  static int choice = -1;
+  if (choice < 0) {
+    const char* v = getenv("SEMICRF_TRANSITION_GEMM");
+    choice = (v && strcmp(v, "fma") == 0) ? 0 : 1;
+  }
+  return choice == 1;
 }
 
 // ---- block-relative linear factors ----------------------------------------
@@ -480,9 +606,12 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
   const int kcap = K > 1 ? K - 1 : 1;
   const int sms = device_sm_count();
   // transition partials
-  const int pb = C <= 32 ? 32 : 64;
+  const int pb = C <= 32 ? 32 : (tr_use_mma(C) ? kTM : 64);
   const int npb = (C + pb - 1) / pb;
-  int nch = (2 * sms + B * npb * npb - 1) / (B * npb * npb);
+  // two CTAs per SM for the CUDA-core kernels; one wave of one CTA per SM
+  // for the tensor-core kernel (its 64 accumulators per lane fill the registers)
+  int nch = pb == kTM ? sms / (B * npb * npb)
+                      : (2 * sms + B * npb * npb - 1) / (B * npb * npb);
   const int maxch = (T + 255) / 256;
   if (nch > maxch) nch = maxch;
   if (nch < 1) nch = 1;
@@ -544,6 +673,13 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   } else if (a.C <= 32) {
     const int npb = (a.C + 31) / 32;
     lmarg_tr_kernel<2><<<dim3(npb * npb, a.nchunk, a.B), kMT, 0, s>>>(a);
+  } else if (tr_use_mma(a.C)) {
+    const int npb = (a.C + kTM - 1) / kTM;
+    const int smem = kTMN * (2 * kTMS * kTMR + kTMS) * 8;
+    e = cudaFuncSetAttribute(lmarg_trmma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem);
+    if (e != cudaSuccess) return e;
+    lmarg_trmma_kernel<<<dim3(npb * npb, a.nchunk, a.B), kMT, smem, s>>>(a);
   } else {
     const int npb = (a.C + 63) / 64;
     lmarg_tr_kernel<4><<<dim3(npb * npb, a.nchunk, a.B), kMT, 0, s>>>(a);
