@@ -98,8 +98,9 @@ enum semicrf_backward_mode { SEMICRF_KEEP_ALPHA = 0, SEMICRF_RECOMPUTE = 1 };
 /* _compute_checkpoint_interval: max(K, floor(sqrt(T*K))). */
 int64_t semicrf_checkpoint_interval(int64_t T, int64_t K);
 
-/* Bytes of state semicrf_forward keeps for semicrf_backward (float64 log-Z
- * and the normalised ring checkpoints). */
+/* Bytes of state semicrf_forward keeps for semicrf_backward: the float64
+ * log partition (B,) first, then the chain tables (SEMICRF_KEEP_ALPHA) or the
+ * normalised restart records (SEMICRF_RECOMPUTE). */
 size_t semicrf_saved_size(const semicrf_problem* p);
 size_t semicrf_forward_workspace_size(const semicrf_problem* p);
 
@@ -107,7 +108,9 @@ size_t semicrf_forward_workspace_size(const semicrf_problem* p);
  * NULL, the ring buffer of alpha at every multiple of S in the reference
  * layout (B, num_ring_checkpoints, K, C) (NEG_INF = -1e9 where unset;
  * checkpoint 0 holds alpha[0] = 0 in slot 0).  When saved is not NULL the
- * state needed by semicrf_backward is written there. */
+ * state needed by semicrf_backward is written there; in the log semiring with
+ * SEMICRF_KEEP_ALPHA the ring checkpoints are then read off the kept alpha
+ * tables after the chains have run. */
 int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_checkpoints,
                     int64_t num_ring_checkpoints, void* saved, void* workspace,
                     size_t workspace_bytes, void* stream);

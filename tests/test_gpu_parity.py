@@ -590,3 +590,41 @@ def test_backward_launcher_raw(proj, oracle):
     with pytest.raises(ValueError):  # log Z of other inputs
         launch_streaming_triton_backward(cum, tr, db, lengths, part + 1.0, ck, S, gout,
                                          proj_start=ps, proj_end=pe)
+
+
+def test_backward_launcher_reuses_forward_state(monkeypatch, oracle):
+    """launch_streaming_triton_backward given the ring checkpoints that
+    launch_streaming_triton_kernel returned runs no forward: it uses the float64
+    state kept beside them.  After an in-place change of an input it recomputes
+    (and then rejects the stale log Z)."""
+    from inputs import make_streaming_inputs
+
+    from torch_semimarkov_b200 import (_lib, launch_streaming_triton_backward,
+                                       launch_streaming_triton_kernel)
+
+    dev = _dev()
+    B, T, K, C = 3, 200, 12, 6
+    inp = make_streaming_inputs(B, T, K, C, seed=62)
+    cum, tr, db = (inp[k].to(dev) for k in ("cum_scores", "transition", "duration_bias"))
+    lengths = torch.tensor([T, 150, 77], device=dev)
+    part, ck, S = launch_streaming_triton_kernel(cum, tr, db, lengths, K)
+    gout = torch.tensor([1.0, -0.5, 2.0], device=dev)
+    calls = []
+    real_forward = _lib.forward
+    monkeypatch.setattr(_lib, "forward", lambda *a, **k: calls.append(1) or real_forward(*a, **k))
+    gc, gt, gd, _, _ = launch_streaming_triton_backward(cum, tr, db, lengths, part, ck, S, gout)
+    assert not calls, "the backward launcher reran the forward"
+    np_in = {k: (None if v is None else v.numpy()) for k, v in inp.items()}
+    z_ref, ref = oracle.forward_backward(np_in["cum_scores"], np_in["transition"],
+                                         np_in["duration_bias"], lengths.cpu().numpy(), K,
+                                         grad_output=gout.cpu().numpy())
+    np.testing.assert_allclose(part.cpu().numpy(), z_ref, rtol=1e-5, atol=1e-5)
+    assert_grad_close(gc.cpu().numpy(), ref["cum_scores"], what="grad_cum")
+    assert_grad_close(gt.cpu().numpy(), ref["transition"], what="grad_transition")
+    assert_grad_close(gd.cpu().numpy(), ref["duration_bias"], what="grad_duration_bias")
+    # the inputs changed after the forward: state is recomputed, and the old
+    # log Z no longer belongs to them
+    cum.add_(0.5 * torch.arange(T + 1, device=dev, dtype=cum.dtype).view(1, -1, 1) / T)
+    with pytest.raises(ValueError):
+        launch_streaming_triton_backward(cum, tr, db, lengths, part, ck, S, gout)
+    assert calls, "changed inputs must be recomputed"

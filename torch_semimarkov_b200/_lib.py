@@ -303,6 +303,12 @@ def forward(prob: Problem, want_saved: bool, num_ring_checkpoints: int = 0):
     return part, ck, saved
 
 
+def saved_log_partition(prob: Problem, saved: torch.Tensor) -> torch.Tensor:
+    """The float64 log partition (B,) a log-semiring forward stored at the
+    start of its saved state (semicrf_saved_size: log Z comes first)."""
+    return saved[: 8 * prob.B].view(torch.float64)
+
+
 def backward(prob: Problem, saved: torch.Tensor, grad_output: torch.Tensor):
     """Run semicrf_backward.  Returns (grad_cum, grad_tr, grad_db, grad_ps, grad_pe)."""
     lib = load()

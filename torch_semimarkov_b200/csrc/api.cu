@@ -430,6 +430,58 @@ size_t semicrf_forward_workspace_size(const semicrf_problem* p) {
   return cv.bytes();
 }
 
+namespace {
+
+// Reference-layout ring checkpoints (triton_forward.py:554-714: checkpoint i
+// holds alpha of the K positions ending at i*S, slot p % K; unset entries are
+// NEG_INF; checkpoint 0 holds alpha[0] = 0) from the kept float64 alpha tables
+// (a = exp(alpha - n)).  The same entries as the generic chain writes when it
+// produces them itself: position u >= 1 goes to checkpoint ceil(u / S) if that
+// checkpoint lies at or before the sequence end and within K - 1 of u.
+__global__ void rings_from_tables_kernel(const double* a_tab, const double* n_tab,
+                                         const int64_t* lengths, float* rings, int B, int T,
+                                         int K, int C, int nref, int S) {
+  const size_t total = (size_t)B * nref * K * C;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const int slot = (int)((i / C) % K);
+    const int ic = (int)((i / ((size_t)C * K)) % nref);
+    const int b = (int)(i / ((size_t)C * K * nref));
+    const long long lraw = lengths[b];
+    const int Lb = lraw < 0 ? 0 : (lraw > T ? T : (int)lraw);
+    float v = kRefNegInf;
+    if (ic == 0) {
+      if (slot == 0) v = 0.f;
+    } else if ((long long)ic * S <= Lb) {
+      // the position of this slot in (ic*S - K, ic*S]
+      const int top = ic * S;
+      int u = top - ((top - slot) % K + K) % K;
+      if (u >= 1 && u > top - K && u > (ic - 1) * S) {
+        const size_t row = (size_t)b * (T + 1) + u;
+        const double a = a_tab[row * C + c];
+        v = a > 0.0 ? (float)(log(a) + n_tab[row]) : kRefNegInf;
+      }
+    }
+    rings[i] = v;
+  }
+}
+
+cudaError_t launch_rings_from_tables(const semicrf_problem* p, const double* a_tab,
+                                     const double* n_tab, float* rings, int nref,
+                                     cudaStream_t s) {
+  const size_t total = (size_t)p->batch * nref * p->K * p->C;
+  if (total == 0) return cudaSuccess;
+  int g = (int)((total + 255) / 256);
+  if (g > device_sm_count() * 8) g = device_sm_count() * 8;
+  rings_from_tables_kernel<<<g, 256, 0, s>>>(a_tab, n_tab, p->lengths, rings, (int)p->batch,
+                                             (int)p->T, (int)p->K, (int)p->C, nref,
+                                             (int)p->checkpoint_interval);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
 int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_checkpoints,
                     int64_t num_ring_checkpoints, void* saved, void* workspace,
                     size_t workspace_bytes, void* stream) {
@@ -504,6 +556,19 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     L.a1 = a;
     L.n1 = (int)p->batch;
     int grid = (int)p->batch;
+    if (saved && p->backward_mode != SEMICRF_RECOMPUTE && ring_checkpoints) {
+      // keep mode with the reference-layout checkpoints: the chains run as
+      // without them (whole or time-chunked, warp-specialised or clustered)
+      // and the checkpoints are then read off the kept alpha tables
+      semicrf_problem q = *p;
+      const int st = semicrf_forward(&q, partition, nullptr, 0, saved, workspace,
+                                     workspace_bytes, stream);
+      if (st != SEMICRF_OK) return st;
+      Carver sc(saved);
+      SavedLayout sl = carve_saved(sc, p);
+      return cuda_status(launch_rings_from_tables(p, sl.a_tab, sl.n_tab, ring_checkpoints,
+                                                  (int)num_ring_checkpoints, s));
+    }
     if (saved) {
       Carver sc(saved);
       SavedLayout sl = carve_saved(sc, p);

@@ -121,7 +121,7 @@ __host__ __device__ inline void ws_make(WsPlan& p, int C, int K, int CP, int LP)
   p.o_h = take(8 * 4 * LP * CP);
   p.o_wprev = take(8 * 2 * CP);
   p.o_part = take(8 * p.nsplit * LP * p.Cs);
-  p.o_abuf = take(8 * CP);
+  p.o_abuf = take(8 * 2 * CP);  // two exchange buffers (alternating positions)
   p.o_wt = take(8 * 2 * p.nwt * p.Cs);  // W tables of the last two prepared blocks
   p.o_misc = take(8 * 16);
   p.o_edb = take(8 * CP);
@@ -646,14 +646,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
       for (int q = 0; q < (CP == 32 ? MV : 1); ++q)
         mxr[q] = (CP == 32 && cv && q < C) ? mx[q * C + c] : 0.0;
-      auto matvec = [&](double a) -> double {
-        abuf[c] = cv ? a : 0.0;
+      // the mat-vec in two halves: publish this lane's a into the exchange
+      // buffer of parity par, then (after independent work) read the whole
+      // vector and form ym.  The buffers alternate by position, so no
+      // barrier is needed after the reads: a lane writes buffer par again
+      // only two positions later, past the next position's barrier, which
+      // every lane reaches after its reads of this one.
+      auto mv_publish = [&](double a, int par) { abuf[par * CP + c] = cv ? a : 0.0; };
+      auto mv_finish = [&](int par) -> double {
+        const double* ab = abuf + par * CP;
         sync_serial();
         double y[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) y[q] = 0.0;
         if (CP == 32) {
-          const double2* ab2 = reinterpret_cast<const double2*>(abuf);
+          const double2* ab2 = reinterpret_cast<const double2*>(ab);
 #pragma unroll
           for (int q = 0; q < MV / 2; ++q) {
             const double2 v = ab2[q];
@@ -661,7 +668,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             y[(2 * q + 1) & 7] = fma(v.y, mxr[2 * q + 1], y[(2 * q + 1) & 7]);
           }
         } else if (cv) {
-          const double2* ab2 = reinterpret_cast<const double2*>(abuf);
+          const double2* ab2 = reinterpret_cast<const double2*>(ab);
 #pragma unroll 4
           for (int q = 0; q < CP / 2; ++q) {
             const double2 v = ab2[q];
@@ -670,7 +677,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             y[q1 & 7] = fma(v.y, q1 < C ? mx[q1 * C + c] : 0.0, y[q1 & 7]);
           }
         }
-        sync_serial();
         return ((y[0] + y[1]) + (y[2] + y[3])) + ((y[4] + y[5]) + (y[6] + y[7]));
       };
 
@@ -681,6 +687,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
       for (int j = 0; j < NWIN; ++j) win[j] = 0.0;
       win[0] = cv ? ring[(R - 1) * Cs + c] : 0.0;  // position u_begin
+      int mpar = 0;
       for (int tau = 0; tau < NB; ++tau) {
         const int bf = tau & 1, sl = tau & 3;
         WT_ADD(12);
@@ -732,16 +739,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             const double S = fma(win[0], dbk[1], rn);
             a = (S > 0.0) ? gi * S : 0.0;
           }
+          mv_publish(a, mpar);
           WT_ADD(9);
           // the next target's R from the sources known now (its duration-1
-          // source is this position's, still to come), while the mat-vec runs
+          // source is this position's, still to come), while the published
+          // values become visible
           if (i + 1 < nP) {
             double q4[4] = {cv ? fn : 0.0, 0.0, 0.0, 0.0};
 #pragma unroll
             for (int j = 0; j + 1 < NWIN; ++j) q4[j & 3] = fma(win[j], dbk[j + 2], q4[j & 3]);
             rn = (q4[0] + q4[1]) + (q4[2] + q4[3]);
           }
-          const double ym = matvec(a);
+          const double ym = mv_finish(mpar);
+          mpar ^= 1;
           WT_ADD(10);
           double e = 0.0;
           if (cv) {
