@@ -514,6 +514,26 @@ def test_large_emission_scale_vs_oracle(scale, kcc, semiring, oracle):
     _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, semiring, oracle)
 
 
+@pytest.mark.parametrize("scale", [5.0, 60.0])
+@pytest.mark.parametrize("C", [6, 40])
+def test_recompute_mode_large_scale_vs_oracle(scale, C, oracle, monkeypatch):
+    """The memory-light backward (restart records every S' positions, tables
+    rebuilt in the backward) at emission scales whose float64 frames clip
+    (N(0, 60^2)): the forward flags it in the saved state, corrects log Z in
+    the log domain, and the backward rebuilds both chains' tables in the log
+    domain; at N(0, 5^2) nothing clips."""
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_BACKWARD", "recompute")
+    B, T, K = 2, 160, 20
+    g = torch.Generator().manual_seed(13)
+    em = torch.randn(B, T, C, generator=g, dtype=torch.float64) * scale
+    cum = torch.cat([torch.zeros(B, 1, C, dtype=torch.float64), em.cumsum(1)], 1).float()
+    tr = (torch.randn(C, C, generator=g, dtype=torch.float64) * 0.1).float()
+    db = (torch.randn(K, C, generator=g, dtype=torch.float64) * 0.1).float()
+    inp = {"cum_scores": cum, "transition": tr, "duration_bias": db, "proj_start": None,
+           "proj_end": None}
+    _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, "log", oracle)
+
+
 @pytest.mark.parametrize("C", [96, 256])
 def test_cluster_chain_large_scale_vs_oracle(C, oracle):
     """64 < C <= 256 runs the cluster chain; with emissions N(0, 60^2) its factors

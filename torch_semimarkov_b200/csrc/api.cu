@@ -113,6 +113,7 @@ struct SavedLayout {
   ChunkPlan cp;    // time chunks of the two chains (keep mode)
   double *hand_a, *hand_b, *rdiff, *dofs;
   int *okf, *fail;
+  int* rec_ovf;    // SEMICRF_RECOMPUTE: set when the forward's float64 frames clipped
 };
 
 ChunkPlan keep_chunk_plan(const semicrf_problem* p) {
@@ -138,6 +139,7 @@ SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
     s.sv_d = cv.take<double>(B * nint * kc);
   } else if (p->backward_mode == SEMICRF_RECOMPUTE) {
     s.sv = cv.take<double>(B * nint * lchain_saved_doubles((int)p->C, (int)p->K));
+    s.rec_ovf = cv.take<int>(1);
   } else {
     const size_t n = B * (p->T + 1) * C;
     s.a_tab = cv.take<double>(n);
@@ -556,6 +558,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
     L.a1 = a;
     L.n1 = (int)p->batch;
     int grid = (int)p->batch;
+    int* rec_ovf = nullptr;
     if (saved && p->backward_mode != SEMICRF_RECOMPUTE && ring_checkpoints) {
       // keep mode with the reference-layout checkpoints: the chains run as
       // without them (whole or time-chunked, warp-specialised or clustered)
@@ -576,6 +579,7 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
       if (p->backward_mode == SEMICRF_RECOMPUTE) {
         L.a0.sv = sl.sv;
         L.a0.write_saved = 1;
+        rec_ovf = sl.rec_ovf;
       } else {
         // keep both chains' tables: the beta chain does not depend on alpha,
         // so it runs beside the alpha chain in the same launch
@@ -624,12 +628,16 @@ int semicrf_forward(const semicrf_problem* p, float* partition, float* ring_chec
       return cuda_status(launch_lchain_fix(L, grid, s));
     }
     // the generic chain: the same rerun for whole chains (ring checkpoints
-    // included); the recompute-mode forward keeps linear checkpoints and has none
-    const bool fix = !L.a0.write_saved && lchain_fix_supported((int)p->C, (int)p->K);
-    if (fix) {
+    // included).  In the recompute mode the flag lives in the saved state: the
+    // rerun corrects log Z and the partition here, and the backward, finding
+    // the flag set, rebuilds its tables in the log domain instead of from the
+    // (clipped) restart records.
+    const bool fix = lchain_fix_supported((int)p->C, (int)p->K);
+    int* ovf = rec_ovf ? rec_ovf : pr.ovf;
+    if (fix || rec_ovf) {
       L.dbl = pr.dbl;
-      L.ovf = pr.ovf;
-      if (cudaMemsetAsync(pr.ovf, 0, sizeof(int), s) != cudaSuccess) return SEMICRF_ERR_CUDA;
+      L.ovf = ovf;
+      if (cudaMemsetAsync(ovf, 0, sizeof(int), s) != cudaSuccess) return SEMICRF_ERR_CUDA;
     }
     cudaError_t e2 = launch_lchain(L, grid, s);
     if (e2 != cudaSuccess || !fix) return cuda_status(e2);
@@ -752,6 +760,14 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
       r.A_tab = w.A_tab;
       r.n_tab = w.n_tab;
       const LChainArgs bb = beta_chain_args(p, w.pr, w.b_tab, w.B_tab, w.m_tab);
+      if (lchain_fix_supported((int)p->C, (int)p->K)) {
+        // start from the forward's flag; the launches below may set it too
+        L.dbl = w.pr.dbl;
+        L.ovf = w.pr.ovf;
+        if (cudaMemcpyAsync(w.pr.ovf, sl.rec_ovf, sizeof(int), cudaMemcpyDeviceToDevice, s) !=
+            cudaSuccess)
+          return SEMICRF_ERR_CUDA;
+      }
       L.a0 = r;
       L.n1 = (int)p->batch * r.nint;
       if (lchain_ws_supported((int)p->C, (int)p->K)) {
@@ -768,6 +784,19 @@ int semicrf_backward(const semicrf_problem* p, const void* saved, const float* g
         e = launch_lchain(L, L.n1 + (int)p->batch, s);
       }
       if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+      if (lchain_fix_supported((int)p->C, (int)p->K)) {
+        // frames that clipped, in the forward (its flag, saved) or in the
+        // recompute above: both chains again, whole, in the log domain,
+        // rewriting the tables (log Z is the forward's, already corrected)
+        LChainLaunch Lf = L;
+        Lf.a0 = r;
+        Lf.a0.mode = 0;
+        Lf.a0.sv = nullptr;
+        Lf.a1 = bb;
+        Lf.n1 = (int)p->batch;
+        e = launch_lchain_fix(Lf, 2 * (int)p->batch, s);
+        if (e != cudaSuccess) return SEMICRF_ERR_CUDA;
+      }
       xa = w.a_tab;
       xA = w.A_tab;
       xn = w.n_tab;
