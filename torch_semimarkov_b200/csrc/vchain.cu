@@ -17,14 +17,18 @@
 // E[s,c] = sv[s,c] - cum[s,c], so a candidate is E[t-k,c] + db[k,c] and the
 // common cum[t,c] is added to the winner only.
 //
-// Lane c of the warp owns label c.  Its ring of the last K' positions lives
-// in per-warp shared memory that only that lane reads and writes, so the
-// recurrence needs no barrier.  The duration maximum is a tree over groups of
-// 16 candidates (all loaded and added independently, then 4 levels of
-// compare-select that keep the smaller k on ties), the groups combined in
-// order; the label maximum m is NC shuffles and the same stable tree.
-// Several sequences run per CTA, one per warp, so a batch of B sequences is B
-// warps across the GPU.
+// Lane c of the warp owns label c; for C <= 16 lanes c and c + 16 both do,
+// and each takes half of every maximum (durations 1..KM/2 and KM/2+1..KM,
+// source labels 0..NC/2-1 and NC/2..NC-1), the halves joined by one
+// shuffle that keeps the lower half on ties, so a position costs each lane
+// half the candidates.  The ring of the last K' positions lives in per-warp
+// shared memory that only the lanes of that label read (and the lower lane
+// writes), so the recurrence needs no barrier.  A duration maximum is a tree
+// over groups of up to 16 candidates (all loaded and added independently,
+// then compare-select levels that keep the smaller k on ties), the groups
+// combined in order; the label maximum m is shuffles and the same stable
+// tree.  Several sequences run per CTA, one per warp, so a batch of B
+// sequences is B warps across the GPU.
 
 #include "semicrf_internal.cuh"
 
@@ -84,9 +88,12 @@ template <int NC, int KM>
 __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArgs a, int kcap,
                                                                  int R, int wpb) {
   extern __shared__ __align__(16) double vsm[];
-  constexpr int KG = 16;               // candidates per tree
-  constexpr int NG = KM / KG;          // groups
-  constexpr bool kDbReg = KM <= 32;    // duration biases in registers
+  constexpr bool HALF = NC <= 16;      // two lanes per label, each half the candidates
+  constexpr int KH = HALF ? KM / 2 : KM;  // durations per lane
+  constexpr int NQ = HALF ? NC / 2 : NC;  // source labels per lane
+  constexpr int KG = KH < 16 ? KH : 16;   // candidates per tree
+  constexpr int NG = KH / KG;             // groups
+  constexpr bool kDbReg = KM <= 32;       // duration biases in registers
   const int C = a.C, K = a.K, T = a.T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   double* dbl = vsm;  // [kcap + 1][C], row k = db[min(k, K-1)]
@@ -106,8 +113,10 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
                                              (size_t)wpb * 2 * R * C) + (size_t)warp * R * C;
   for (int i = lane; i < 2 * R * C; i += 32) ring[i] = kDNegInf;
   __syncwarp();
-  const int c = lane;
+  const int c = HALF ? (lane & 15) : lane;
+  const int hf = HALF ? lane >> 4 : 0;  // which half of the candidates
   const bool cv = c < C;
+  const bool wr = cv && hf == 0;        // the lane that writes label c's outputs
   const int Rm = R - 1;
   const long long lraw = a.lengths[b];
   const int Lb = lraw < 0 ? 0 : (lraw > T ? T : (int)lraw);
@@ -116,27 +125,45 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
   uint8_t* bpc_b = a.bp_c ? a.bp_c + (size_t)b * (T + 1) * C : nullptr;
   uint16_t* bp_b = a.bp ? a.bp + (size_t)b * (T + 1) * C : nullptr;
 
-  // column c of the transition matrix (sources q), -inf beyond C
-  double trc[NC];
+  // this lane's sources q = hf*NQ + j of column c of the transition matrix,
+  // -inf beyond C
+  double trc[NQ];
 #pragma unroll
-  for (int q = 0; q < NC; ++q)
-    trc[q] = (cv && q < C) ? (double)a.tr[(size_t)q * C + c] : kDNegInf;
-  // duration-bias row of label c (k = 0 .. KM; -inf outside 1 .. kcap)
-  double dbr[kDbReg ? KM + 1 : 1];
+  for (int j = 0; j < NQ; ++j) {
+    const int q = hf * NQ + j;
+    trc[j] = (cv && q < C) ? (double)a.tr[(size_t)q * C + c] : kDNegInf;
+  }
+  // this lane's durations k = hf*KH + j (j = 1 .. KH) of label c's bias row,
+  // -inf outside 1 .. kcap
+  double dbr[kDbReg ? KH + 1 : 1];
 #pragma unroll
-  for (int k = 0; k < (kDbReg ? KM + 1 : 1); ++k)
-    dbr[k] = (kDbReg && cv && k >= 1 && k <= kcap) ? dbl[k * C + c] : kDNegInf;
-
-  // m = max_q (x_q + tr[q,c]) and its first maximiser
-  auto label_max = [&](double x, int& arg) -> double {
-    double v[NC];
-    int ix[NC];
-#pragma unroll
-    for (int q = 0; q < NC; ++q) {
-      v[q] = __shfl_sync(0xffffffffu, x, q) + trc[q];
-      ix[q] = q;
+  for (int j = 0; j < (kDbReg ? KH + 1 : 1); ++j) {
+    const int k = hf * KH + j;
+    dbr[j] = (kDbReg && cv && j >= 1 && k <= kcap) ? dbl[k * C + c] : kDNegInf;
+  }
+  // the two halves' maxima joined: the lower half (smaller index) wins ties
+  auto join = [&](double& v, int& ix) {
+    if (HALF) {
+      const double ov = __shfl_xor_sync(0xffffffffu, v, 16);
+      const int oi = __shfl_xor_sync(0xffffffffu, ix, 16);
+      if (hf == 0 ? ov > v : ov >= v) {
+        v = ov;
+        ix = oi;
+      }
     }
-    stable_max<NC>(v, ix);
+  };
+
+  // m = max_q (x_q + tr[q,c]) and its first maximiser (x of label q is in lane q)
+  auto label_max = [&](double x, int& arg) -> double {
+    double v[NQ];
+    int ix[NQ];
+#pragma unroll
+    for (int j = 0; j < NQ; ++j) {
+      v[j] = __shfl_sync(0xffffffffu, x, hf * NQ + j) + trc[j];
+      ix[j] = hf * NQ + j;
+    }
+    stable_max<NQ>(v, ix);
+    join(v[0], ix[0]);
     arg = ix[0];
     return v[0];
   };
@@ -146,7 +173,7 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
   double x = 0.0;
   {
     const double m = label_max(cv ? 0.0 : kDNegInf, arg);
-    if (cv) {
+    if (wr) {
       const double ps = (a.ps && T > 0) ? (double)a.ps[(size_t)b * T * C + c] : 0.0;
       ring[c] = ring[(size_t)R * C + c] = (m + ps) - (double)cum_b[c];
       rarg[c] = (uint8_t)arg;
@@ -176,8 +203,9 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
         int ix[KG];
 #pragma unroll
         for (int j = 0; j < KG; ++j) {
-          const int k = g * KG + j + 1;
-          const double db_k = kDbReg ? dbr[k] : (k <= kcap ? dbl[k * C + c] : kDNegInf);
+          const int kl = g * KG + j + 1;  // this lane's duration index
+          const int k = hf * KH + kl;
+          const double db_k = kDbReg ? dbr[kl] : (k <= kcap ? dbl[k * C + c] : kDNegInf);
           v[j] = top[-k * C] + db_k;
           ix[j] = k;
         }
@@ -188,17 +216,18 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
         }
       }
     }
+    join(best, bk);
     if (best != kDNegInf) best += cum_t;
     x = best;
     if (cv && best != kDNegInf && a.pe) x = best + (double)a.pe[((size_t)b * T + t - 1) * C + c];
-    if (cv && bpk_b) bpk_b[(size_t)t * C + c] = (int16_t)bk;
-    if (cv && bp_b) {
+    if (wr && bpk_b) bpk_b[(size_t)t * C + c] = (int16_t)bk;
+    if (wr && bp_b) {
       // duration in the low byte, the source label at the segment start above
       const int src = bk > 0 ? rarg[((t - bk) & Rm) * C + c] : 0;
       bp_b[(size_t)t * C + c] = (uint16_t)(bk | (src << 8));
     }
     const double m = label_max(cv ? x : kDNegInf, arg);
-    if (cv) {
+    if (wr) {
       const double ps = (a.ps && t < T) ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
       const double ne = (m + ps) - cum_t;
       ring[(size_t)(t & Rm) * C + c] = ne;
@@ -208,12 +237,12 @@ __global__ void __launch_bounds__(32 * kVMaxWarps) vchain_kernel(const VChainArg
     }
   }
   // score = max_c x[Lb,c] and the first maximising label
-  double mv = cv ? x : kDNegInf;
-  if (Lb == 0) mv = cv ? 0.0 : kDNegInf;
+  double mv = wr ? x : kDNegInf;
+  if (Lb == 0) mv = wr ? 0.0 : kDNegInf;
   double mx = mv;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  int cand = (cv && mv == mx) ? c : 0x7fffffff;
+  int cand = (wr && mv == mx) ? c : 0x7fffffff;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
   if (lane == 0) {
