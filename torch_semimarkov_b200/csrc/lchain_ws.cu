@@ -462,24 +462,32 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           double acc[LP];
 #pragma unroll
           for (int i = 0; i < LP; ++i) acc[i] = 0.0;
+          // ring block of source block q = fqa + mq, stepped down with wrap
+          // (no division per block)
+          int bq = (tau - fqa) % NR;
+          if (bq < 0) bq += NR;
 #pragma unroll
           for (int mq = 0; mq < BPC; ++mq) {
+            // every load is in bounds and unconditional (blocks past qmax and
+            // sources before s_lo contribute zeros), so that the compiler can
+            // issue a block's loads while the previous block's FMAs run
             const int q = fqa + mq;
-            if (q <= qmax) {
-              const int sb = u0 - q * LP;
-              int bq = (tau - q) % NR;
-              if (bq < 0) bq += NR;
-              const double* rp = ring + (size_t)bq * LP * Cs + fc;
-              const double Wq = wcur[q * Cs + fc];
-              double x[LP];
+            const bool qok = q <= qmax;
+            const int sb = u0 - q * LP;
+            const double* rp = ring + (size_t)bq * LP * Cs + fc;
+            const double Wq = wcur[(q < NWT ? q : NWT - 1) * Cs + fc];
+            double x[LP];
 #pragma unroll
-              for (int r = 0; r < LP; ++r) x[r] = (sb + r >= s_lo) ? rp[(size_t)r * Cs] * Wq : 0.0;
-#pragma unroll
-              for (int r = 0; r < LP; ++r)
-#pragma unroll
-                for (int i = 0; i < LP; ++i)
-                  acc[i] = fma(x[r], dw[mq * LP + (LP - 1) + i - r], acc[i]);
+            for (int r = 0; r < LP; ++r) {
+              const double v = rp[(size_t)r * Cs];
+              x[r] = (qok && sb + r >= s_lo) ? v * Wq : 0.0;
             }
+#pragma unroll
+            for (int r = 0; r < LP; ++r)
+#pragma unroll
+              for (int i = 0; i < LP; ++i)
+                acc[i] = fma(x[r], dw[mq * LP + (LP - 1) + i - r], acc[i]);
+            bq = bq == 0 ? NR - 1 : bq - 1;
           }
 #pragma unroll
           for (int i = 0; i < LP; ++i) part[(fj * LP + i) * Cs + fc] = acc[i];
