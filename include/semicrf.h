@@ -85,12 +85,16 @@ typedef struct semicrf_problem {
                                      when the forward keeps SEMICRF_KEEP_ALPHA
                                      state: 0 = automatic (when the batch
                                      leaves SMs idle), -1 = never, > 0 = force
-                                     it with this many warm-up positions.
-                                     Chunks start early from a guessed state
-                                     and are accepted only where their state
-                                     matches the previous chunk's to 1e-10 in
-                                     projective distance; other sequences are
-                                     recomputed as one chain. */
+                                     it with (bits 0..15) this many warm-up
+                                     positions and (bits 16..30, 0 = none) a
+                                     second, longer warm-up.  Chunks start
+                                     early from a guessed state and are
+                                     accepted only where their state matches
+                                     the previous chunk's to 1e-10 in
+                                     projective distance; other sequences
+                                     rerun their chunks with the second
+                                     warm-up, and those that still do not
+                                     join are recomputed as one chain. */
 } semicrf_problem;
 
 enum semicrf_backward_mode { SEMICRF_KEEP_ALPHA = 0, SEMICRF_RECOMPUTE = 1 };

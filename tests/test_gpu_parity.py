@@ -456,12 +456,14 @@ def test_max_forward_no_grad_vs_oracle(case, oracle):
 
 # time-chunked chains (keep mode, batches that leave SMs idle): chunks start
 # early from a guessed state and are joined after a projective check; a short
-# forced warm-up exercises the serial rerun of sequences that do not join
+# forced warm-up exercises the serial rerun of sequences that do not join, and
+# a short one with a longer second warm-up the rerun of their chunks
 CHUNK_CASES = [
     # B, T, K, C, gen, proj, env
     (1, 5000, 20, 8, "cfg3", None, "auto"),
     (2, 4000, 33, 24, "cfg2", "both", "auto"),
     (1, 3000, 20, 8, "default", None, "8"),
+    (2, 3000, 20, 8, "default", None, "8,64"),
     (1, 12000, 1000, 8, "cfg3", None, "auto"),
 ]
 

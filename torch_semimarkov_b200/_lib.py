@@ -43,13 +43,18 @@ KEEP_ALPHA_FREE_FRACTION = 0.5
 def chunk_warmup_from_env() -> int:
     """Time chunking of the log-semiring chains (semicrf_problem.chunk_warmup):
     TORCH_SEMIMARKOV_B200_CHUNKS=off disables it, =<n> forces it with an
-    n-position warm-up; unset or auto lets the library decide."""
+    n-position warm-up, =<n>,<m> with an n-position warm-up and an m-position
+    second pass for sequences that do not join; unset or auto lets the
+    library decide."""
     env = os.environ.get("TORCH_SEMIMARKOV_B200_CHUNKS", "").lower()
     if env in ("", "auto"):
         return 0
     if env == "off":
         return -1
-    return max(1, int(env))
+    first, _, second = env.partition(",")
+    n = min(max(1, int(first)), 0xFFFF)
+    m = min(max(0, int(second)), 0x7FFF) if second else 0
+    return n | (m << 16)
 
 
 def keep_table_bytes(B: int, T: int, C: int) -> int:

@@ -113,13 +113,14 @@ struct SavedLayout {
   ChunkPlan cp;    // time chunks of the two chains (keep mode)
   double *hand_a, *hand_b, *rdiff, *dofs;
   int *okf, *fail;
+  int* redo;       // [2][B]: the sequences whose chunks rerun with the second warm-up
   int* rec_ovf;    // SEMICRF_RECOMPUTE: set when the forward's float64 frames clipped
 };
 
 ChunkPlan keep_chunk_plan(const semicrf_problem* p) {
   if (p->semiring != SEMICRF_LOG || p->backward_mode != SEMICRF_KEEP_ALPHA ||
       !lchain_ws_supported((int)p->C, (int)p->K))
-    return ChunkPlan{1, (int)p->T, 0};
+    return ChunkPlan{1, (int)p->T, 0, 0};
   return chunk_plan((int)p->batch, (int)p->T, (int)p->K, (int)p->C, 2, p->chunk_warmup);
 }
 
@@ -158,6 +159,7 @@ SavedLayout carve_saved(Carver& cv, const semicrf_problem* p) {
       s.dofs = cv.take<double>(2 * nc);
       s.okf = cv.take<int>(2 * nc);
       s.fail = cv.take<int>(2 * B);
+      s.redo = cv.take<int>(2 * B);
     }
   }
   return s;
@@ -223,8 +225,10 @@ LBwdLayout carve_lbwd(Carver& cv, const semicrf_problem* p) {
 }
 
 // Both chains of every sequence in time chunks (one CTA per chunk and chain),
-// then the boundary check and offset fix-up per chain, then a serial rerun of
-// any sequence whose chunks did not join.
+// then the boundary check and offset fix-up per chain; when the plan has a
+// second warm-up, the chunks of sequences that did not join again with it and
+// their boundaries checked again; then a serial rerun of any sequence whose
+// chunks still did not join.
 cudaError_t chunked_chains(const semicrf_problem* p, LChainLaunch L, const SavedLayout& sl,
                            cudaStream_t s) {
   const int B = (int)p->batch, P = sl.cp.nchunk;
@@ -238,24 +242,46 @@ cudaError_t chunked_chains(const semicrf_problem* p, LChainLaunch L, const Saved
   L.n1 = B * P;
   cudaError_t e = launch_lchain_ws(L, 2 * B * P, s);
   if (e != cudaSuccess) return e;
-  for (int role = 0; role < 2; ++role) {
-    ChunkFix f{};
-    f.B = B;
-    f.T = (int)p->T;
-    f.K = (int)p->K;
-    f.C = (int)p->C;
-    f.dir = role;
-    f.cp = sl.cp;
-    f.lengths = p->lengths;
-    f.hand = role ? sl.hand_b : sl.hand_a;
-    f.rdiff = sl.rdiff + (size_t)role * B * P;
-    f.okf = sl.okf + (size_t)role * B * P;
-    f.D = sl.dofs + (size_t)role * B * P;
-    f.fail = sl.fail + (size_t)role * B;
-    f.n_tab = role ? sl.m_tab : sl.n_tab;
-    f.logz = role ? nullptr : L.a0.logz;
-    f.partition = role ? nullptr : L.a0.partition;
-    e = launch_chunk_fix(f, s);
+  auto fix_all = [&](const int* only) -> cudaError_t {
+    for (int role = 0; role < 2; ++role) {
+      ChunkFix f{};
+      f.B = B;
+      f.T = (int)p->T;
+      f.K = (int)p->K;
+      f.C = (int)p->C;
+      f.dir = role;
+      f.cp = sl.cp;
+      f.lengths = p->lengths;
+      f.hand = role ? sl.hand_b : sl.hand_a;
+      f.rdiff = sl.rdiff + (size_t)role * B * P;
+      f.okf = sl.okf + (size_t)role * B * P;
+      f.D = sl.dofs + (size_t)role * B * P;
+      f.fail = sl.fail + (size_t)role * B;
+      f.only = only ? only + (size_t)role * B : nullptr;
+      f.n_tab = role ? sl.m_tab : sl.n_tab;
+      f.logz = role ? nullptr : L.a0.logz;
+      f.partition = role ? nullptr : L.a0.partition;
+      cudaError_t e = launch_chunk_fix(f, s);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  };
+  e = fix_all(nullptr);
+  if (e != cudaSuccess) return e;
+  if (sl.cp.warm2 > 0) {
+    // sequences whose boundaries did not join: their chunks again with the
+    // longer warm-up, then their boundaries checked again (the others are
+    // final and untouched: the chains skip them, the fix-up ignores them)
+    if (cudaMemcpyAsync(sl.redo, sl.fail, 2 * (size_t)B * sizeof(int),
+                        cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return cudaErrorUnknown;
+    LChainLaunch L2 = L;
+    L2.a0.warm = L2.a1.warm = sl.cp.warm2;
+    L2.a0.only = sl.redo;
+    L2.a1.only = sl.redo + B;
+    e = launch_lchain_ws(L2, 2 * B * P, s);
+    if (e != cudaSuccess) return e;
+    e = fix_all(sl.redo);
     if (e != cudaSuccess) return e;
   }
   // sequences whose chunks did not join: each chain again, whole

@@ -11,8 +11,10 @@
 // so when d <= tol every later value of chunk j differs from the exact one by
 // the same factor, exp(r), to relative error d.  The chunk's offsets
 // D_j = D_{j-1} + r_j are added to its normalisers (n_tab) and to log Z.  A
-// sequence with any boundary above tol is flagged and rerun as one chain, so
-// the result never rests on the guess.
+// sequence with any boundary above tol is flagged; when the plan has a second
+// warm-up its chunks are rerun with it and checked again, and a sequence that
+// still does not join is rerun as one chain, so the result never rests on
+// the guess.
 
 #include "semicrf_internal.cuh"
 
@@ -32,6 +34,7 @@ __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
 // one CTA per (boundary j, sequence): r_j and whether it is acceptable
 __global__ void __launch_bounds__(256) chunk_verify_kernel(const ChunkFix f, int kcap) {
   const int j = blockIdx.x + 1, b = blockIdx.y;
+  if (f.only && !f.only[b]) return;
   const int nch = f.cp.nchunk;
   const int Lb = seq_len(f.lengths, b, f.T);
   __shared__ double s_mx[2][8], s_mn[8], s_mxd[8];
@@ -113,6 +116,7 @@ __global__ void __launch_bounds__(256) chunk_verify_kernel(const ChunkFix f, int
 __global__ void chunk_prefix_kernel(const ChunkFix f) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= f.B) return;
+  if (f.only && !f.only[b]) return;
   const int nch = f.cp.nchunk;
   const int Lb = seq_len(f.lengths, b, f.T);
   double acc = 0.0;
@@ -135,7 +139,7 @@ __global__ void chunk_apply_kernel(const ChunkFix f) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
     const int b = (int)(i / (f.T + 1)), t = (int)(i % (f.T + 1));
-    if (f.fail[b]) continue;
+    if (f.fail[b] || (f.only && !f.only[b])) continue;
     const int Lb = seq_len(f.lengths, b, f.T);
     if (t > Lb) continue;
     const int u = f.dir == 0 ? t : Lb - t;
@@ -155,32 +159,62 @@ __global__ void chunk_apply_kernel(const ChunkFix f) {
 }  // namespace
 
 ChunkPlan chunk_plan(int B, int T, int K, int C, int nroles, int warm_override) {
-  ChunkPlan p{1, T > 0 ? T : 1, 0};
+  ChunkPlan p{1, T > 0 ? T : 1, 0, 0};
   if (B <= 0 || T <= 0 || warm_override < 0) return p;
   const int kcap = K > 1 ? K - 1 : 1;
-  // the warm-up: the longest duration (the hand-off window must lie inside
-  // it) plus a margin, in whole blocks.  From a uniform start the window
-  // already agrees with the previous chunk's up to a constant at that point
-  // on the benchmark inputs (configuration 2: every boundary joins with a
-  // warm-up of K - 1 + 5); the boundary check still decides, and a sequence
-  // whose chunks do not join is rerun whole.
-  int warm = warm_override > 0 ? warm_override : kcap + 32;
-  if (warm < kcap) warm = kcap;  // the hand-off window must lie in the warm-up
-  warm = ((warm + kLP - 1) / kLP) * kLP;
-  // as many chunks as idle SMs allow, each at least twice the warm-up long
+  auto blocks = [](int w) { return ((w + kLP - 1) / kLP) * kLP; };
   const int sms = device_sm_count();
-  int nch = sms / (B * nroles);
-  const int by_len = T / (2 * warm);
-  if (warm_override > 0 && nch < 2) nch = 2;
-  if (nch > by_len) nch = by_len;
+  // chunks for a given warm-up: as many as idle SMs allow, each at least
+  // twice the warm-up long
+  auto count = [&](int w) {
+    int n = sms / (B * nroles);
+    const int by_len = T / (2 * w);
+    if (warm_override > 0 && n < 2) n = 2;
+    return n > by_len ? by_len : n;
+  };
+  // Two warm-ups: the long one, twice the longest duration plus 64, and the
+  // short one, the longest duration (the hand-off window must lie inside the
+  // warm-up) plus 32.  How fast the window forgets the uniform start depends
+  // on the scores; on configuration 2 (K = 300) every boundary joins after
+  // K - 1 + 5 positions, on configuration 3 (K = 1000) not after K - 1 + 32.
+  // When the long warm-up costs at most a quarter of the chunk length it
+  // allows, it is the only one; otherwise the chunks run with the short one
+  // and a sequence whose boundaries do not join reruns its chunks with the
+  // long one.  warm_override > 0 gives the first warm-up in bits 0..15 and an
+  // optional second one in bits 16..30.
+  const int wl = blocks(2 * kcap + 64);
+  int warm, warm2;
+  if (warm_override > 0) {
+    warm = warm_override & 0xffff;
+    warm2 = (warm_override >> 16) & 0x7fff;
+  } else {
+    const int nl = count(wl);
+    const int len_l = nl >= 2 ? blocks((T + nl - 1) / nl) : 0;
+    if (nl >= 2 && 4 * wl <= len_l) {
+      warm = wl;
+      warm2 = 0;
+    } else {
+      warm = kcap + 32;
+      warm2 = wl;
+    }
+  }
+  if (warm < kcap) warm = kcap;  // the hand-off window must lie in the warm-up
+  warm = blocks(warm);
+  int nch = count(warm);
   if (nch < 2) return p;
   int len = (T + nch - 1) / nch;
-  len = ((len + kLP - 1) / kLP) * kLP;
+  len = blocks(len);
   if (len < kcap) return p;
   p.nchunk = (T + len - 1) / len;
-  if (p.nchunk < 2) return ChunkPlan{1, T, 0};
+  if (p.nchunk < 2) return ChunkPlan{1, T, 0, 0};
   p.len = len;
   p.warm = warm;
+  // the second warm-up must start at or after position 0 (u_out >= len)
+  if (warm2 > 0) {
+    warm2 = blocks(warm2 < kcap ? kcap : warm2);
+    if (warm2 > len) warm2 = len;
+    p.warm2 = warm2 > warm ? warm2 : 0;
+  }
   return p;
 }
 

@@ -175,6 +175,7 @@ cudaError_t launch_lchain_cl(const LChainLaunch& L, int nchains, cudaStream_t s)
 // time chunking of the float64 chains (lchunk.cu)
 struct ChunkPlan {
   int nchunk, len, warm;
+  int warm2;  // > 0: sequences whose chunks do not join rerun their chunks with this warm-up
 };
 // chunks for B sequences (times nroles chains each) of length T; nchunk = 1
 // means no chunking.  warm_override > 0 forces chunking with that warm-up.
@@ -192,6 +193,7 @@ struct ChunkFix {
   int* okf;       // [B][nchunk]
   double* D;      // [B][nchunk]
   int* fail;      // [B]
+  const int* only;  // null, or [B]: check and fix only the sequences flagged here
   double* n_tab;  // (B, T+1) or null
   double* logz;   // (B) or null
   float* partition;
