@@ -388,8 +388,23 @@ __global__ void __launch_bounds__(kMT) lmarg_blk_kernel(const LMargArgs a) {
 // An item is a (label, kLG consecutive k) pair: MI items per thread.  A thread
 // forms 16 targets x kLG lags per step from 16 + (16 + kLG - 1) staged values,
 // so each shared-memory load serves more than five FMAs.
+// The sources stay in a ring of NR = 2^m >= ny rows across the target blocks
+// of a split (Ylin as stored, zero past the sequence end): each block adds
+// only its 64 new rows, loaded into registers while the previous block
+// computes, and the block factor G of a source is applied as the window of 31
+// rows is read (a window spans at most two source blocks).
 constexpr int kLG = 16;
+constexpr int kDbPF = 4;  // prefetched X and Y values per thread: kTT * cg <= kDbPF * kMT
 static_assert(kTT % 16 == 0, "lmarg_db_kernel steps over targets in groups of 16");
+static_assert(kTT == 64, "the ring's block arithmetic assumes 64-position blocks");
+
+__host__ __device__ inline int db_ring_rows(int kcap) {
+  const int ny = kTT + kcap + 16;
+  int r = 64;
+  while (r < ny) r <<= 1;
+  return r;
+}
+
 template <int MI>
 __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LMargArgs a) {
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -403,10 +418,11 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
   // k_lo <= 16*(nkg-1) + 1, window m < kLG + 15, so the last row read is
   // kTT - 16 + 16*nkg + 14 <= kTT + kcap + 13 < ny
   const int ny = kTT + kcap + 16;
+  const int NR = db_ring_rows(kcap), RM = NR - 1;
   const int nq = ny / kTT + 2;  // source blocks a tile touches
   double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
-  double* Y = X + (size_t)kTT * CG;               // [ny][CG]
-  double* G = Y + (size_t)ny * CG;                // [nq][CG]
+  double* Y = X + (size_t)kTT * CG;               // [NR][CG] ring, row s at s & RM
+  double* G = Y + (size_t)NR * CG;                // [nq][CG]
   const int nkg = (kcap + kLG - 1) / kLG;
   const int nitems = cgn * nkg;
   const int Lb = seq_len(a.lengths, b, T);
@@ -422,83 +438,99 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
   for (int j = 0; j < MI; ++j)
 #pragma unroll
     for (int q = 0; q < kLG; ++q) acc[j][q] = 0.0;
-
-  for (int tau = tau_lo; tau < tau_hi; ++tau) {
-    const int t0 = tau * kTT;
-    const int n = min(kTT, Lb - t0);
-    __syncthreads();
-    for (int e = tid; e < nq * cgn; e += kMT) {
-      const int q = e / cgn, cc = e % cgn;
-      const int beta = tau + q;
-      double gv = 0.0;
-      if (beta < nblk) {
-        const double rx = mx_b[(size_t)tau * C + cc], ry = my_b[(size_t)beta * C + cc];
-        if (rx > -INFINITY && ry > -INFINITY) {
-          const double ex = ry + rx - lz;
-          // beyond this the factored tile loses terms (or clamps): the sequence
-          // is recomputed term by term by lmarg_db_fix_kernel
-          if (ex > kDbFlag) a.dbflag[b] = 1;
-          gv = exp(fmin(ex, 700.0));
-        }
-      }
-      G[q * CG + cc] = gv;
-    }
-    // staging: four loads in flight per thread before any is used
-    for (int e0 = tid; e0 < kTT * cgn; e0 += 4 * kMT) {
-      double v[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int e = e0 + r * kMT;
-        const int i = e / cgn, cc = e % cgn;
-        v[r] = (e < kTT * cgn && i < n) ? a.la[(rowb + t0 + i) * C + g0 + cc] : 0.0;
-      }
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int e = e0 + r * kMT;
-        if (e < kTT * cgn) X[(e / cgn) * CG + e % cgn] = v[r];
-      }
-    }
-    __syncthreads();
-    for (int e0 = tid; e0 < ny * cgn; e0 += 4 * kMT) {
-      double v[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int e = e0 + r * kMT;
+  if (tau_lo >= tau_hi) {
+    // nothing of this sequence in this split: zero partials
+  } else {
+    // a source row of the ring (0 past the sequence end)
+    auto ysrc = [&](int s, int cc) -> double {
+      return (s <= Lb) ? a.lb[(rowb + s) * C + g0 + cc] : 0.0;
+    };
+    // the first block's sources: rows t0+1 .. t0+ny-64 now (the block's own
+    // 64 new rows, t0+ny-63 .. t0+ny, arrive with the prefetch below)
+    {
+      const int t0 = tau_lo * kTT;
+      for (int e = tid; e < (ny - kTT) * cgn; e += kMT) {
         const int j = e / cgn, cc = e % cgn;
         const int s = t0 + 1 + j;
-        v[r] = (e < ny * cgn && s <= Lb && j < n - 1 + kcap) ? a.lb[(rowb + s) * C + g0 + cc]
-                                                             : 0.0;
-      }
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int e = e0 + r * kMT;
-        if (e < ny * cgn) {
-          const int j = e / cgn, cc = e % cgn;
-          const int s = t0 + 1 + j;
-          Y[j * CG + cc] = v[r] != 0.0 ? v[r] * G[(s / kTT - tau) * CG + cc] : 0.0;
-        }
+        Y[(s & RM) * CG + cc] = ysrc(s, cc);
       }
     }
-    __syncthreads();
+    // per thread: up to four X rows and four new Y rows of the next block
+    constexpr int kPF = kDbPF;
+    double px[kPF], py[kPF];
+    auto prefetch = [&](int tau) {
+      const int t0 = tau * kTT, n = min(kTT, Lb - t0);
 #pragma unroll
-    for (int jt = 0; jt < MI; ++jt) {
-      const int it = tid + jt * kMT;
-      if (it < nitems) {
-        const int cc = it % cgn, kg = it / cgn;
-        const int k_lo = 1 + kLG * kg;
-        // target i pairs with Y[i + k - 1]: for targets i0 .. i0+15 the window
-        // y[m] = Y[i0 + k_lo - 1 + m], m < kLG + 15, covers all kLG lags (X is
-        // zero beyond the last target and kTT is a multiple of 16, so whole
-        // groups of 16 are safe; the last row read, kTT + kcap + 13, is staged)
-        for (int i0 = 0; i0 < n; i0 += 16) {
-          double y[kLG + 15];
+      for (int r = 0; r < kPF; ++r) {
+        const int e = tid + r * kMT;
+        px[r] = py[r] = 0.0;
+        if (e < kTT * cgn) {
+          const int i = e / cgn, cc = e % cgn;
+          if (i < n) px[r] = a.la[(rowb + t0 + i) * C + g0 + cc];
+          py[r] = ysrc(t0 + ny - kTT + 1 + i, cc);
+        }
+      }
+    };
+    prefetch(tau_lo);
+    for (int tau = tau_lo; tau < tau_hi; ++tau) {
+      const int t0 = tau * kTT;
+      const int n = min(kTT, Lb - t0);
+      __syncthreads();  // the previous block's reads of X, Y and G are done
 #pragma unroll
-          for (int m = 0; m < kLG + 15; ++m) y[m] = Y[(i0 + k_lo - 1 + m) * CG + cc];
+      for (int r = 0; r < kPF; ++r) {
+        const int e = tid + r * kMT;
+        if (e < kTT * cgn) {
+          const int i = e / cgn, cc = e % cgn;
+          X[i * CG + cc] = px[r];
+          Y[((t0 + ny - kTT + 1 + i) & RM) * CG + cc] = py[r];
+        }
+      }
+      for (int e = tid; e < nq * cgn; e += kMT) {
+        const int q = e / cgn, cc = e % cgn;
+        const int beta = tau + q;
+        double gv = 0.0;
+        if (beta < nblk) {
+          const double rx = mx_b[(size_t)tau * C + cc], ry = my_b[(size_t)beta * C + cc];
+          if (rx > -INFINITY && ry > -INFINITY) {
+            const double ex = ry + rx - lz;
+            // beyond this the factored tile loses terms (or clamps): the sequence
+            // is recomputed term by term by lmarg_db_fix_kernel
+            if (ex > kDbFlag) a.dbflag[b] = 1;
+            gv = exp(fmin(ex, 700.0));
+          }
+        }
+        G[q * CG + cc] = gv;
+      }
+      __syncthreads();
+      if (tau + 1 < tau_hi) prefetch(tau + 1);  // in flight while this block computes
 #pragma unroll
-          for (int d = 0; d < 16; ++d) {
-            const double xd = X[(i0 + d) * CG + cc];
+      for (int jt = 0; jt < MI; ++jt) {
+        const int it = tid + jt * kMT;
+        if (it < nitems) {
+          const int cc = it % cgn, kg = it / cgn;
+          const int k_lo = 1 + kLG * kg;
+          // target i pairs with Y[i + k - 1]: for targets i0 .. i0+15 the
+          // window y[m] = Y[i0 + k_lo - 1 + m], m < kLG + 15, covers all kLG
+          // lags (X is zero beyond the last target, and lags past kcap are
+          // discarded below)
+          for (int i0 = 0; i0 < n; i0 += 16) {
+            const int j0 = i0 + k_lo - 1;
+            // source block of row j: (1 + j) >> 6; the window's first block
+            // and the offset at which the next one starts
+            const int q0 = (1 + j0) >> 6;
+            const int msplit = 64 * (q0 + 1) - 1 - j0;
+            const double gl = G[q0 * CG + cc], gh = G[(q0 + 1) * CG + cc];
+            const int base = t0 + 1 + j0;
+            double y[kLG + 15];
 #pragma unroll
-            for (int q = 0; q < kLG; ++q) acc[jt][q] = fma(xd, y[d + q], acc[jt][q]);
+            for (int m = 0; m < kLG + 15; ++m)
+              y[m] = Y[((base + m) & RM) * CG + cc] * (m < msplit ? gl : gh);
+#pragma unroll
+            for (int d = 0; d < 16; ++d) {
+              const double xd = X[(i0 + d) * CG + cc];
+#pragma unroll
+              for (int q = 0; q < kLG; ++q) acc[jt][q] = fma(xd, y[d + q], acc[jt][q]);
+            }
           }
         }
       }
@@ -620,13 +652,14 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
   // per SM with one item per thread where possible, else one CTA with two
   const int ny = kTT + kcap + 16;
   const int nq = ny / kTT + 2;
-  const size_t per_label = 8 * (size_t)(kTT + ny + nq);
+  const size_t per_label = 8 * (size_t)(kTT + db_ring_rows(kcap) + nq);
   const int nkg = (kcap + kLG - 1) / kLG;
   auto fit = [&](size_t smem, int items) {
     long cg = (long)(smem / per_label);
     const long ci = (long)items * kMT / nkg;
     if (cg > ci) cg = ci;
     if (cg > C) cg = C;
+    if (cg > kDbPF * kMT / kTT) cg = kDbPF * kMT / kTT;  // one block's rows prefetched
     return (int)cg;
   };
   int cg = fit(110 * 1024, 1);
