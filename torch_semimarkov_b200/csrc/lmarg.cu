@@ -39,45 +39,84 @@ __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
   return l < 0 ? 0 : (l > T ? T : (int)l);
 }
 
-// ---- per-position marginals ------------------------------------------------
-__global__ void __launch_bounds__(kMT) lmarg_pos_kernel(const LMargArgs a) {
+// ---- per-position marginals and block-relative factors -----------------------
+// One CTA per (64-position block, label group of at most kPG labels, sequence).
+// Each element (t, c) of the block gives the marginals -> grad_cum /
+// grad_ps / grad_pe and the log start and end factors
+//     la = log xA + xn + ps - cum   (t < len),   lb = log yA + yn + cum + pe (t >= 1),
+// which stay in shared memory; then per label the block maxima maX / mbY and
+// the linear factors exp(la - maX), exp(lb - mbY) (0 where the log factor is
+// -inf) go to global memory.  One pass over the tables: the log factors are
+// never written out and read back.
+constexpr int kPG = 32;  // labels per CTA
+
+__global__ void __launch_bounds__(kMT) lmarg_posblk_kernel(const LMargArgs a) {
+  __shared__ double sla[kTT][kPG + 1], slb[kTT][kPG + 1];
+  __shared__ double smx[2][kPG];
   const int C = a.C, T = a.T;
-  const size_t per_b = (size_t)(T + 1) * C;
-  const size_t total = (size_t)a.B * per_b;
-  for (size_t i = (size_t)blockIdx.x * kMT + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * kMT) {
-    const int b = (int)(i / per_b);
-    const size_t r = i % per_b;
-    const int t = (int)(r / C), c = (int)(r % C);
-    const int Lb = seq_len(a.lengths, b, T);
-    const double g = (double)a.grad_output[b];
+  const int blk = blockIdx.x, g0 = blockIdx.y * kPG, b = blockIdx.z;
+  const int cgn = min(kPG, C - g0);
+  const int t0 = blk * kTT, nt = min(kTT, T + 1 - t0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Lb = seq_len(a.lengths, b, T);
+  const double g = (double)a.grad_output[b];
+  const double lz = a.logz[b];
+  const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
+  for (int e = tid; e < nt * cgn; e += kMT) {
+    const int ti = e / cgn, cc = e % cgn;
+    const int t = t0 + ti, c = g0 + cc;
+    const size_t i = ((size_t)b * (T + 1) + t) * C + c;
     double pend = 0.0, pst = 0.0;
     double la = -INFINITY, lb = -INFINITY;
     if (Lb >= 1 && t <= Lb) {
       const size_t row = (size_t)b * (T + 1) + t;
       const double xn = a.xn[row], yn = a.yn[row];
-      const double f = exp(xn + yn - a.logz[b]);
-      if (t >= 1) pend = a.xa[i] * a.yA[i] * f;
-      if (t < Lb) pst = a.xA[i] * a.ya[i] * f;
-      const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
+      const double f = exp(xn + yn - lz);
+      const double xA = a.xA[i], yA = a.yA[i];
+      if (t >= 1) pend = a.xa[i] * yA * f;
+      if (t < Lb) pst = xA * a.ya[i] * f;
       const double cu = (double)cum_b[(size_t)t * C + c];
       if (t < Lb) {
         const double ps = a.ps ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
-        const double v = a.xA[i];
-        la = (v > 0.0) ? log(v) + xn + ps - cu : -INFINITY;
+        la = (xA > 0.0) ? log(xA) + xn + ps - cu : -INFINITY;
       }
       if (t >= 1) {
         const double pe = a.pe ? (double)a.pe[((size_t)b * T + t - 1) * C + c] : 0.0;
-        const double v = a.yA[i];
-        lb = (v > 0.0) ? log(v) + yn + cu + pe : -INFINITY;
+        lb = (yA > 0.0) ? log(yA) + yn + cu + pe : -INFINITY;
       }
     }
     a.grad_cum[i] = (float)(g * (pend - pst));
     if (a.grad_ps && t < T) a.grad_ps[((size_t)b * T + t) * C + c] = (float)(g * pst);
     if (a.grad_pe && t >= 1) a.grad_pe[((size_t)b * T + t - 1) * C + c] = (float)(g * pend);
-    a.la[i] = la;
-    a.lb[i] = lb;
+    sla[ti][cc] = la;
+    slb[ti][cc] = lb;
   }
+  __syncthreads();
+  // block maxima: one warp per (label, table), two rows per lane
+  for (int w = warp; w < 2 * cgn; w += kMT / 32) {
+    const int cc = w >> 1;
+    const bool isb = w & 1;
+    double m = -INFINITY;
+    for (int ti = lane; ti < nt; ti += 32) m = fmax(m, isb ? slb[ti][cc] : sla[ti][cc]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) smx[isb][cc] = m;
+  }
+  __syncthreads();
+  const int nblk = (T + 1 + kTT - 1) / kTT;
+  for (int e = tid; e < nt * cgn; e += kMT) {
+    const int ti = e / cgn, cc = e % cgn;
+    const size_t i = ((size_t)b * (T + 1) + t0 + ti) * C + g0 + cc;
+    const double x = sla[ti][cc], y = slb[ti][cc];
+    a.la[i] = (x > -INFINITY) ? exp(x - smx[0][cc]) : 0.0;
+    a.lb[i] = (y > -INFINITY) ? exp(y - smx[1][cc]) : 0.0;
+  }
+  if (tid < cgn) {
+    const size_t j = ((size_t)b * nblk + blk) * C + g0 + tid;
+    a.maX[j] = smx[0][tid];
+    a.mbY[j] = smx[1][tid];
+  }
+  if (blk == 0 && blockIdx.y == 0 && tid == 0) a.dbflag[b] = 0;  // lmarg_db_kernel sets it
 }
 
 // ---- transition partials for C <= 24: the same sums, with every thread busy ----
@@ -343,39 +382,6 @@ bool tr_use_mma(int C) {
     choice = (v && strcmp(v, "fma") == 0) ? 0 : 1;
   }
   return choice == 1;
-}
-
-// ---- block-relative linear factors ----------------------------------------
-// Targets and sources are grouped in blocks of kTT positions.  Per (block,
-// label) with m = max over the block of the log factor, the tables are
-// rewritten in place as exp(l - m) (0 where l = -inf) and m is kept:
-//     la -> Xlin, maX;   lb -> Ylin, mbY.
-__global__ void __launch_bounds__(kMT) lmarg_blk_kernel(const LMargArgs a) {
-  const int C = a.C, T = a.T;
-  const int nblk = (T + 1 + kTT - 1) / kTT;
-  const size_t total = (size_t)a.B * nblk * C;
-  for (size_t i = (size_t)blockIdx.x * kMT + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * kMT) {
-    const int c = (int)(i % C);
-    const int blk = (int)((i / C) % nblk);
-    const int b = (int)(i / ((size_t)C * nblk));
-    const int t0 = blk * kTT, t1 = min(t0 + kTT, T + 1);
-    double* la = a.la + ((size_t)b * (T + 1)) * C + c;
-    double* lb = a.lb + ((size_t)b * (T + 1)) * C + c;
-    double ma = -INFINITY, mb = -INFINITY;
-    for (int t = t0; t < t1; ++t) {
-      ma = fmax(ma, la[(size_t)t * C]);
-      mb = fmax(mb, lb[(size_t)t * C]);
-    }
-    for (int t = t0; t < t1; ++t) {
-      const double x = la[(size_t)t * C], y = lb[(size_t)t * C];
-      la[(size_t)t * C] = (x > -INFINITY) ? exp(x - ma) : 0.0;
-      lb[(size_t)t * C] = (y > -INFINITY) ? exp(y - mb) : 0.0;
-    }
-    a.maX[i] = ma;
-    a.mbY[i] = mb;
-    if (blk == 0 && c == 0) a.dbflag[b] = 0;  // lmarg_db_kernel sets it
-  }
 }
 
 // ---- duration partials: part_db[b][split][k-1][c] = sum_t X[t,c] Y[t+k,c] ----
@@ -689,18 +695,10 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   if (!p.ok || p.nchunk != a.nchunk || p.nsplit != a.nsplit || p.cg != a.cg)
     return cudaErrorInvalidValue;
   const int gmax = device_sm_count() * 16;
-  const size_t n = (size_t)a.B * (a.T + 1) * a.C;
-  int g = (int)((n + kMT - 1) / kMT);
-  if (g > gmax) g = gmax;
-  lmarg_pos_kernel<<<g, kMT, 0, s>>>(a);
+  lmarg_posblk_kernel<<<dim3(p.nblk, (a.C + kPG - 1) / kPG, a.B), kMT, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const size_t nb = (size_t)a.B * p.nblk * a.C;
-  g = (int)((nb + kMT - 1) / kMT);
-  if (g > gmax) g = gmax;
-  lmarg_blk_kernel<<<g, kMT, 0, s>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  int g;
   if (a.C <= 24) {
     lmarg_tr24_kernel<<<dim3(1, a.nchunk, a.B), kMT, 0, s>>>(a);
   } else if (a.C <= 32) {
