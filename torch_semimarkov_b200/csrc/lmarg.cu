@@ -122,13 +122,18 @@ __global__ void __launch_bounds__(kMT) lmarg_posblk_kernel(const LMargArgs a) {
 // ---- transition partials for C <= 24: the same sums, with every thread busy ----
 // 8x8 threads hold 3x3 tiles of the 24x24 pair block (9 FMAs per 6 shared-memory
 // loads); the four 64-thread groups take every fourth staged position, and
-// their partial tiles are added in group order at the end.
+// their partial tiles are added in group order at the end.  Positions are
+// staged TS at a time; the next stage's table rows are loaded into registers
+// while the current one computes, and f_t scales the x values as they are read.
 __global__ void __launch_bounds__(kMT) lmarg_tr24_kernel(const LMargArgs a) {
-  constexpr int PB = 24, TS = 32, NG = kMT / 64;
+  constexpr int PB = 24, TS = 96, NG = kMT / 64, NE = TS * PB / kMT;
+  static_assert(TS * PB % kMT == 0, "whole stage per thread count");
   __shared__ __align__(16) double xs[TS][PB];
   __shared__ __align__(16) double ys[TS][PB];
   __shared__ double fs[TS];
-  __shared__ double red[NG - 1][9][64];
+  // the groups' partial tiles reuse the staging buffer once the loop is done
+  static_assert((NG - 1) * 9 * 64 <= TS * PB, "partials fit in the x stage");
+  double(*red)[9][64] = reinterpret_cast<double(*)[9][64]>(&xs[0][0]);
   const int C = a.C, T = a.T;
   const int ch = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, grp = tid >> 6, l = tid & 63, tx = l & 7, ty = l >> 3;
@@ -143,28 +148,41 @@ __global__ void __launch_bounds__(kMT) lmarg_tr24_kernel(const LMargArgs a) {
     for (int j = 0; j < 3; ++j) acc[i][j] = 0.0;
   const double lz = a.logz[b];
   const size_t rowb = (size_t)b * (T + 1);
-  for (int t0 = t_lo; t0 < t_hi; t0 += TS) {
+  double px[NE], py[NE], pf = 0.0;
+  auto prefetch = [&](int t0) {
     const int n = min(TS, t_hi - t0);
-    __syncthreads();
-    if (tid < TS) fs[tid] = tid < n ? exp(a.xn[rowb + t0 + tid] + a.yn[rowb + t0 + tid] - lz) : 0.0;
-    __syncthreads();
-    for (int e = tid; e < TS * PB; e += kMT) {
+#pragma unroll
+    for (int r = 0; r < NE; ++r) {
+      const int e = tid + r * kMT;
       const int i = e / PB, q = e % PB;
-      double x = 0.0, y = 0.0;
+      px[r] = py[r] = 0.0;
       if (i < n && q < C) {
         const size_t row = (rowb + t0 + i) * C;
-        x = a.xa[row + q] * fs[i];
-        y = a.ya[row + q];
+        px[r] = a.xa[row + q];
+        py[r] = a.ya[row + q];
       }
-      xs[i][q] = x;
-      ys[i][q] = y;
     }
+    pf = (tid < n) ? a.xn[rowb + t0 + tid] + a.yn[rowb + t0 + tid] : 0.0;
+  };
+  if (t_lo < t_hi) prefetch(t_lo);
+  for (int t0 = t_lo; t0 < t_hi; t0 += TS) {
+    const int n = min(TS, t_hi - t0);
+    __syncthreads();  // the previous stage's reads are done
+#pragma unroll
+    for (int r = 0; r < NE; ++r) {
+      const int e = tid + r * kMT;
+      xs[e / PB][e % PB] = px[r];
+      ys[e / PB][e % PB] = py[r];
+    }
+    if (tid < TS) fs[tid] = tid < n ? exp(pf - lz) : 0.0;
     __syncthreads();
+    if (t0 + TS < t_hi) prefetch(t0 + TS);  // in flight during the FMAs below
     for (int i = grp; i < n; i += NG) {
+      const double f = fs[i];
       double xv[3], yv[3];
 #pragma unroll
       for (int q = 0; q < 3; ++q) {
-        xv[q] = xs[i][ty * 3 + q];
+        xv[q] = xs[i][ty * 3 + q] * f;
         yv[q] = ys[i][tx * 3 + q];
       }
 #pragma unroll
@@ -173,6 +191,7 @@ __global__ void __launch_bounds__(kMT) lmarg_tr24_kernel(const LMargArgs a) {
         for (int q = 0; q < 3; ++q) acc[p][q] = fma(xv[p], yv[q], acc[p][q]);
     }
   }
+  __syncthreads();  // every read of the last stage is done before red reuses it
   if (grp > 0)
 #pragma unroll
     for (int p = 0; p < 3; ++p)
