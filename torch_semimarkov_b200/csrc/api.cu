@@ -243,8 +243,10 @@ cudaError_t chunked_chains(const semicrf_problem* p, LChainLaunch L, const Saved
   cudaError_t e = launch_lchain_ws(L, 2 * B * P, s);
   if (e != cudaSuccess) return e;
   auto fix_all = [&](const int* only) -> cudaError_t {
+    ChunkFix fr[2];
     for (int role = 0; role < 2; ++role) {
-      ChunkFix f{};
+      ChunkFix& f = fr[role];
+      f = ChunkFix{};
       f.B = B;
       f.T = (int)p->T;
       f.K = (int)p->K;
@@ -261,10 +263,8 @@ cudaError_t chunked_chains(const semicrf_problem* p, LChainLaunch L, const Saved
       f.n_tab = role ? sl.m_tab : sl.n_tab;
       f.logz = role ? nullptr : L.a0.logz;
       f.partition = role ? nullptr : L.a0.partition;
-      cudaError_t e = launch_chunk_fix(f, s);
-      if (e != cudaSuccess) return e;
     }
-    return cudaSuccess;
+    return launch_chunk_fix(fr[0], fr[1], s);
   };
   e = fix_all(nullptr);
   if (e != cudaSuccess) return e;

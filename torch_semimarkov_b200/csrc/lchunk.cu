@@ -31,14 +31,30 @@ __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
   return l < 0 ? 0 : (l > T ? T : (int)l);
 }
 
-// one CTA per (boundary j, sequence): r_j and whether it is acceptable
-__global__ void __launch_bounds__(256) chunk_verify_kernel(const ChunkFix f, int kcap) {
+// one CTA per (boundary j, sequence, chain): r_j and whether it is acceptable.
+// The two windows are read once into registers (KVP values per thread and
+// window, for windows up to kVT * kVP entries; longer ones are read twice).
+constexpr int kVT = 512, kVP = 16;
+
+__device__ __forceinline__ double block_max(double v, double* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  v = sh[0];
+  for (int w = 1; w < kVT / 32; ++w) v = fmax(v, sh[w]);
+  return v;
+}
+
+__global__ void __launch_bounds__(kVT) chunk_verify_kernel(const ChunkFix f0, const ChunkFix f1,
+                                                           int kcap) {
+  const ChunkFix& f = blockIdx.z ? f1 : f0;
   const int j = blockIdx.x + 1, b = blockIdx.y;
   if (f.only && !f.only[b]) return;
   const int nch = f.cp.nchunk;
   const int Lb = seq_len(f.lengths, b, f.T);
-  __shared__ double s_mx[2][8], s_mn[8], s_mxd[8];
-  __shared__ int s_bad[8];
+  __shared__ double s_a[kVT / 32], s_b[kVT / 32];
   if (j * f.cp.len >= Lb) {
     if (threadIdx.x == 0) {
       f.rdiff[(size_t)b * nch + j] = 0.0;
@@ -46,66 +62,55 @@ __global__ void __launch_bounds__(256) chunk_verify_kernel(const ChunkFix f, int
     }
     return;
   }
-  const size_t n = (size_t)kcap * f.C;
-  const double* e = f.hand + (((size_t)b * nch + (j - 1)) * 2 + 1) * n;  // end of chunk j-1
-  const double* g = f.hand + (((size_t)b * nch + j) * 2 + 0) * n;        // guess of chunk j
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // pass 1: the largest log source of each window
+  const int n = kcap * f.C;
+  const double* e = f.hand + (((size_t)b * nch + (j - 1)) * 2 + 1) * (size_t)n;  // end of chunk j-1
+  const double* g = f.hand + (((size_t)b * nch + j) * 2 + 0) * (size_t)n;        // guess of chunk j
+  const bool cached = n <= kVT * kVP;
+  double ev[kVP], gv[kVP];
   double me = -INFINITY, mg = -INFINITY;
-  for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
-    me = fmax(me, e[i]);
-    mg = fmax(mg, g[i]);
+  if (cached) {
+#pragma unroll
+    for (int r = 0; r < kVP; ++r) {
+      const int i = threadIdx.x + r * kVT;
+      ev[r] = i < n ? e[i] : -INFINITY;
+      gv[r] = i < n ? g[i] : -INFINITY;
+      me = fmax(me, ev[r]);
+      mg = fmax(mg, gv[r]);
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += kVT) {
+      me = fmax(me, e[i]);
+      mg = fmax(mg, g[i]);
+    }
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    me = fmax(me, __shfl_xor_sync(0xffffffffu, me, o));
-    mg = fmax(mg, __shfl_xor_sync(0xffffffffu, mg, o));
-  }
-  if (lane == 0) {
-    s_mx[0][warp] = me;
-    s_mx[1][warp] = mg;
-  }
-  __syncthreads();
-  me = s_mx[0][0];
-  mg = s_mx[1][0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-    me = fmax(me, s_mx[0][w]);
-    mg = fmax(mg, s_mx[1][w]);
-  }
-  // pass 2: spread of the differences over the entries that matter
+  // the largest log source of each window
+  me = block_max(me, s_a);
+  mg = block_max(mg, s_b);
+  // spread of the differences over the entries that matter
   double dmin = INFINITY, dmax = -INFINITY;
   int bad = 0;
-  for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const double x = e[i], y = g[i];
+  auto take = [&](double x, double y) {
     const bool re = x > me - kNegl, rg = y > mg - kNegl;
-    if (!re && !rg) continue;
+    if (!re && !rg) return;
     if (!(x > -INFINITY) || !(y > -INFINITY)) {
       bad = 1;
-      continue;
+      return;
     }
     const double d = x - y;
     dmin = fmin(dmin, d);
     dmax = fmax(dmax, d);
+  };
+  if (cached) {
+#pragma unroll
+    for (int r = 0; r < kVP; ++r)
+      if (threadIdx.x + r * kVT < n) take(ev[r], gv[r]);
+  } else {
+    for (int i = threadIdx.x; i < n; i += kVT) take(e[i], g[i]);
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    dmin = fmin(dmin, __shfl_xor_sync(0xffffffffu, dmin, o));
-    dmax = fmax(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
-    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-  }
-  if (lane == 0) {
-    s_mn[warp] = dmin;
-    s_mxd[warp] = dmax;
-    s_bad[warp] = bad;
-  }
-  __syncthreads();
+  dmax = block_max(dmax, s_a);
+  dmin = -block_max(-dmin, s_b);
+  bad = __syncthreads_or(bad);
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-      dmin = fmin(dmin, s_mn[w]);
-      dmax = fmax(dmax, s_mxd[w]);
-      bad |= s_bad[w];
-    }
-    if (s_mn[0] < dmin) dmin = s_mn[0];
-    if (s_mxd[0] > dmax) dmax = s_mxd[0];
-    bad |= s_bad[0];
     const bool ok = !bad && dmax >= dmin && (dmax - dmin) <= kTol;
     f.rdiff[(size_t)b * nch + j] = ok ? 0.5 * (dmax + dmin) : 0.0;
     f.okf[(size_t)b * nch + j] = ok ? 1 : 0;
@@ -113,9 +118,11 @@ __global__ void __launch_bounds__(256) chunk_verify_kernel(const ChunkFix f, int
 }
 
 // per sequence: prefix sum of the offsets and the failure flag
-__global__ void chunk_prefix_kernel(const ChunkFix f) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= f.B) return;
+__global__ void chunk_prefix_kernel(const ChunkFix f0, const ChunkFix f1) {
+  const int bb = blockIdx.x * blockDim.x + threadIdx.x;
+  if (bb >= 2 * f0.B) return;
+  const ChunkFix& f = bb >= f0.B ? f1 : f0;
+  const int b = bb >= f0.B ? bb - f0.B : bb;
   if (f.only && !f.only[b]) return;
   const int nch = f.cp.nchunk;
   const int Lb = seq_len(f.lengths, b, f.T);
@@ -133,7 +140,8 @@ __global__ void chunk_prefix_kernel(const ChunkFix f) {
 }
 
 // add each chunk's offset to its normalisers (and log Z)
-__global__ void chunk_apply_kernel(const ChunkFix f) {
+__global__ void chunk_apply_kernel(const ChunkFix f0, const ChunkFix f1) {
+  const ChunkFix& f = blockIdx.y ? f1 : f0;
   const int nch = f.cp.nchunk, L = f.cp.len;
   const size_t total = (size_t)f.B * (f.T + 1);
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -223,19 +231,19 @@ size_t chunk_hand_doubles(int B, int K, int C, const ChunkPlan& cp) {
   return cp.nchunk > 1 ? (size_t)B * cp.nchunk * 2 * kcap * C : 0;
 }
 
-cudaError_t launch_chunk_fix(const ChunkFix& f, cudaStream_t s) {
-  if (f.B <= 0 || f.cp.nchunk < 2) return cudaSuccess;
-  const int kcap = f.K > 1 ? f.K - 1 : 1;
-  chunk_verify_kernel<<<dim3(f.cp.nchunk - 1, f.B), 256, 0, s>>>(f, kcap);
+cudaError_t launch_chunk_fix(const ChunkFix& f0, const ChunkFix& f1, cudaStream_t s) {
+  if (f0.B <= 0 || f0.cp.nchunk < 2) return cudaSuccess;
+  const int kcap = f0.K > 1 ? f0.K - 1 : 1;
+  chunk_verify_kernel<<<dim3(f0.cp.nchunk - 1, f0.B, 2), kVT, 0, s>>>(f0, f1, kcap);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  chunk_prefix_kernel<<<(f.B + 127) / 128, 128, 0, s>>>(f);
+  chunk_prefix_kernel<<<(2 * f0.B + 127) / 128, 128, 0, s>>>(f0, f1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const size_t total = (size_t)f.B * (f.T + 1);
+  const size_t total = (size_t)f0.B * (f0.T + 1);
   int g = (int)((total + 255) / 256);
-  if (g > device_sm_count() * 8) g = device_sm_count() * 8;
-  chunk_apply_kernel<<<g, 256, 0, s>>>(f);
+  if (g > device_sm_count() * 4) g = device_sm_count() * 4;
+  chunk_apply_kernel<<<dim3(g, 2), 256, 0, s>>>(f0, f1);
   return cudaGetLastError();
 }
 

@@ -198,7 +198,8 @@ struct ChunkFix {
   double* logz;   // (B) or null
   float* partition;
 };
-cudaError_t launch_chunk_fix(const ChunkFix& f, cudaStream_t s);
+// both chains (f0: alpha, f1: beta) in one launch per step
+cudaError_t launch_chunk_fix(const ChunkFix& f0, const ChunkFix& f1, cudaStream_t s);
 bool lchain_ws_supported(int C, int K);
 bool lchain_supported(int C, int K);
 size_t lchain_saved_doubles(int C, int K);       // restart record per checkpoint
