@@ -536,6 +536,22 @@ def test_recompute_mode_large_scale_vs_oracle(scale, C, oracle, monkeypatch):
     _check_vs_oracle(inp, np.array([T, T - 37]), np.array([1.0, 0.7]), K, "log", oracle)
 
 
+@pytest.mark.parametrize("chains", ["1", "2", "3"])
+def test_cluster_chain_counts_vs_oracle(chains, oracle, monkeypatch):
+    """64 < C <= 256 on clusters of four CTAs with 1, 2 or 3 chains per cluster
+    (the library picks the fewest with which all clusters are resident at once;
+    SEMICRF_CLUSTER_CHAINS forces one), odd batch and ragged lengths so that a
+    cluster's chains end at different positions and the last cluster is partial."""
+    monkeypatch.setenv("SEMICRF_CLUSTER_CHAINS", chains)
+    monkeypatch.setenv("TORCH_SEMIMARKOV_B200_BACKWARD", "keep")
+    from inputs import make_streaming_inputs
+
+    B, T, K, C = 5, 120, 12, 96
+    inp = make_streaming_inputs(B, T, K, C, seed=71)
+    lengths = np.array([T, 97, 64, 120, 33])
+    _check_vs_oracle(inp, lengths, np.linspace(0.5, 1.5, B), K, "log", oracle)
+
+
 @pytest.mark.parametrize("C", [96, 256])
 def test_cluster_chain_large_scale_vs_oracle(C, oracle):
     """64 < C <= 256 runs the cluster chain; with emissions N(0, 60^2) its factors

@@ -33,6 +33,8 @@
 
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+
 #include "semicrf_internal.cuh"
 
 namespace semicrf {
@@ -318,6 +320,21 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
   // every CTA's constants are in place before any remote store reaches it
   cluster.sync();
 
+  // element g of a per-chain register array, by selects over the unrolled index
+  auto pick_i = [&](const int (&v)[G], int g) -> int {
+    int r = v[0];
+#pragma unroll
+    for (int q = 1; q < G; ++q)
+      if (q == g) r = v[q];
+    return r;
+  };
+  auto pick_d = [&](const double (&v)[G], int g) -> double {
+    double r = v[0];
+#pragma unroll
+    for (int q = 1; q < G; ++q)
+      if (q == g) r = v[q];
+    return r;
+  };
   int par = 0;
   int lastpar[G];
   double prev_n[G];
@@ -367,7 +384,7 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
     for (int w = tid; w < G * PB; w += kNT) {
       const int g = w / PB, i = (w % PB) / CL, cc = w % CL;
       if (cc >= Cr || i >= nPq[g]) continue;
-      const double n_cur = g == 0 ? ncq[0] : ncq[G - 1];
+      const double n_cur = pick_d(ncq, g);
       const double rf = ref0[g * CL + cc];
       const double cu = pcu0[w];
       const double lg_ = pto0[w] + rf + dbmax[cc] + csign * cu - n_cur;
@@ -394,7 +411,7 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
       const int s_top = s_hi - j * chunk;
       int n = chunk;
       if (s_top - n + 1 < s_lo) n = s_top - s_lo + 1;
-      const int nPg = g == 0 ? nPq[0] : nPq[G - 1];
+      const int nPg = pick_i(nPq, g);
       if (cc < Cr && n > 0 && nPg > 0) {
         double win[kLP];
 #pragma unroll
@@ -433,8 +450,8 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
     __syncthreads();
 
     // ===== phase B: the block's targets in order =====
-    const int nPme = lt ? (gs == 0 ? nPq[0] : nPq[G - 1]) : 0;
-    const double ncme = lt ? (gs == 0 ? ncq[0] : ncq[G - 1]) : 0.0;
+    const int nPme = lt ? pick_i(nPq, gs) : 0;
+    const double ncme = lt ? pick_d(ncq, gs) : 0.0;
     int nPmax = 0;
 #pragma unroll
     for (int g = 0; g < G; ++g) nPmax = nPmax > nPq[g] ? nPmax : nPq[g];
@@ -520,6 +537,32 @@ __global__ void __cluster_dims__(kNCL, 1, 1) __launch_bounds__(kNT, 1)
   }
 }
 
+// How many clusters of lchain_cl_kernel<G> can be resident at once on the
+// current device (its GPC layout decides: a cluster's CTAs share one GPC), or
+// 0 when the query fails; cached per device.
+template <int G>
+int max_active_clusters(size_t smem) {
+  constexpr int kMaxDev = 64;
+  static int cache[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  if (dev < kMaxDev && cache[dev] > 0) return cache[dev];
+  if (cudaFuncSetAttribute(lchain_cl_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kNCL * 64);
+  cfg.blockDim = dim3(kNT);
+  cfg.dynamicSmemBytes = smem;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (const void*)lchain_cl_kernel<G>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (dev < kMaxDev) cache[dev] = n;
+  return n;
+}
+
 template <int G>
 cudaError_t launch_g(const LChainLaunch& L, int nroles, const CPlan& p, cudaStream_t s) {
   const int ngroups = (L.n1 + G - 1) / G;
@@ -542,12 +585,36 @@ bool lchain_cl_supported(int C, int K) {
 cudaError_t launch_lchain_cl(const LChainLaunch& L, int nchains, cudaStream_t s) {
   if (nchains <= 0 || L.n1 <= 0) return cudaSuccess;
   const int nroles = nchains > L.n1 ? 2 : 1;
-  CPlan p;
-  // two chains per cluster when one per cluster would not fit in one wave
-  // (about 148 / 4 clusters of four one-CTA-per-SM CTAs) and their state fits
-  if (nroles * L.n1 > 36 && cchoose(p, L.C, L.K, 2)) return launch_g<2>(L, nroles, p, s);
-  if (!cchoose(p, L.C, L.K, 1)) return cudaErrorInvalidValue;
-  return launch_g<1>(L, nroles, p, s);
+  // 1, 2 or 3 chains per cluster (those whose state fits in shared memory):
+  // more chains per cluster cost more per position but need fewer clusters,
+  // and a cluster that does not fit in the first wave costs a whole second
+  // one.  How many clusters are resident at once depends on the device (33
+  // of four CTAs on most B200 parts, fewer on some), so it is queried.
+  CPlan p1, p2, p3;
+  const bool f1 = cchoose(p1, L.C, L.K, 1), f2 = cchoose(p2, L.C, L.K, 2),
+             f3 = cchoose(p3, L.C, L.K, 3);
+  if (!f1) return cudaErrorInvalidValue;
+  // SEMICRF_CLUSTER_CHAINS=1|2|3 forces the count (tests and measurements)
+  if (const char* v = getenv("SEMICRF_CLUSTER_CHAINS")) {
+    const int g = atoi(v);
+    if (g == 3 && f3) return launch_g<3>(L, nroles, p3, s);
+    if (g == 2 && f2) return launch_g<2>(L, nroles, p2, s);
+    if (g == 1) return launch_g<1>(L, nroles, p1, s);
+  }
+  auto groups = [&](int g) { return nroles * ((L.n1 + g - 1) / g); };
+  // estimated time: waves x the relative cost of one wave with g chains per
+  // cluster (1, 1.4, 2.2: measured per position at C = 256, K = 64 on a
+  // B200); a failed query assumes the B200's usual 33 resident clusters
+  auto waves = [&](int g, int m) {
+    if (m <= 0) m = 33;
+    return (groups(g) + m - 1) / m;
+  };
+  const double t1 = waves(1, max_active_clusters<1>((size_t)p1.total * 8)) * 1.0;
+  const double t2 = f2 ? waves(2, max_active_clusters<2>((size_t)p2.total * 8)) * 1.4 : 1e30;
+  const double t3 = f3 ? waves(3, max_active_clusters<3>((size_t)p3.total * 8)) * 2.2 : 1e30;
+  if (t1 <= t2 && t1 <= t3) return launch_g<1>(L, nroles, p1, s);
+  if (t2 <= t3) return launch_g<2>(L, nroles, p2, s);
+  return launch_g<3>(L, nroles, p3, s);
 }
 
 }  // namespace semicrf
