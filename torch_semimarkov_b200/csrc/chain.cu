@@ -127,19 +127,29 @@ bool chain_supported(int C, int K, int semiring, bool bp) {
 // prep kernel: per-launch constants (same for every sequence)
 // ---------------------------------------------------------------------------
 // column maxima (over sources) of tr and tr^T, and duration-bias maxima
+// one warp per label c: the lanes stride over the rows, then a warp maximum
 __global__ void prep_max_kernel(const float* __restrict__ tr, const float* __restrict__ db, int K,
                                 int C, int kcap, int semiring, Prepared pr) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+  const int c = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (c >= C) return;  // warp-uniform
   float mf = kNegInf, mb = kNegInf, md = kNegInf;
-  for (int r = 0; r < C; ++r) {
+  for (int r = lane; r < C; r += 32) {
     mf = fmaxf(mf, tr[r * C + c]);  // M_f[r][c] = tr[r][c]
     mb = fmaxf(mb, tr[c * C + r]);  // M_b[r][c] = tr[c][r]
   }
-  for (int k = 1; k <= kcap; ++k) md = fmaxf(md, db[(k < K - 1 ? k : K - 1) * C + c]);
-  pr.colmax_f[c] = semiring == 0 ? mf : 0.f;
-  pr.colmax_b[c] = semiring == 0 ? mb : 0.f;
-  pr.dbmax[c] = md;
+  for (int k = 1 + lane; k <= kcap; k += 32) md = fmaxf(md, db[(k < K - 1 ? k : K - 1) * C + c]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mf = fmaxf(mf, __shfl_xor_sync(0xffffffffu, mf, o));
+    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    md = fmaxf(md, __shfl_xor_sync(0xffffffffu, md, o));
+  }
+  if (lane == 0) {
+    pr.colmax_f[c] = semiring == 0 ? mf : 0.f;
+    pr.colmax_b[c] = semiring == 0 ? mb : 0.f;
+    pr.dbmax[c] = md;
+  }
 }
 
 // the tables, given the maxima
@@ -173,7 +183,7 @@ cudaError_t launch_prep(const float* tr, const float* db, int K, int C, int kcap
                         int semiring, const Prepared& prep, cudaStream_t s) {
   const int kx = kcap + kPrepRowsExtra;
   (void)P;
-  prep_max_kernel<<<(C + 127) / 128, 128, 0, s>>>(tr, db, K, C, kcap, semiring, prep);
+  prep_max_kernel<<<(C + 7) / 8, 256, 0, s>>>(tr, db, K, C, kcap, semiring, prep);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int work = C * C > kx * C ? C * C : kx * C;

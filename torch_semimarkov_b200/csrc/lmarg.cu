@@ -42,62 +42,111 @@ __device__ __forceinline__ int seq_len(const int64_t* lengths, int b, int T) {
 // ---- per-position marginals and block-relative factors -----------------------
 // One CTA per (64-position block, label group of at most kPG labels, sequence).
 // Each element (t, c) of the block gives the marginals -> grad_cum /
-// grad_ps / grad_pe and the log start and end factors
-//     la = log xA + xn + ps - cum   (t < len),   lb = log yA + yn + cum + pe (t >= 1),
-// which stay in shared memory; then per label the block maxima maX / mbY and
-// the linear factors exp(la - maX), exp(lb - mbY) (0 where the log factor is
-// -inf) go to global memory.  One pass over the tables: the log factors are
-// never written out and read back.
+// grad_ps / grad_pe and the start and end factors in the split form
+//     exp(la) = xA exp(sa),  sa = xn + ps - cum   (t < len),
+//     exp(lb) = yA exp(sb),  sb = yn + cum + pe   (t >= 1),
+// which stay in shared memory; then per label a block reference maX / mbY and
+// the linear factors xA exp(sa - maX), yA exp(sb - mbY) go to global memory.
+// The reference only has to bound the block's log factors from above (every
+// linear factor is then at most 1) and lie close to their maximum (so that the
+// largest stays near 1): it is the maximum of (e + 1) ln 2 + s, e the binary
+// exponent of xA or yA, which exceeds log xA + s by less than ln 2.  So no
+// logarithm is taken, and f_t = exp(xn + yn - logZ) once per row: two
+// exponentials per element instead of five transcendentals.  One pass over
+// the tables: the factors are never written out and read back.
 constexpr int kPG = 32;  // labels per CTA
 
+// (e + 1) ln 2 + s >= log v + s for v > 0 with binary exponent e (a subnormal
+// v counts as e = -1023, still a bound); -inf where the factor is absent
+__device__ __forceinline__ double log_bound(double v, double s) {
+  if (!(v > 0.0) || !(s > -INFINITY)) return -INFINITY;
+  const int e = (int)((__double_as_longlong(v) >> 52) & 0x7ff) - 1023;
+  return (double)(e + 1) * 0.69314718055994531 + s;
+}
+
+// v exp(s - mx) (at most 1: mx bounds log v + s); where exp(s - mx) alone
+// would overflow (a tiny v near the block maximum) it is exp(log v + s - mx)
+__device__ __forceinline__ double linear_factor(double v, double s, double mx) {
+  if (!(v > 0.0) || !(s > -INFINITY)) return 0.0;
+  const double d = s - mx;
+  return d < 700.0 ? v * exp(d) : exp(log(v) + d);
+}
+
+__host__ __device__ inline int posblk_ld(int C) { return (C < kPG ? C : kPG) | 1; }
+__host__ __device__ inline int posblk_smem(int C) { return 4 * kTT * posblk_ld(C) * 8; }
+
 __global__ void __launch_bounds__(kMT) lmarg_posblk_kernel(const LMargArgs a) {
-  __shared__ double sla[kTT][kPG + 1], slb[kTT][kPG + 1];
+  extern __shared__ __align__(16) unsigned char pbsm[];
+  __shared__ double srow[3][kTT];  // xn, yn, f_t of each row
   __shared__ double smx[2][kPG];
   const int C = a.C, T = a.T;
   const int blk = blockIdx.x, g0 = blockIdx.y * kPG, b = blockIdx.z;
   const int cgn = min(kPG, C - g0);
+  const int ld = posblk_ld(C);  // odd: the column maxima read without bank conflicts
+  double* sxA = reinterpret_cast<double*>(pbsm);  // [kTT][ld] xA (0: no start factor)
+  double* ssa = sxA + kTT * ld;                  // [kTT][ld] sa
+  double* syA = ssa + kTT * ld;                  // [kTT][ld] yA (0: no end factor)
+  double* ssb = syA + kTT * ld;                  // [kTT][ld] sb
   const int t0 = blk * kTT, nt = min(kTT, T + 1 - t0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int Lb = seq_len(a.lengths, b, T);
   const double g = (double)a.grad_output[b];
   const double lz = a.logz[b];
   const float* cum_b = a.cum + (size_t)b * (T + 1) * C;
+  for (int ti = tid; ti < nt; ti += kMT) {
+    const int t = t0 + ti;
+    double xn = 0.0, yn = 0.0, f = 0.0;
+    if (Lb >= 1 && t <= Lb) {
+      const size_t row = (size_t)b * (T + 1) + t;
+      xn = a.xn[row];
+      yn = a.yn[row];
+      f = exp(xn + yn - lz);
+    }
+    srow[0][ti] = xn;
+    srow[1][ti] = yn;
+    srow[2][ti] = f;
+  }
+  __syncthreads();
   for (int e = tid; e < nt * cgn; e += kMT) {
     const int ti = e / cgn, cc = e % cgn;
     const int t = t0 + ti, c = g0 + cc;
     const size_t i = ((size_t)b * (T + 1) + t) * C + c;
     double pend = 0.0, pst = 0.0;
-    double la = -INFINITY, lb = -INFINITY;
+    double xv = 0.0, yv = 0.0, sa = 0.0, sb = 0.0;
     if (Lb >= 1 && t <= Lb) {
-      const size_t row = (size_t)b * (T + 1) + t;
-      const double xn = a.xn[row], yn = a.yn[row];
-      const double f = exp(xn + yn - lz);
+      const double f = srow[2][ti];
       const double xA = a.xA[i], yA = a.yA[i];
       if (t >= 1) pend = a.xa[i] * yA * f;
       if (t < Lb) pst = xA * a.ya[i] * f;
       const double cu = (double)cum_b[(size_t)t * C + c];
       if (t < Lb) {
         const double ps = a.ps ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
-        la = (xA > 0.0) ? log(xA) + xn + ps - cu : -INFINITY;
+        xv = xA;
+        sa = srow[0][ti] + ps - cu;
       }
       if (t >= 1) {
         const double pe = a.pe ? (double)a.pe[((size_t)b * T + t - 1) * C + c] : 0.0;
-        lb = (yA > 0.0) ? log(yA) + yn + cu + pe : -INFINITY;
+        yv = yA;
+        sb = srow[1][ti] + cu + pe;
       }
     }
     a.grad_cum[i] = (float)(g * (pend - pst));
     if (a.grad_ps && t < T) a.grad_ps[((size_t)b * T + t) * C + c] = (float)(g * pst);
     if (a.grad_pe && t >= 1) a.grad_pe[((size_t)b * T + t - 1) * C + c] = (float)(g * pend);
-    sla[ti][cc] = la;
-    slb[ti][cc] = lb;
+    sxA[ti * ld + cc] = xv;
+    ssa[ti * ld + cc] = sa;
+    syA[ti * ld + cc] = yv;
+    ssb[ti * ld + cc] = sb;
   }
   __syncthreads();
-  // block maxima: one warp per (label, table), two rows per lane
+  // block references: one warp per (label, table), two rows per lane
   for (int w = warp; w < 2 * cgn; w += kMT / 32) {
     const int cc = w >> 1;
     const bool isb = w & 1;
+    const double* v = isb ? syA : sxA;
+    const double* sv = isb ? ssb : ssa;
     double m = -INFINITY;
-    for (int ti = lane; ti < nt; ti += 32) m = fmax(m, isb ? slb[ti][cc] : sla[ti][cc]);
+    for (int ti = lane; ti < nt; ti += 32) m = fmax(m, log_bound(v[ti * ld + cc], sv[ti * ld + cc]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) smx[isb][cc] = m;
@@ -107,9 +156,8 @@ __global__ void __launch_bounds__(kMT) lmarg_posblk_kernel(const LMargArgs a) {
   for (int e = tid; e < nt * cgn; e += kMT) {
     const int ti = e / cgn, cc = e % cgn;
     const size_t i = ((size_t)b * (T + 1) + t0 + ti) * C + g0 + cc;
-    const double x = sla[ti][cc], y = slb[ti][cc];
-    a.la[i] = (x > -INFINITY) ? exp(x - smx[0][cc]) : 0.0;
-    a.lb[i] = (y > -INFINITY) ? exp(y - smx[1][cc]) : 0.0;
+    a.la[i] = linear_factor(sxA[ti * ld + cc], ssa[ti * ld + cc], smx[0][cc]);
+    a.lb[i] = linear_factor(syA[ti * ld + cc], ssb[ti * ld + cc], smx[1][cc]);
   }
   if (tid < cgn) {
     const size_t j = ((size_t)b * nblk + blk) * C + g0 + tid;
@@ -696,10 +744,15 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
   if (cg < 1) cg = 1;
   p.cg = cg;
   p.ncg = (C + cg - 1) / cg;
-  const int target = (p.mi == 1 ? 4 : 2) * sms;
+  // about six waves of resident CTAs, so that the sequences' unequal lengths
+  // even out (measured at configuration 2: 1.13 ms backward with two waves,
+  // 1.06 ms with six), but at least four target blocks per CTA (the ring fill
+  // is a fixed cost per CTA)
+  const int target = (p.mi == 1 ? 12 : 6) * sms;
   int nsp = (target + B * p.ncg - 1) / (B * p.ncg);
   const int maxsp = (T + kTT - 1) / kTT;
-  if (nsp > maxsp) nsp = maxsp;
+  const int capsp = maxsp / 4 > 1 ? maxsp / 4 : 1;
+  if (nsp > capsp) nsp = capsp;
   if (nsp < 1) nsp = 1;
   p.nsplit = nsp;
   p.nblk = (T + 1 + kTT - 1) / kTT;
@@ -714,8 +767,11 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   if (!p.ok || p.nchunk != a.nchunk || p.nsplit != a.nsplit || p.cg != a.cg)
     return cudaErrorInvalidValue;
   const int gmax = device_sm_count() * 16;
-  lmarg_posblk_kernel<<<dim3(p.nblk, (a.C + kPG - 1) / kPG, a.B), kMT, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaFuncSetAttribute(
+      lmarg_posblk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, posblk_smem(a.C));
+  if (e != cudaSuccess) return e;
+  lmarg_posblk_kernel<<<dim3(p.nblk, (a.C + kPG - 1) / kPG, a.B), kMT, posblk_smem(a.C), s>>>(a);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int g;
   if (a.C <= 24) {
