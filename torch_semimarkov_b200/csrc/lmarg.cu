@@ -75,7 +75,7 @@ __device__ __forceinline__ double linear_factor(double v, double s, double mx) {
 __host__ __device__ inline int posblk_ld(int C) { return (C < kPG ? C : kPG) | 1; }
 __host__ __device__ inline int posblk_smem(int C) { return 4 * kTT * posblk_ld(C) * 8; }
 
-__global__ void __launch_bounds__(kMT) lmarg_posblk_kernel(const LMargArgs a) {
+__global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a) {
   extern __shared__ __align__(16) unsigned char pbsm[];
   __shared__ double srow[3][kTT];  // xn, yn, f_t of each row
   __shared__ double smx[2][kPG];
@@ -107,36 +107,61 @@ __global__ void __launch_bounds__(kMT) lmarg_posblk_kernel(const LMargArgs a) {
     srow[2][ti] = f;
   }
   __syncthreads();
-  for (int e = tid; e < nt * cgn; e += kMT) {
-    const int ti = e / cgn, cc = e % cgn;
-    const int t = t0 + ti, c = g0 + cc;
-    const size_t i = ((size_t)b * (T + 1) + t) * C + c;
-    double pend = 0.0, pst = 0.0;
-    double xv = 0.0, yv = 0.0, sa = 0.0, sb = 0.0;
-    if (Lb >= 1 && t <= Lb) {
-      const double f = srow[2][ti];
-      const double xA = a.xA[i], yA = a.yA[i];
-      if (t >= 1) pend = a.xa[i] * yA * f;
-      if (t < Lb) pst = xA * a.ya[i] * f;
-      const double cu = (double)cum_b[(size_t)t * C + c];
-      if (t < Lb) {
-        const double ps = a.ps ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
-        xv = xA;
-        sa = srow[0][ti] + ps - cu;
-      }
-      if (t >= 1) {
-        const double pe = a.pe ? (double)a.pe[((size_t)b * T + t - 1) * C + c] : 0.0;
-        yv = yA;
-        sb = srow[1][ti] + cu + pe;
+  // kPB elements per thread at a time, all their loads issued before the
+  // first store (the stores could alias the tables as far as the compiler knows)
+  constexpr int kPB = 2;
+  const int ne = nt * cgn;
+  for (int e0 = tid; e0 < ne; e0 += kPB * kMT) {
+    double vxA[kPB], vyA[kPB], vxa[kPB], vya[kPB], vsa[kPB], vsb[kPB];  // vsa = ps - cum, vsb = cum + pe
+#pragma unroll
+    for (int j = 0; j < kPB; ++j) {
+      const int e = e0 + j * kMT;
+      const int ti = e / cgn, cc = e % cgn;
+      const int t = t0 + ti, c = g0 + cc;
+      const size_t i = ((size_t)b * (T + 1) + t) * C + c;
+      vxA[j] = vyA[j] = vxa[j] = vya[j] = vsa[j] = vsb[j] = 0.0;
+      if (e < ne && Lb >= 1 && t <= Lb) {
+        vxA[j] = a.xA[i];
+        vyA[j] = a.yA[i];
+        if (t >= 1) vxa[j] = a.xa[i];
+        if (t < Lb) vya[j] = a.ya[i];
+        const double cu = (double)cum_b[(size_t)t * C + c];
+        const double ps = (a.ps && t < Lb) ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
+        const double pe = (a.pe && t >= 1) ? (double)a.pe[((size_t)b * T + t - 1) * C + c] : 0.0;
+        vsa[j] = ps - cu;
+        vsb[j] = cu + pe;
       }
     }
-    a.grad_cum[i] = (float)(g * (pend - pst));
-    if (a.grad_ps && t < T) a.grad_ps[((size_t)b * T + t) * C + c] = (float)(g * pst);
-    if (a.grad_pe && t >= 1) a.grad_pe[((size_t)b * T + t - 1) * C + c] = (float)(g * pend);
-    sxA[ti * ld + cc] = xv;
-    ssa[ti * ld + cc] = sa;
-    syA[ti * ld + cc] = yv;
-    ssb[ti * ld + cc] = sb;
+#pragma unroll
+    for (int j = 0; j < kPB; ++j) {
+      const int e = e0 + j * kMT;
+      if (e >= ne) break;
+      const int ti = e / cgn, cc = e % cgn;
+      const int t = t0 + ti, c = g0 + cc;
+      const size_t i = ((size_t)b * (T + 1) + t) * C + c;
+      double pend = 0.0, pst = 0.0;
+      double xv = 0.0, yv = 0.0, sa = 0.0, sb = 0.0;
+      if (Lb >= 1 && t <= Lb) {
+        const double f = srow[2][ti];
+        if (t >= 1) pend = vxa[j] * vyA[j] * f;
+        if (t < Lb) {
+          pst = vxA[j] * vya[j] * f;
+          xv = vxA[j];
+          sa = srow[0][ti] + vsa[j];
+        }
+        if (t >= 1) {
+          yv = vyA[j];
+          sb = srow[1][ti] + vsb[j];
+        }
+      }
+      a.grad_cum[i] = (float)(g * (pend - pst));
+      if (a.grad_ps && t < T) a.grad_ps[((size_t)b * T + t) * C + c] = (float)(g * pst);
+      if (a.grad_pe && t >= 1) a.grad_pe[((size_t)b * T + t - 1) * C + c] = (float)(g * pend);
+      sxA[ti * ld + cc] = xv;
+      ssa[ti * ld + cc] = sa;
+      syA[ti * ld + cc] = yv;
+      ssb[ti * ld + cc] = sb;
+    }
   }
   __syncthreads();
   // block references: one warp per (label, table), two rows per lane
@@ -465,8 +490,13 @@ bool tr_use_mma(int C) {
 // of a split (Ylin as stored, zero past the sequence end): each block adds
 // only its 64 new rows, loaded into registers while the previous block
 // computes, and the block factor G of a source is applied as the window of 31
-// rows is read (a window spans at most two source blocks).
+// rows is read.  Rows 0..kDbMirror-1 are kept twice, the copy after row NR-1,
+// so that a window is kDbMirror consecutive rows wherever it starts (one
+// address per window, fixed offsets after it).  A window starts on a multiple
+// of 16, so it reaches a second source block only when it starts at 48 mod 64,
+// and then from its 16th row on.
 constexpr int kLG = 16;
+constexpr int kDbMirror = 32;  // >= the window's kLG + 15 rows
 constexpr int kDbPF = 4;  // prefetched X and Y values per thread: kTT * cg <= kDbPF * kMT
 static_assert(kTT % 16 == 0, "lmarg_db_kernel steps over targets in groups of 16");
 static_assert(kTT == 64, "the ring's block arithmetic assumes 64-position blocks");
@@ -494,8 +524,8 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
   const int NR = db_ring_rows(kcap), RM = NR - 1;
   const int nq = ny / kTT + 2;  // source blocks a tile touches
   double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
-  double* Y = X + (size_t)kTT * CG;               // [NR][CG] ring, row s at s & RM
-  double* G = Y + (size_t)NR * CG;                // [nq][CG]
+  double* Y = X + (size_t)kTT * CG;               // [NR + kDbMirror][CG] ring, row s at s & RM
+  double* G = Y + (size_t)(NR + kDbMirror) * CG;  // [nq][CG]
   const int nkg = (kcap + kLG - 1) / kLG;
   const int nitems = cgn * nkg;
   const int Lb = seq_len(a.lengths, b, T);
@@ -524,8 +554,10 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
       const int t0 = tau_lo * kTT;
       for (int e = tid; e < (ny - kTT) * cgn; e += kMT) {
         const int j = e / cgn, cc = e % cgn;
-        const int s = t0 + 1 + j;
-        Y[(s & RM) * CG + cc] = ysrc(s, cc);
+        const int s = t0 + 1 + j, r = s & RM;
+        const double v = ysrc(s, cc);
+        Y[r * CG + cc] = v;
+        if (r < kDbMirror) Y[(r + NR) * CG + cc] = v;
       }
     }
     // per thread: up to four X rows and four new Y rows of the next block
@@ -555,7 +587,9 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
         if (e < kTT * cgn) {
           const int i = e / cgn, cc = e % cgn;
           X[i * CG + cc] = px[r];
-          Y[((t0 + ny - kTT + 1 + i) & RM) * CG + cc] = py[r];
+          const int row = (t0 + ny - kTT + 1 + i) & RM;
+          Y[row * CG + cc] = py[r];
+          if (row < kDbMirror) Y[(row + NR) * CG + cc] = py[r];
         }
       }
       for (int e = tid; e < nq * cgn; e += kMT) {
@@ -587,20 +621,20 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
           // lags (X is zero beyond the last target, and lags past kcap are
           // discarded below)
           for (int i0 = 0; i0 < n; i0 += 16) {
-            const int j0 = i0 + k_lo - 1;
-            // source block of row j: (1 + j) >> 6; the window's first block
-            // and the offset at which the next one starts
+            const int j0 = i0 + k_lo - 1;  // a multiple of 16
+            // source block of row j: (1 + j) >> 6; the window's first block,
+            // and the factor of its rows 15.. (the next block's when j0 = 48 mod 64)
             const int q0 = (1 + j0) >> 6;
-            const int msplit = 64 * (q0 + 1) - 1 - j0;
-            const double gl = G[q0 * CG + cc], gh = G[(q0 + 1) * CG + cc];
-            const int base = t0 + 1 + j0;
+            const double gl = G[q0 * CG + cc];
+            const double gh = (j0 & 63) == 48 ? G[(q0 + 1) * CG + cc] : gl;
+            const double* yw = Y + ((t0 + 1 + j0) & RM) * CG + cc;
             double y[kLG + 15];
 #pragma unroll
-            for (int m = 0; m < kLG + 15; ++m)
-              y[m] = Y[((base + m) & RM) * CG + cc] * (m < msplit ? gl : gh);
+            for (int m = 0; m < kLG + 15; ++m) y[m] = yw[m * CG] * (m < 15 ? gl : gh);
+            const double* xw = X + i0 * CG + cc;
 #pragma unroll
             for (int d = 0; d < 16; ++d) {
-              const double xd = X[(i0 + d) * CG + cc];
+              const double xd = xw[d * CG];
 #pragma unroll
               for (int q = 0; q < kLG; ++q) acc[jt][q] = fma(xd, y[d + q], acc[jt][q]);
             }
@@ -725,7 +759,7 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
   // per SM with one item per thread where possible, else one CTA with two
   const int ny = kTT + kcap + 16;
   const int nq = ny / kTT + 2;
-  const size_t per_label = 8 * (size_t)(kTT + db_ring_rows(kcap) + nq);
+  const size_t per_label = 8 * (size_t)(kTT + db_ring_rows(kcap) + kDbMirror + nq);
   const int nkg = (kcap + kLG - 1) / kLG;
   auto fit = [&](size_t smem, int items) {
     long cg = (long)(smem / per_label);
