@@ -501,10 +501,12 @@ constexpr int kDbPF = 4;  // prefetched X and Y values per thread: kTT * cg <= k
 static_assert(kTT % 16 == 0, "lmarg_db_kernel steps over targets in groups of 16");
 static_assert(kTT == 64, "the ring's block arithmetic assumes 64-position blocks");
 
+// ring rows: a power of two with room for a block's ny rows plus the next
+// block's 64 new ones, which are stored while the block computes
 __host__ __device__ inline int db_ring_rows(int kcap) {
   const int ny = kTT + kcap + 16;
   int r = 64;
-  while (r < ny) r <<= 1;
+  while (r < ny + kTT) r <<= 1;
   return r;
 }
 
@@ -523,9 +525,11 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
   const int ny = kTT + kcap + 16;
   const int NR = db_ring_rows(kcap), RM = NR - 1;
   const int nq = ny / kTT + 2;  // source blocks a tile touches
-  double* X = reinterpret_cast<double*>(smraw);   // [kTT][CG]
-  double* Y = X + (size_t)kTT * CG;               // [NR + kDbMirror][CG] ring, row s at s & RM
-  double* G = Y + (size_t)(NR + kDbMirror) * CG;  // [nq][CG]
+  // X and G are double-buffered (block tau uses buffer (tau - tau_lo) & 1):
+  // the next block is staged while this one computes, one barrier per block
+  double* X = reinterpret_cast<double*>(smraw);   // [2][kTT][CG]
+  double* Y = X + (size_t)2 * kTT * CG;           // [NR + kDbMirror][CG] ring, row s at s & RM
+  double* G = Y + (size_t)(NR + kDbMirror) * CG;  // [2][nq][CG]
   const int nkg = (kcap + kLG - 1) / kLG;
   const int nitems = cgn * nkg;
   const int Lb = seq_len(a.lengths, b, T);
@@ -576,17 +580,17 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
         }
       }
     };
-    prefetch(tau_lo);
-    for (int tau = tau_lo; tau < tau_hi; ++tau) {
+    // block tau's X rows, its 64 new Y rows and its G factors into buffer buf
+    auto stage = [&](int tau, int buf) {
       const int t0 = tau * kTT;
-      const int n = min(kTT, Lb - t0);
-      __syncthreads();  // the previous block's reads of X, Y and G are done
+      double* Xb = X + (size_t)buf * kTT * CG;
+      double* Gb = G + (size_t)buf * nq * CG;
 #pragma unroll
       for (int r = 0; r < kPF; ++r) {
         const int e = tid + r * kMT;
         if (e < kTT * cgn) {
           const int i = e / cgn, cc = e % cgn;
-          X[i * CG + cc] = px[r];
+          Xb[i * CG + cc] = px[r];
           const int row = (t0 + ny - kTT + 1 + i) & RM;
           Y[row * CG + cc] = py[r];
           if (row < kDbMirror) Y[(row + NR) * CG + cc] = py[r];
@@ -606,10 +610,26 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
             gv = exp(fmin(ex, 700.0));
           }
         }
-        G[q * CG + cc] = gv;
+        Gb[q * CG + cc] = gv;
       }
+    };
+    prefetch(tau_lo);
+    stage(tau_lo, 0);
+    if (tau_lo + 1 < tau_hi) prefetch(tau_lo + 1);
+    for (int tau = tau_lo; tau < tau_hi; ++tau) {
+      const int t0 = tau * kTT;
+      const int n = min(kTT, Lb - t0);
+      const int cur = (tau - tau_lo) & 1;
+      // block tau is staged, and every read of block tau - 1 (the other
+      // buffer) is done; block tau + 1's new Y rows lie outside block tau's
+      // ny rows of the ring (NR >= ny + kTT)
       __syncthreads();
-      if (tau + 1 < tau_hi) prefetch(tau + 1);  // in flight while this block computes
+      if (tau + 1 < tau_hi) {
+        stage(tau + 1, cur ^ 1);
+        if (tau + 2 < tau_hi) prefetch(tau + 2);  // in flight while this block computes
+      }
+      const double* Xc = X + (size_t)cur * kTT * CG;
+      const double* Gc = G + (size_t)cur * nq * CG;
 #pragma unroll
       for (int jt = 0; jt < MI; ++jt) {
         const int it = tid + jt * kMT;
@@ -625,13 +645,13 @@ __global__ void __launch_bounds__(kMT, MI == 1 ? 2 : 1) lmarg_db_kernel(const LM
             // source block of row j: (1 + j) >> 6; the window's first block,
             // and the factor of its rows 15.. (the next block's when j0 = 48 mod 64)
             const int q0 = (1 + j0) >> 6;
-            const double gl = G[q0 * CG + cc];
-            const double gh = (j0 & 63) == 48 ? G[(q0 + 1) * CG + cc] : gl;
+            const double gl = Gc[q0 * CG + cc];
+            const double gh = (j0 & 63) == 48 ? Gc[(q0 + 1) * CG + cc] : gl;
             const double* yw = Y + ((t0 + 1 + j0) & RM) * CG + cc;
             double y[kLG + 15];
 #pragma unroll
             for (int m = 0; m < kLG + 15; ++m) y[m] = yw[m * CG] * (m < 15 ? gl : gh);
-            const double* xw = X + i0 * CG + cc;
+            const double* xw = Xc + i0 * CG + cc;
 #pragma unroll
             for (int d = 0; d < 16; ++d) {
               const double xd = xw[d * CG];
@@ -759,7 +779,7 @@ LMargPlan lmarg_plan(int B, int T, int K, int C) {
   // per SM with one item per thread where possible, else one CTA with two
   const int ny = kTT + kcap + 16;
   const int nq = ny / kTT + 2;
-  const size_t per_label = 8 * (size_t)(kTT + db_ring_rows(kcap) + kDbMirror + nq);
+  const size_t per_label = 8 * (size_t)(2 * kTT + db_ring_rows(kcap) + kDbMirror + 2 * nq);
   const int nkg = (kcap + kLG - 1) / kLG;
   auto fit = [&](size_t smem, int items) {
     long cg = (long)(smem / per_label);
