@@ -111,12 +111,27 @@ __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a)
   // first store (the stores could alias the tables as far as the compiler knows)
   constexpr int kPB = 2;
   const int ne = nt * cgn;
+  // element e = (row e / cgn, label e % cgn), stepped by kMT without divisions
+  const int dq = kMT / cgn, dr = kMT % cgn;
+  auto step = [&](int& ti, int& cc) {
+    ti += dq;
+    cc += dr;
+    if (cc >= cgn) {
+      cc -= cgn;
+      ++ti;
+    }
+  };
+  int ti0 = tid / cgn, cc0 = tid % cgn;
   for (int e0 = tid; e0 < ne; e0 += kPB * kMT) {
     double vxA[kPB], vyA[kPB], vxa[kPB], vya[kPB], vsa[kPB], vsb[kPB];  // vsa = ps - cum, vsb = cum + pe
+    int tis[kPB], ccs[kPB];
 #pragma unroll
     for (int j = 0; j < kPB; ++j) {
       const int e = e0 + j * kMT;
-      const int ti = e / cgn, cc = e % cgn;
+      tis[j] = ti0;
+      ccs[j] = cc0;
+      step(ti0, cc0);
+      const int ti = tis[j], cc = ccs[j];
       const int t = t0 + ti, c = g0 + cc;
       const size_t i = ((size_t)b * (T + 1) + t) * C + c;
       vxA[j] = vyA[j] = vxa[j] = vya[j] = vsa[j] = vsb[j] = 0.0;
@@ -136,7 +151,7 @@ __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a)
     for (int j = 0; j < kPB; ++j) {
       const int e = e0 + j * kMT;
       if (e >= ne) break;
-      const int ti = e / cgn, cc = e % cgn;
+      const int ti = tis[j], cc = ccs[j];
       const int t = t0 + ti, c = g0 + cc;
       const size_t i = ((size_t)b * (T + 1) + t) * C + c;
       double pend = 0.0, pst = 0.0;
@@ -178,8 +193,10 @@ __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a)
   }
   __syncthreads();
   const int nblk = (T + 1 + kTT - 1) / kTT;
-  for (int e = tid; e < nt * cgn; e += kMT) {
-    const int ti = e / cgn, cc = e % cgn;
+  ti0 = tid / cgn;
+  cc0 = tid % cgn;
+  for (int e = tid; e < ne; e += kMT, step(ti0, cc0)) {
+    const int ti = ti0, cc = cc0;
     const size_t i = ((size_t)b * (T + 1) + t0 + ti) * C + g0 + cc;
     a.la[i] = linear_factor(sxA[ti * ld + cc], ssa[ti * ld + cc], smx[0][cc]);
     a.lb[i] = linear_factor(syA[ti * ld + cc], ssb[ti * ld + cc], smx[1][cc]);
