@@ -225,10 +225,10 @@ struct LMargArgs {
   float* grad_cum;
   float* grad_ps;
   float* grad_pe;
-  double* la;       // (B, T+1, C) scratch: log start factor, then block-relative linear
-  double* lb;       // (B, T+1, C) scratch: log end factor, then block-relative linear
-  double* maX;      // (B, nblk, C) block maxima of la
-  double* mbY;      // (B, nblk, C) block maxima of lb
+  double* la;       // (B, T+1, C) block-relative linear start factors exp(log la - maX)
+  double* lb;       // (B, T+1, C) block-relative linear end factors exp(log lb - mbY)
+  double* maX;      // (B, nblk, C) block references of log la: within ln 2 above the maximum
+  double* mbY;      // (B, nblk, C) block references of log lb: within ln 2 above the maximum
   double* part_tr;  // (B, nchunk, C*C)
   int nchunk;
   double* part_db;  // (B, nsplit, kcap, C)
