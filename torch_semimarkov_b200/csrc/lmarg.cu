@@ -75,6 +75,9 @@ __device__ __forceinline__ double linear_factor(double v, double s, double mx) {
 __host__ __device__ inline int posblk_ld(int C) { return (C < kPG ? C : kPG) | 1; }
 __host__ __device__ inline int posblk_smem(int C) { return 4 * kTT * posblk_ld(C) * 8; }
 
+// W consecutive labels per item (W = 2: 16-byte table loads and stores, half
+// the index work; the host picks it when C is even and every pointer is aligned)
+template <int W>
 __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a) {
   extern __shared__ __align__(16) unsigned char pbsm[];
   __shared__ double srow[3][kTT];  // xn, yn, f_t of each row
@@ -107,75 +110,131 @@ __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a)
     srow[2][ti] = f;
   }
   __syncthreads();
-  // kPB elements per thread at a time, all their loads issued before the
-  // first store (the stores could alias the tables as far as the compiler knows)
-  constexpr int kPB = 2;
-  const int ne = nt * cgn;
-  // element e = (row e / cgn, label e % cgn), stepped by kMT without divisions
-  const int dq = kMT / cgn, dr = kMT % cgn;
-  auto step = [&](int& ti, int& cc) {
+  // W-wide loads and stores of the tables (aligned: checked by the host)
+  auto ldd = [](const double* p, double (&v)[W]) {
+    if constexpr (W == 2) {
+      const double2 q = *reinterpret_cast<const double2*>(p);
+      v[0] = q.x;
+      v[1] = q.y;
+    } else {
+      v[0] = *p;
+    }
+  };
+  auto ldf = [](const float* p, double (&v)[W]) {
+    if constexpr (W == 2) {
+      const float2 q = *reinterpret_cast<const float2*>(p);
+      v[0] = (double)q.x;
+      v[1] = (double)q.y;
+    } else {
+      v[0] = (double)*p;
+    }
+  };
+  auto stf = [](float* p, const float (&v)[W]) {
+    if constexpr (W == 2) {
+      *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+    } else {
+      *p = v[0];
+    }
+  };
+  auto std_ = [](double* p, const double (&v)[W]) {
+    if constexpr (W == 2) {
+      *reinterpret_cast<double2*>(p) = make_double2(v[0], v[1]);
+    } else {
+      *p = v[0];
+    }
+  };
+  // kPB items (2 labels) per thread at a time, all their loads issued before
+  // the first store (the stores could alias the tables as far as the compiler knows)
+  constexpr int kPB = 2 / W;
+  const int nw = cgn / W;  // items per row
+  const int ne = nt * nw;
+  // item e = (row e / nw, labels W * (e % nw) ..), stepped by kMT without divisions
+  const int dq = kMT / nw, dr = kMT % nw;
+  auto step = [&](int& ti, int& ci) {
     ti += dq;
-    cc += dr;
-    if (cc >= cgn) {
-      cc -= cgn;
+    ci += dr;
+    if (ci >= nw) {
+      ci -= nw;
       ++ti;
     }
   };
-  int ti0 = tid / cgn, cc0 = tid % cgn;
+  int ti0 = tid / nw, ci0 = tid % nw;
   for (int e0 = tid; e0 < ne; e0 += kPB * kMT) {
-    double vxA[kPB], vyA[kPB], vxa[kPB], vya[kPB], vsa[kPB], vsb[kPB];  // vsa = ps - cum, vsb = cum + pe
-    int tis[kPB], ccs[kPB];
+    // vsa = ps - cum, vsb = cum + pe
+    double vxA[kPB][W], vyA[kPB][W], vxa[kPB][W], vya[kPB][W], vsa[kPB][W], vsb[kPB][W];
+    int tis[kPB], cis[kPB];
 #pragma unroll
     for (int j = 0; j < kPB; ++j) {
       const int e = e0 + j * kMT;
       tis[j] = ti0;
-      ccs[j] = cc0;
-      step(ti0, cc0);
-      const int ti = tis[j], cc = ccs[j];
-      const int t = t0 + ti, c = g0 + cc;
+      cis[j] = ci0;
+      step(ti0, ci0);
+      const int t = t0 + tis[j], c = g0 + W * cis[j];
       const size_t i = ((size_t)b * (T + 1) + t) * C + c;
-      vxA[j] = vyA[j] = vxa[j] = vya[j] = vsa[j] = vsb[j] = 0.0;
+#pragma unroll
+      for (int w = 0; w < W; ++w) vxA[j][w] = vyA[j][w] = vxa[j][w] = vya[j][w] = vsa[j][w] = vsb[j][w] = 0.0;
       if (e < ne && Lb >= 1 && t <= Lb) {
-        vxA[j] = a.xA[i];
-        vyA[j] = a.yA[i];
-        if (t >= 1) vxa[j] = a.xa[i];
-        if (t < Lb) vya[j] = a.ya[i];
-        const double cu = (double)cum_b[(size_t)t * C + c];
-        const double ps = (a.ps && t < Lb) ? (double)a.ps[((size_t)b * T + t) * C + c] : 0.0;
-        const double pe = (a.pe && t >= 1) ? (double)a.pe[((size_t)b * T + t - 1) * C + c] : 0.0;
-        vsa[j] = ps - cu;
-        vsb[j] = cu + pe;
+        ldd(a.xA + i, vxA[j]);
+        ldd(a.yA + i, vyA[j]);
+        if (t >= 1) ldd(a.xa + i, vxa[j]);
+        if (t < Lb) ldd(a.ya + i, vya[j]);
+        double cu[W], ps[W], pe[W];
+        ldf(cum_b + (size_t)t * C + c, cu);
+#pragma unroll
+        for (int w = 0; w < W; ++w) ps[w] = pe[w] = 0.0;
+        if (a.ps && t < Lb) ldf(a.ps + ((size_t)b * T + t) * C + c, ps);
+        if (a.pe && t >= 1) ldf(a.pe + ((size_t)b * T + t - 1) * C + c, pe);
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          vsa[j][w] = ps[w] - cu[w];
+          vsb[j][w] = cu[w] + pe[w];
+        }
       }
     }
 #pragma unroll
     for (int j = 0; j < kPB; ++j) {
       const int e = e0 + j * kMT;
       if (e >= ne) break;
-      const int ti = tis[j], cc = ccs[j];
+      const int ti = tis[j], cc = W * cis[j];
       const int t = t0 + ti, c = g0 + cc;
       const size_t i = ((size_t)b * (T + 1) + t) * C + c;
-      double pend = 0.0, pst = 0.0;
-      double xv = 0.0, yv = 0.0, sa = 0.0, sb = 0.0;
-      if (Lb >= 1 && t <= Lb) {
-        const double f = srow[2][ti];
-        if (t >= 1) pend = vxa[j] * vyA[j] * f;
-        if (t < Lb) {
-          pst = vxA[j] * vya[j] * f;
-          xv = vxA[j];
-          sa = srow[0][ti] + vsa[j];
+      double pend[W], pst[W];
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        pend[w] = pst[w] = 0.0;
+        double xv = 0.0, yv = 0.0, sa = 0.0, sb = 0.0;
+        if (Lb >= 1 && t <= Lb) {
+          const double f = srow[2][ti];
+          if (t >= 1) pend[w] = vxa[j][w] * vyA[j][w] * f;
+          if (t < Lb) {
+            pst[w] = vxA[j][w] * vya[j][w] * f;
+            xv = vxA[j][w];
+            sa = srow[0][ti] + vsa[j][w];
+          }
+          if (t >= 1) {
+            yv = vyA[j][w];
+            sb = srow[1][ti] + vsb[j][w];
+          }
         }
-        if (t >= 1) {
-          yv = vyA[j];
-          sb = srow[1][ti] + vsb[j];
-        }
+        sxA[ti * ld + cc + w] = xv;
+        ssa[ti * ld + cc + w] = sa;
+        syA[ti * ld + cc + w] = yv;
+        ssb[ti * ld + cc + w] = sb;
       }
-      a.grad_cum[i] = (float)(g * (pend - pst));
-      if (a.grad_ps && t < T) a.grad_ps[((size_t)b * T + t) * C + c] = (float)(g * pst);
-      if (a.grad_pe && t >= 1) a.grad_pe[((size_t)b * T + t - 1) * C + c] = (float)(g * pend);
-      sxA[ti * ld + cc] = xv;
-      ssa[ti * ld + cc] = sa;
-      syA[ti * ld + cc] = yv;
-      ssb[ti * ld + cc] = sb;
+      float gv[W];
+#pragma unroll
+      for (int w = 0; w < W; ++w) gv[w] = (float)(g * (pend[w] - pst[w]));
+      stf(a.grad_cum + i, gv);
+      if (a.grad_ps && t < T) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) gv[w] = (float)(g * pst[w]);
+        stf(a.grad_ps + ((size_t)b * T + t) * C + c, gv);
+      }
+      if (a.grad_pe && t >= 1) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) gv[w] = (float)(g * pend[w]);
+        stf(a.grad_pe + ((size_t)b * T + t - 1) * C + c, gv);
+      }
     }
   }
   __syncthreads();
@@ -193,13 +252,19 @@ __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a)
   }
   __syncthreads();
   const int nblk = (T + 1 + kTT - 1) / kTT;
-  ti0 = tid / cgn;
-  cc0 = tid % cgn;
-  for (int e = tid; e < ne; e += kMT, step(ti0, cc0)) {
-    const int ti = ti0, cc = cc0;
+  ti0 = tid / nw;
+  ci0 = tid % nw;
+  for (int e = tid; e < ne; e += kMT, step(ti0, ci0)) {
+    const int ti = ti0, cc = W * ci0;
     const size_t i = ((size_t)b * (T + 1) + t0 + ti) * C + g0 + cc;
-    a.la[i] = linear_factor(sxA[ti * ld + cc], ssa[ti * ld + cc], smx[0][cc]);
-    a.lb[i] = linear_factor(syA[ti * ld + cc], ssb[ti * ld + cc], smx[1][cc]);
+    double xl[W], yl[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      xl[w] = linear_factor(sxA[ti * ld + cc + w], ssa[ti * ld + cc + w], smx[0][cc + w]);
+      yl[w] = linear_factor(syA[ti * ld + cc + w], ssb[ti * ld + cc + w], smx[1][cc + w]);
+    }
+    std_(a.la + i, xl);
+    std_(a.lb + i, yl);
   }
   if (tid < cgn) {
     const size_t j = ((size_t)b * nblk + blk) * C + g0 + tid;
@@ -207,6 +272,15 @@ __global__ void __launch_bounds__(kMT, 4) lmarg_posblk_kernel(const LMargArgs a)
     a.mbY[j] = smx[1][tid];
   }
   if (blk == 0 && blockIdx.y == 0 && tid == 0) a.dbflag[b] = 0;  // lmarg_db_kernel sets it
+}
+
+// the paired kernel needs an even C and 16-byte (tables) / 8-byte (scores,
+// gradients) aligned bases
+bool posblk_pairs(const LMargArgs& a) {
+  auto al = [](const void* p, uintptr_t n) { return p == nullptr || (uintptr_t)p % n == 0; };
+  return a.C % 2 == 0 && al(a.xA, 16) && al(a.yA, 16) && al(a.xa, 16) && al(a.ya, 16) &&
+         al(a.la, 16) && al(a.lb, 16) && al(a.cum, 8) && al(a.ps, 8) && al(a.pe, 8) &&
+         al(a.grad_cum, 8) && al(a.grad_ps, 8) && al(a.grad_pe, 8);
 }
 
 // ---- transition partials for C <= 24: the same sums, with every thread busy ----
@@ -838,10 +912,19 @@ cudaError_t launch_lmarg(const LMargArgs& a, float* grad_tr, float* grad_db, cud
   if (!p.ok || p.nchunk != a.nchunk || p.nsplit != a.nsplit || p.cg != a.cg)
     return cudaErrorInvalidValue;
   const int gmax = device_sm_count() * 16;
-  cudaError_t e = cudaFuncSetAttribute(
-      lmarg_posblk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, posblk_smem(a.C));
-  if (e != cudaSuccess) return e;
-  lmarg_posblk_kernel<<<dim3(p.nblk, (a.C + kPG - 1) / kPG, a.B), kMT, posblk_smem(a.C), s>>>(a);
+  const dim3 gpb(p.nblk, (a.C + kPG - 1) / kPG, a.B);
+  cudaError_t e;
+  if (posblk_pairs(a)) {
+    e = cudaFuncSetAttribute(lmarg_posblk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             posblk_smem(a.C));
+    if (e != cudaSuccess) return e;
+    lmarg_posblk_kernel<2><<<gpb, kMT, posblk_smem(a.C), s>>>(a);
+  } else {
+    e = cudaFuncSetAttribute(lmarg_posblk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             posblk_smem(a.C));
+    if (e != cudaSuccess) return e;
+    lmarg_posblk_kernel<1><<<gpb, kMT, posblk_smem(a.C), s>>>(a);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int g;
