@@ -82,3 +82,18 @@ def test_chunk_warmup_unset(monkeypatch):
 def test_checkpoint_interval(T, K, S):
     # max(K, floor(sqrt(T K))), the reference's _compute_checkpoint_interval
     assert _lib.checkpoint_interval(T, K) == S
+
+
+def test_launcher_input_key_tracks_storage_and_writes():
+    # launch_streaming_triton_backward reuses a forward's state only while the
+    # inputs are the same storage, unwritten since (autograd.py's _input_key)
+    from torch_semimarkov_b200.streaming.autograd import _input_key
+
+    a = torch.zeros(2, 5, 3)
+    b = torch.zeros(3, 3)
+    k0 = _input_key(a, b, None)
+    assert _input_key(a, b, None) == k0
+    assert _input_key(a.clone(), b, None) != k0  # other storage
+    a.add_(1.0)  # an in-place write bumps the version
+    assert _input_key(a, b, None) != k0
+    assert _input_key(a, b, b) != _input_key(a, b, None)
